@@ -1,0 +1,518 @@
+#!/usr/bin/env python3
+"""Benchmark of the GLM-5.2 DSA indexer + top-k + absorbed-MLA attention substep.
+
+Contract: ``python bench.py --gpus N --steps K --warmup W`` (N > 1 under
+torchrun, one rank per GPU) prints ONE JSON line on rank 0.
+
+Workload (``config.workload``): BASELINE config 4 — one decode token for each
+of 8 independent sequences, each with a 131072-key bf16 latent cache
+[T, 576] and fp8-e4m3 index keys [T, 128] + per-key scale, top-2048, as an
+indexer-owning layer. At N GPUs every cache is split into N contiguous key
+shards (strong scaling: the same total work). A step = one layer-step of the
+substep over all 8 sequences; the metric is microseconds per layer-step.
+The caches (1.35 GB) exceed L2 (126 MB) at every N <= 8, so every step reads
+HBM. Inputs are synthetic (seeded, BASELINE's distributions), generated on the
+device. ``--impl reference`` times the reference's algorithm on the host cores
+(the numpy port in oracle/, since the reference's own path is numpy).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG4 = dict(batch=8, T=131072, k=2048)
+METRIC = "MLA+DSA attention substep latency, decode, 8 seq x 128K ctx, top-2048 (us/layer)"
+
+
+# ---------------------------------------------------------------------------------------------
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 1/2/3 side measurements")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+# ---- clocks sampler ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows: list[list[str]] = []
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.p = None
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=2)
+        except Exception:
+            self.p.kill()
+        self.t.join(timeout=1)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- device inputs ------------------------------------------------------------------------------
+def make_device_inputs(torch, batch, T_local, t0, seed_base, device, n_q=1):
+    """Seeded synthetic inputs on the device: c_kv ~ N(0,1) RMS-normalised rows,
+    k_rot ~ N(0,1) roped at absolute positions (theta 1e6), bf16; index keys
+    ~ N(0,1) quantised to e4m3 with per-key scale = amax/448; q ~ N(0,1) bf16,
+    w ~ U(0,1). Sequence s uses seed seed_base + 1000*s (its shard: + t0)."""
+    from windlass_b200 import attn as A
+    kv = torch.empty(batch, T_local, 576, dtype=torch.bfloat16, device=device)
+    keys = torch.empty(batch, T_local, 128, dtype=torch.uint8, device=device)
+    scale = torch.empty(batch, T_local, dtype=torch.float32, device=device)
+    qshape = (batch,) if n_q == 1 else (n_q,)
+    g = torch.Generator(device=device)
+    inv = 1.0 / (1e6 ** (torch.arange(0, 64, 2, dtype=torch.float64, device=device) / 64))
+    for s in range(batch):
+        g.manual_seed(seed_base + 1000 * s + 7919 * t0)
+        x = torch.randn(T_local, 512, generator=g, device=device)
+        kv[s, :, :512] = (x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+        r = torch.randn(T_local, 64, generator=g, device=device)
+        ang = (torch.arange(t0, t0 + T_local, device=device, dtype=torch.float64)[:, None] * inv[None]).float()
+        a, b = r[:, 0::2], r[:, 1::2]
+        kv[s, :, 512:] = torch.cat([a * ang.cos() - b * ang.sin(), b * ang.cos() + a * ang.sin()], -1).to(torch.bfloat16)
+        k = torch.randn(T_local, 128, generator=g, device=device)
+        sc = (k.abs().amax(-1) / 448.0).clamp_min(1e-30)
+        keys[s] = (k / sc[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+        scale[s] = sc
+    g.manual_seed(seed_base + 17)
+    q_abs = torch.randn(*qshape, 64, 576, generator=g, device=device).to(torch.bfloat16)
+    q_idx = torch.randn(*qshape, 32, 128, generator=g, device=device).to(torch.bfloat16)
+    w_idx = torch.rand(*qshape, 32, generator=g, device=device)
+    return dict(kv=A.LatentKV.packed(kv), kv_raw=kv, keys=A.IndexKeys(keys, scale), q_abs=q_abs, q_idx=q_idx,
+                w_idx=w_idx)
+
+
+def elapsed_ms(torch, fn, steps, stream):
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(steps):
+        fn(i)
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e)
+
+
+# ---- the reference arm (host cores) --------------------------------------------------------------
+def cpu_sample_inputs(T, seed):
+    from oracle import attn_ref as o
+    return o.make_inputs(T, 4, seq=seed)
+
+
+def cpu_step(inp, k):
+    """One sequence of the workload through the reference's algorithm (numpy,
+    fp32 like tools/ref_glm_chain.py)."""
+    from oracle import attn_ref as o
+    return o.decode_step(inp, k, dtype=np.float32)
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def time_cpu(budget_s: float, max_steps: int | None = None):
+    """Time whole sequences of the workload on the host until the budget is spent."""
+    inp = cpu_sample_inputs(CFG4["T"], 0)
+    cpu_step(inp, CFG4["k"])  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_step(inp, CFG4["k"])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or (max_steps and n >= max_steps):
+            break
+    per_seq_us = el / n * 1e6
+    return per_seq_us * CFG4["batch"], n
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    # every step: one whole sequence (a bounded sample of the 8-sequence step), x8
+    inp = cpu_sample_inputs(CFG4["T"], 0)
+    for _ in range(max(args.warmup, 1)):
+        cpu_step(inp, CFG4["k"])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_step(inp, CFG4["k"])
+        times.append(time.perf_counter() - t0)
+    us = statistics.mean(times) * 1e6 * CFG4["batch"]
+    cores = cpu_threads()
+    sample = (f"1 of the 8 sequences (T=131072, top-2048) per step through oracle/attn_ref.py "
+              f"(numpy fp32), scaled x8; {args.steps} steps")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": "cfg4: decode, 8 seq x T=131072, top-2048, owner layer",
+                   "batch": 8, "T": 131072, "index_topk": 2048},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---- our arm ------------------------------------------------------------------------------------
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from windlass_b200 import _lib
+    from windlass_b200 import attn as A
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    B, T, K = CFG4["batch"], CFG4["T"], CFG4["k"]
+    T_local = T // world
+    t0 = rank * T_local
+    cfg = A.glm52_cfg(T)
+    data = make_device_inputs(torch, B, T_local, t0, 20260805, device)
+    stream = torch.cuda.current_stream()
+    L = _lib.lib()
+
+    # ---- the step: one owner layer-step over 8 sequences ----
+    ctx = torch.empty(B, 64, 512, dtype=torch.float32, device=device)
+    lse = torch.empty(B, 64, dtype=torch.float32, device=device)
+    sel = torch.empty(B, K, dtype=torch.int32, device=device)
+    sel_n = torch.empty(B, dtype=torch.int32, device=device)
+    io, keep = A.decode_io(cfg, data["kv"], data["q_abs"], keys=data["keys"], q_idx=data["q_idx"],
+                           w_idx=data["w_idx"], sel_out=sel, sel_n_out=sel_n, ctx=ctx, lse=lse)
+    comm = None
+    if world > 1:
+        comm = A.Comm(rank, world)
+        shard = _lib.Shard(t0, T)
+        nbytes = L.wl_attn_sharded_workspace_bytes(C.byref(cfg), T_local, B, world)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+        def step(i=0):
+            _lib.check(L.wl_attn_decode_sharded(C.byref(cfg), C.byref(io), C.byref(shard), comm.h, ws.data_ptr(),
+                                                nbytes, stream.cuda_stream))
+        launches_per_step = 9
+    else:
+        nbytes = L.wl_attn_workspace_bytes(C.byref(cfg), T, B)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+        def step(i=0):
+            _lib.check(L.wl_attn_decode(C.byref(cfg), C.byref(io), ws.data_ptr(), nbytes, stream.cuda_stream))
+        launches_per_step = 4
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    # Capture one step in a CUDA graph (the launch chain of a layer-step).
+    graph = None
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        torch.cuda.synchronize()
+        graph = g
+    except Exception as ex:  # pragma: no cover - reported, not hidden
+        print(f"# graph capture failed ({ex}); timing eager launches", file=sys.stderr)
+    run = (lambda i: graph.replay()) if graph is not None else step
+    for _ in range(3):
+        run(0)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = elapsed_ms(torch, run, args.steps, stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    t_step = torch.tensor([ms / args.steps], device=device)
+    if world > 1:
+        dist.all_reduce(t_step, op=dist.ReduceOp.MAX)
+    us = t_step.item() * 1e3
+    _lib.check(A.device_error(clear=True)[0], "device error word after the timed region")
+
+    # ---- e2e: public API with host buffers (queries in, ctx out, every step) ----
+    h_q = [torch.empty_like(data[n], device="cpu").pin_memory() for n in ("q_abs", "q_idx", "w_idx")]
+    for h, n in zip(h_q, ("q_abs", "q_idx", "w_idx")):
+        h.copy_(data[n].cpu())
+    h_ctx = torch.empty(B, 64, 512, dtype=torch.float32).pin_memory()
+    h_sel = torch.empty(B, K, dtype=torch.int32).pin_memory()
+
+    def e2e_step(i=0):
+        for h, n in zip(h_q, ("q_abs", "q_idx", "w_idx")):
+            data[n].copy_(h, non_blocking=True)
+        step()
+        h_ctx.copy_(ctx, non_blocking=True)
+        h_sel.copy_(sel, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_e2e = elapsed_ms(torch, e2e_step, args.steps, stream)
+    t_e2e = torch.tensor([ms_e2e / args.steps], device=device)
+    if world > 1:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    h2d = sum(h.numel() * h.element_size() for h in h_q)
+    d2h = h_ctx.numel() * 4 + h_sel.numel() * 4
+
+    # ---- per-kernel breakdown through the individual entry points (roofline) ----
+    roof = None
+    breakdown = None
+    if world == 1:
+        breakdown, roof = kernel_breakdown(torch, A, _lib, cfg, data, args.steps, stream)
+
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras = side_configs(torch, A, _lib, device, stream)
+
+    if world > 1 and comm is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            cpu_us, n = time_cpu(args.cpu_seconds)
+            cpu = {"value": round(cpu_us, 1), "unit": "us/layer", "cores": cpu_threads(), "kind": "port",
+                   "sample": f"{n} x 1 of the 8 sequences (T=131072, top-2048) through oracle/attn_ref.py "
+                             f"(numpy fp32), scaled x8"}
+        line = {
+            "metric": METRIC, "value": round(us, 2), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded on device, BASELINE distributions)",
+            "config": {"workload": "cfg4: decode, 8 seq x T=131072, top-2048, owner layer",
+                       "batch": B, "T": T, "index_topk": K, "parallelism": f"kv-seq shard x{world}",
+                       "l2": "inputs (1.35 GB of caches) larger than L2", "graph": graph is not None},
+            "tokens_per_s": round(B / (us * 1e-6), 1),
+            "e2e": {"value": round(t_e2e.item() * 1e3, 2), "unit": "us/layer", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "roofline": roof,
+            "kernels_us": breakdown,
+            "cpu_baseline": cpu,
+            "extras": extras,
+        }
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def load_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+def traffic_per_key(kernel: str):
+    """DRAM bytes per unit measured by ncu, from the committed summary
+    profiles/<kernel>.txt (line 'dram_bytes_per_unit: X'), else None."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}.txt")
+    try:
+        for line in open(p):
+            if line.startswith("dram_bytes_per_unit:"):
+                return float(line.split(":")[1])
+    except Exception:
+        pass
+    return None
+
+
+def kernel_breakdown(torch, A, _lib, cfg, data, steps, stream):
+    """Each kernel of the layer-step timed with CUDA events on the launching stream."""
+    L = _lib.lib()
+    B, T, K = CFG4["batch"], CFG4["T"], CFG4["k"]
+    dev = data["q_abs"].device
+    index = torch.empty(B, T, dtype=torch.float32, device=dev)
+    sel = torch.empty(B, K, dtype=torch.int32, device=dev)
+    cnt = torch.empty(B, dtype=torch.int32, device=dev)
+    S = 16
+    o_part = torch.empty(B, S, 64, 512, dtype=torch.float32, device=dev)
+    l_part = torch.empty(B, S, 64, dtype=torch.float32, device=dev)
+    ctx = torch.empty(B, 64, 512, dtype=torch.float32, device=dev)
+    lse = torch.empty(B, 64, dtype=torch.float32, device=dev)
+    rows = _lib.Rows(B, 1, T, 0)
+    kc, lc = data["keys"].c(), data["kv"].c()
+    st = stream.cuda_stream
+    calls = {
+        "indexer_scores": lambda: L.wl_indexer_scores(C.byref(cfg), C.byref(kc), T, C.byref(rows),
+                                                      data["q_idx"].data_ptr(), data["w_idx"].data_ptr(),
+                                                      index.data_ptr(), T, st),
+        "topk": lambda: L.wl_indexer_topk(index.data_ptr(), T, C.byref(rows), T, K, None, sel.data_ptr(), K,
+                                          cnt.data_ptr(), st),
+        "mla_sparse_attn": lambda: L.wl_mla_sparse_attn(C.byref(cfg), C.byref(lc), T, C.byref(rows),
+                                                        data["q_abs"].data_ptr(), sel.data_ptr(), K,
+                                                        cnt.data_ptr(), 0, 0, T, 128, o_part.data_ptr(),
+                                                        l_part.data_ptr(), S, st),
+        "lse_merge": lambda: L.wl_lse_merge(o_part.data_ptr(), l_part.data_ptr(), B, S, S * 64 * 512, 64 * 512,
+                                            S * 64, 64, 64, 512, ctx.data_ptr(), lse.data_ptr(), st),
+    }
+    n = max(5, min(steps, 50))
+    ev = {k: [] for k in calls}
+    for it in range(n + 2):
+        for name, fn in calls.items():
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            _lib.check(fn(), name)
+            e.record(stream)
+            if it >= 2:
+                ev[name].append((s, e))
+    torch.cuda.synchronize()
+    us = {k: statistics.mean(s.elapsed_time(e) for s, e in v) * 1e3 for k, v in ev.items()}
+    # algorithmic bytes per launch
+    algo = {
+        "indexer_scores": B * T * (128 + 4 + 4) + B * (32 * 128 * 2 + 32 * 4),
+        "topk": B * T * 4 + B * K * 4,
+        "mla_sparse_attn": B * K * 1152 + B * S * (64 * 576 * 2) + B * S * 64 * 512 * 4,
+        "lse_merge": B * S * 64 * 512 * 4 + B * 64 * 512 * 4,
+    }
+    dom = max(us, key=us.get)
+    peaks = load_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = algo[dom] / (us[dom] * 1e-6) / 1e9
+    per_key = traffic_per_key(dom)
+    units = B * T if dom in ("indexer_scores", "topk") else B * K
+    roof = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": "fallback" if peaks.get("fallback") else "measured",
+            "traffic": round(per_key * units) if per_key else None, "algo_bytes": algo[dom]}
+    return {k: round(v, 2) for k, v in us.items()}, roof
+
+
+def side_configs(torch, A, _lib, device, stream):
+    """Short measurements of BASELINE configs 1, 2 and 3 on this GPU."""
+    out = {}
+    L = _lib.lib()
+    # decode, batch 1: config 2 (T=32768) and config 1 (T=4096), owner + consumer;
+    # enough cache instances that each step reads HBM (> 2x L2 in total).
+    for name, T in (("cfg2_decode_32k", 32768), ("cfg1_decode_4k", 4096)):
+        per = T * (1152 + 132)
+        n_inst = max(2, int(np.ceil(300e6 / per)))
+        cfg = A.glm52_cfg(T)
+        insts = [make_device_inputs(torch, 1, T, 0, 20260802 + i, device) for i in range(n_inst)]
+        nbytes = L.wl_attn_workspace_bytes(C.byref(cfg), T, 1)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        ios = []
+        for d in insts:
+            io, keep = A.decode_io(cfg, d["kv"], d["q_abs"], keys=d["keys"], q_idx=d["q_idx"], w_idx=d["w_idx"])
+            io2, keep2 = A.decode_io(cfg, d["kv"], d["q_abs"], mode=_lib.WL_MODE_CONSUMER,
+                                     sel_in=keep["sel_out"], sel_n_in=keep["sel_n_out"], canonical=True)
+            ios.append((io, keep, io2, keep2))
+        res = {}
+        for mode in (0, 1):
+            graphs = []
+            for i in range(n_inst):
+                io = ios[i][0] if mode == 0 else ios[i][2]
+                fn = lambda io=io: _lib.check(L.wl_attn_decode(C.byref(cfg), C.byref(io), ws.data_ptr(), nbytes,
+                                                               stream.cuda_stream))
+                fn()
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn()
+                graphs.append(g)
+            for i in range(3 * n_inst):
+                graphs[i % n_inst].replay()
+            torch.cuda.synchronize()
+            steps = 20 * n_inst
+            ms = elapsed_ms(torch, lambda i: graphs[i % n_inst].replay(), steps, stream)
+            us = ms / steps * 1e3
+            algo = (T * 132 if mode == 0 else 0) + min(2048, T) * 1152
+            res["owner" if mode == 0 else "consumer"] = {"us_per_layer": round(us, 2),
+                                                         "algo_bytes": algo,
+                                                         "achieved_gbs": round(algo / (us * 1e-6) / 1e9, 1)}
+        out[name] = res
+        del insts, ios
+        torch.cuda.empty_cache()
+    # chunked prefill: config 3 (4096 rows on a 4096 prefix, top-2048)
+    pos0, n_q = 4096, 4096
+    T = pos0 + n_q
+    cfg = A.glm52_cfg(T)
+    d = make_device_inputs(torch, 1, T, 0, 20260803, device, n_q=n_q)
+    fn = lambda i=0: A.attn_prefill(cfg, d["kv"], d["q_abs"], pos0, keys=d["keys"], q_idx=d["q_idx"],
+                                    w_idx=d["w_idx"])
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    ms = elapsed_ms(torch, fn, 5, stream) / 5
+    idx_flops = 2 * 32 * 128 * sum(pos0 + 1 + i for i in range(n_q))
+    att_flops = n_q * 2048 * 64 * (2 * 576 + 2 * 512)
+    out["cfg3_prefill"] = {"ms": round(ms, 3), "tflops": round((idx_flops + att_flops) / (ms * 1e-3) / 1e12, 1),
+                           "idx_gflop": round(idx_flops / 1e9, 1), "attn_gflop": round(att_flops / 1e9, 1)}
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,299 @@
+/*
+ * wl_attn.h — C ABI of the B200 (sm_100a) GLM-5.2 attention substep:
+ * DSA lightning-indexer scoring over fp8-e4m3 index keys, exact per-query
+ * top-k key selection, and absorbed-MLA attention over the bf16 latent cache,
+ * for decode and chunked prefill, optionally with the KV sequence sharded
+ * across the GPUs of one node (NCCL).
+ *
+ * Drop-in boundary. The reference runs this substep inside
+ *     run_attention(const Config&, const LayerWeights&, uint32_t layer,
+ *                   uint32_t pos, float* d_hidden, IndexShare&, cudaStream_t)
+ * at src/glm_layer_runner.cuh:525-527, specifically the block
+ * src/glm_layer_runner.cuh:582-644 (indexer -> index mask -> absorbed
+ * attention). Every entry point below replaces one piece of that block; the
+ * reference function each one stands in for is cited beside it.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only. Every pointer argument named "device" is
+ *    device memory owned by the caller; nothing here allocates on a hot path.
+ *  - Every call is stream-ordered on the caller's `stream` (a cudaStream_t
+ *    passed as void*; NULL is the legacy default stream) and returns a status
+ *    code instead of aborting (the reference aborts: GLM_CUDA_OK at
+ *    src/glm_loader.cuh:24-26, IndexShare::require at
+ *    src/glm_layer_runner.cuh:507-516, T > max_seq at :576-580).
+ *  - Shapes are GLM-5.2's (Config at src/glm_loader.cuh:33-69): 64 attention
+ *    heads, kv_lora 512 + rope 64 = 576-wide absorbed query and latent row,
+ *    32 indexer heads x 128. Other shapes return WL_ERR_UNSUPPORTED.
+ *  - Index selections ("sel") are int32 key positions. Lists this library
+ *    writes are canonical: strictly ascending, unique, inside [0, T).
+ */
+#ifndef WL_ATTN_H
+#define WL_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WL_ABI_VERSION 1
+
+/* ---- status codes --------------------------------------------------------- */
+enum {
+    WL_OK                = 0,
+    WL_ERR_ARG           = 1,  /* null pointer, bad size or stride                */
+    WL_ERR_T_EXCEEDS_MAX = 2,  /* T > cfg.T_max (reference: abort at :576-580)     */
+    WL_ERR_NO_INDICES    = 3,  /* consumer layer with nothing published (:507-516) */
+    WL_ERR_CUDA          = 4,  /* a CUDA runtime call failed                       */
+    WL_ERR_NCCL          = 5,  /* an NCCL call failed                              */
+    WL_ERR_TIMEOUT       = 6,  /* a bounded device-side wait ran out               */
+    WL_ERR_WORKSPACE     = 7,  /* workspace missing or smaller than required       */
+    WL_ERR_UNSUPPORTED   = 8,  /* shape outside the compiled GLM-5.2 dimensions    */
+    WL_ERR_DEVICE        = 9   /* a device-side bounds check fired                 */
+};
+
+/* Human-readable text for a status code (never NULL). */
+const char* wl_strerror(int status);
+
+/* ---- configuration (subset of Config, src/glm_loader.cuh:33-69) ----------- */
+typedef struct wl_attn_cfg {
+    int32_t n_heads;       /* num_attention_heads          = 64   */
+    int32_t kv_lora;       /* kv_lora_rank                 = 512  */
+    int32_t rope_dim;      /* qk_rope_head_dim             = 64   */
+    int32_t idx_heads;     /* index_n_heads                = 32   */
+    int32_t idx_dim;       /* index_head_dim               = 128  */
+    int32_t index_topk;    /* index_topk                   = 2048 */
+    float   softmax_scale; /* qk_head_dim^-0.5 = 1/16 (glm_layer_runner.cuh:641) */
+    float   idx_qk_scale;  /* index_head_dim^-0.5 (glm_kernels.cuh:463)         */
+    int32_t T_max;         /* Config::max_seq: rows the caller's caches hold    */
+} wl_attn_cfg;
+
+/* Fill `cfg` with GLM-5.2's values and the given cache capacity. */
+void wl_attn_cfg_glm52(wl_attn_cfg* cfg, int32_t T_max);
+
+/* ---- cache views ------------------------------------------------------------
+ * Latent cache: the reference keeps kv_c_cache [max_seq,512] and k_rot_cache
+ * [max_seq,64] in fp32, row = absolute position (glm_loader.cuh:282-283). Here
+ * the same two-pointer addressing holds bf16 rows. A packed [T,576] row is the
+ * case k_rot = c_kv + 512 with both row strides 576. Strides are in elements;
+ * row strides must be multiples of 8 and both pointers 16-byte aligned.
+ * `*_seq_stride` steps between independent sequences of a batch. */
+typedef struct wl_latent_cache {
+    const void* c_kv;   int64_t c_kv_row_stride;  int64_t c_kv_seq_stride;
+    const void* k_rot;  int64_t k_rot_row_stride; int64_t k_rot_seq_stride;
+} wl_latent_cache;
+
+/* Indexer key cache of an owning layer: the reference stores bf16 [max_seq,128]
+ * (glm_loader.cuh:307, written by indexer_store_k_bf16 at glm_kernels.cuh:280).
+ * Here: fp8-e4m3 [T, idx_dim] packed rows (128 bytes each) plus one fp32
+ * dequantisation scale per key; key t's value is e4m3(keys[t]) * scale[t].
+ * `keys` must be 16-byte aligned. Seq strides: bytes for keys, floats for scale. */
+typedef struct wl_index_cache {
+    const void*  keys;  int64_t keys_seq_stride;
+    const float* scale; int64_t scale_seq_stride;
+} wl_index_cache;
+
+/* Query rows of one call. Row r belongs to sequence r / rows_per_seq and sees
+ * keys [0, len0 + (r % rows_per_seq) * len_step), clamped to T. Decode:
+ * rows_per_seq = 1, len0 = T, len_step = 0. Chunked prefill of n_q rows after
+ * a pos0-token prefix: rows_per_seq = n_q, len0 = pos0 + 1, len_step = 1 (the
+ * causal rule of run_prefill_layer_major, glm_layer_runner.cuh:963-973). */
+typedef struct wl_rows {
+    int32_t n_rows;
+    int32_t rows_per_seq;
+    int32_t len0;
+    int32_t len_step;
+} wl_rows;
+
+/* ---- IndexShare (glm_layer_runner.cuh:485-517; ref_glm_chain.py:445-462) --
+ * Owner layers publish their raw top-k; "shared" layers read it unchanged;
+ * a shared layer with nothing published fails with WL_ERR_NO_INDICES. `dense`
+ * is the standalone-layer test mode: attend every key, never fail. */
+typedef struct wl_index_share {
+    const int32_t* idx;       /* device [n_rows, stride] canonical lists     */
+    const int32_t* n_dev;     /* device [n_rows] counts (may be NULL)        */
+    int64_t        stride;    /* elements between rows of idx                */
+    int32_t        n;         /* count when n_dev is NULL                    */
+    uint32_t       producer;  /* layer that published; UINT32_MAX = none     */
+    int32_t        dense;
+} wl_index_share;
+
+void wl_index_share_reset(wl_index_share* s);                 /* IndexShare::reset   */
+void wl_index_share_publish(wl_index_share* s, uint32_t layer, /* IndexShare::publish */
+                            const int32_t* idx, const int32_t* n_dev,
+                            int64_t stride, int32_t n);
+int  wl_index_share_require(const wl_index_share* s, uint32_t layer); /* ::require */
+
+/* ---- decode (one query token per sequence) ------------------------------- */
+enum { WL_MODE_OWNER = 0, WL_MODE_CONSUMER = 1, WL_MODE_DENSE = 2 };
+enum { WL_SEL_CANONICAL = 1 };  /* consumer asserts sel_in is already canonical */
+
+typedef struct wl_attn_decode_io {
+    int32_t batch;              /* independent sequences                       */
+    int32_t T;                  /* keys per sequence (= pos + 1)               */
+    wl_latent_cache latent;
+    wl_index_cache  index;      /* owner only                                  */
+    const void*  q_abs;         /* bf16 [batch, n_heads, kv_lora+rope_dim]     */
+    const void*  q_idx;         /* bf16 [batch, idx_heads, idx_dim], post-RoPE */
+    const float* w_idx;         /* fp32 [batch, idx_heads], x idx_heads^-0.5   */
+    int32_t  mode;              /* WL_MODE_*                                   */
+    int32_t  sel_flags;         /* WL_SEL_CANONICAL                            */
+    int32_t* sel_out;           /* owner: [batch, sel_stride] (may be NULL)    */
+    int32_t* sel_n_out;         /* owner: [batch] counts (may be NULL)         */
+    const int32_t* sel_in;      /* consumer: [batch, sel_stride]               */
+    const int32_t* sel_n_in;    /* consumer: [batch] counts, or NULL -> sel_n  */
+    int32_t  sel_n;             /* consumer count when sel_n_in is NULL        */
+    int64_t  sel_stride;        /* >= min(index_topk, T)                       */
+    float*   index_out;         /* owner, optional: [batch, index_stride] fp32 */
+    int64_t  index_stride;
+    float*   ctx;               /* out: fp32 [batch, n_heads, kv_lora]         */
+    float*   lse;               /* out, optional: fp32 [batch, n_heads]        */
+} wl_attn_decode_io;
+
+/* Workspace needed by wl_attn_decode / wl_attn_decode_sharded for up to
+ * `batch` sequences of up to T_max keys (bytes, 256-byte aligned base). */
+size_t wl_attn_workspace_bytes(const wl_attn_cfg* cfg, int32_t T_max, int32_t batch);
+
+/* The attention substep for one decode token per sequence. Replaces
+ * glm_layer_runner.cuh:582-644: owner -> indexer scores (glm_kernels.cuh:
+ * 453-477) + top-k (:344-414) + sparse absorbed attention (glm_layer_runner.cuh:
+ * 251-298) over the selected keys; consumer -> the same attention over sel_in;
+ * dense -> attention over every key. Output ctx is the reference's s_ctx. */
+int wl_attn_decode(const wl_attn_cfg* cfg, const wl_attn_decode_io* io,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same substep with run_attention's IndexShare dispatch
+ * (glm_layer_runner.cuh:594-619): if `owner`, run the indexer and publish the
+ * selection (io->sel_out, which must be set) into *share; otherwise require
+ * *share and consume it (or attend densely if share->dense). */
+int wl_attn_layer_decode(const wl_attn_cfg* cfg, wl_attn_decode_io* io,
+                         int32_t owner, uint32_t layer, wl_index_share* share,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- chunked prefill ------------------------------------------------------
+ * n_q new rows for one sequence whose cache already holds the pos0-token
+ * prefix AND the n_q new rows (T = pos0 + n_q). Row i is causal over keys
+ * [0, pos0 + i]. The reference has no batched prefill attention: it calls the
+ * decode form once per row in ascending order (glm_layer_runner.cuh:963-983);
+ * this computes exactly those per-row results in one call. */
+typedef struct wl_attn_prefill_io {
+    int32_t n_q;
+    int32_t pos0;
+    wl_latent_cache latent;
+    wl_index_cache  index;
+    const void*  q_abs;         /* bf16 [n_q, n_heads, 576]                   */
+    const void*  q_idx;         /* bf16 [n_q, idx_heads, idx_dim]             */
+    const float* w_idx;         /* fp32 [n_q, idx_heads]                      */
+    int32_t  mode;
+    int32_t  sel_flags;
+    int32_t* sel_out;           /* owner: [n_q, sel_stride]                   */
+    int32_t* sel_n_out;         /* owner: [n_q]                               */
+    const int32_t* sel_in;      /* consumer: [n_q, sel_stride]                */
+    const int32_t* sel_n_in;    /* consumer: [n_q] or NULL -> min(topk, row len) */
+    int64_t  sel_stride;
+    float*   index_out;         /* optional [n_q, index_stride]               */
+    int64_t  index_stride;
+    float*   ctx;               /* out: fp32 [n_q, n_heads, kv_lora]          */
+    float*   lse;               /* out, optional: fp32 [n_q, n_heads]         */
+} wl_attn_prefill_io;
+
+size_t wl_attn_prefill_workspace_bytes(const wl_attn_cfg* cfg, int32_t n_q, int32_t T);
+int wl_attn_prefill(const wl_attn_cfg* cfg, const wl_attn_prefill_io* io,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- the individual hot-path kernels ------------------------------------- */
+
+/* a1+a2 fused: index[r][t] = sum_h w[r][h] * relu(idx_qk_scale * scale[t] *
+ * (q[r][h] . e4m3(keys[t]))) for t < len(r). Replaces indexer_scores_relu +
+ * indexer_combine (glm_kernels.cuh:308-340); no [H,T] intermediate. */
+int wl_indexer_scores(const wl_attn_cfg* cfg, const wl_index_cache* cache,
+                      int32_t T, const wl_rows* rows,
+                      const void* q_idx, const float* w_idx,
+                      float* index_out, int64_t index_stride, void* stream);
+
+/* a3: exact top-min(k, len(r)) per row, ties to the lowest index, written
+ * canonical (ascending); k >= len(r) writes the identity 0..len-1. Replaces
+ * indexer_topk (glm_kernels.cuh:344-414) / ref_glm_chain.py:504-515.
+ * `cand_idx` (may be NULL) maps positions to output indices: row r's element
+ * j is reported as cand_idx[r*index_stride + j] (used to merge candidates). */
+int wl_indexer_topk(const float* index, int64_t index_stride, const wl_rows* rows,
+                    int32_t T, int32_t k, const int32_t* cand_idx,
+                    int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
+                    void* stream);
+
+/* a5 semantics: turn an arbitrary index list (any order, duplicates, entries
+ * outside [0, len(r))) into the canonical list of the keys it keeps. Same
+ * selection as index_mask_fill/scatter (glm_kernels.cuh:526-537): out-of-range
+ * entries unmask nothing, duplicates count once. */
+int wl_sel_normalize(const int32_t* sel_in, int64_t in_stride,
+                     const int32_t* n_in_dev, int32_t n_in,
+                     const wl_rows* rows, int32_t T,
+                     int32_t* sel_out, int64_t out_stride, int32_t* n_out_dev,
+                     void* stream);
+
+/* a7: sparse absorbed-MLA attention over canonical lists (NULL = every key),
+ * restricted to the key window [win_lo, win_hi) whose first key is cache row 0,
+ * split into CTAs of `split_keys` selected keys (multiple of 128; 0 = the whole
+ * list in one CTA). Writes per split the normalised partial output and its
+ * log-sum-exp: o_part[(r*max_splits + s)*n_heads*kv_lora ...],
+ * lse_part[(r*max_splits + s)*n_heads ...]. Replaces mla_decode_absorbed
+ * (glm_layer_runner.cuh:251-298) with its mask (glm_kernels.cuh:526-545). */
+int wl_mla_sparse_attn(const wl_attn_cfg* cfg, const wl_latent_cache* cache,
+                       int32_t T, const wl_rows* rows, const void* q_abs,
+                       const int32_t* sel, int64_t sel_stride,
+                       const int32_t* sel_n_dev, int32_t sel_n,
+                       int64_t win_lo, int64_t win_hi, int32_t split_keys,
+                       float* o_part, float* lse_part, int32_t max_splits,
+                       void* stream);
+
+/* (o, lse) merge of `n_parts` partials per row: o = sum_s e^(lse_s - L) o_s,
+ * L = log sum_s e^(lse_s). Part s of row r lives at o_part + r*row_stride +
+ * s*part_stride (floats; lse likewise with lse_row_stride / lse_part_stride). */
+int wl_lse_merge(const float* o_part, const float* lse_part, int32_t n_rows,
+                 int32_t n_parts, int64_t row_stride, int64_t part_stride,
+                 int64_t lse_row_stride, int64_t lse_part_stride,
+                 int32_t n_heads, int32_t kv_lora,
+                 float* ctx, float* lse, void* stream);
+
+/* ---- KV-sequence sharding over the GPUs of one node (NCCL) ----------------
+ * Rank r holds keys [t0, t0 + io->T) of every cache. Each rank scores and
+ * selects locally; one NCCL all-gather merges the (score, global index)
+ * candidates into the exact single-GPU selection, each rank attends over its
+ * part of it, and a second all-gather merges the (o, lse) partials. Every
+ * rank returns the full ctx/lse and (owner) the global selection. No reference
+ * counterpart: the reference is single-GPU (README.md:88). */
+typedef struct wl_comm wl_comm;
+int wl_comm_unique_id(uint8_t id_out[128]);
+int wl_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank,
+                   wl_comm** out);
+int wl_comm_destroy(wl_comm* comm);
+
+typedef struct wl_shard {
+    int64_t t0;        /* global position of this rank's cache row 0 */
+    int64_t T_global;  /* keys across all ranks                      */
+} wl_shard;
+
+size_t wl_attn_sharded_workspace_bytes(const wl_attn_cfg* cfg, int32_t T_local_max,
+                                       int32_t batch, int32_t nranks);
+int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io,
+                           const wl_shard* shard, wl_comm* comm,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- diagnostics ------------------------------------------------------------ */
+/* Device-side error word of the calling thread's current device: bounds-check
+ * failures and bounded-wait timeouts of any kernel of this library set it.
+ * Synchronises the device. `clear` resets it to 0. Returns the WL_ERR_* code
+ * (WL_OK when clean); *detail (may be NULL) receives the raw word. */
+int wl_device_error(int32_t clear, uint32_t* detail);
+
+/* sizeof of each public struct, for binding checks: fills up to n entries in
+ * the order cfg, latent_cache, index_cache, rows, index_share, decode_io,
+ * prefill_io, shard; returns how many exist. */
+int32_t wl_struct_sizes(int64_t* out, int32_t n);
+int32_t wl_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WL_ATTN_H */

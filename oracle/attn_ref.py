@@ -1,0 +1,266 @@
+"""CPU oracle for the GLM-5.2 attention substep — TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg may import this module, and only as the checker / reported baseline. The
+product path (``windlass_b200``) never calls it: it fails loudly when its CUDA
+library is missing.
+
+This is a numpy restatement of the reference's algorithm for the path, each
+function citing the reference it follows (paths inside ssubbotin/windlass):
+
+  indexer_scores   tools/ref_glm_chain.py:482-501   (relu between qk and the
+                   head sum; two scales D^-0.5 and, folded into w, H^-0.5)
+  indexer_topk     tools/ref_glm_chain.py:504-515   (min(k, T); stable argsort:
+                   ties to the lowest index)
+  index_drop_mask  tools/ref_glm_chain.py:518-529   (out-of-range indices
+                   unmask nothing)
+  mla_absorbed     src/glm_layer_runner.cuh:251-298 (absorbed form of
+                   attn_block's s = q.K, drop -> -inf, softmax, p.V,
+                   tools/ref_glm_chain.py:616-638)
+  lse_merge        the standard (o, lse) combination of disjoint key sets
+  quantize_e4m3    BASELINE's fp8 index-key format (not in the reference):
+                   e4m3 (OCP "fn", round-to-nearest-even) with one fp32 scale
+                   per key = amax / 448.
+
+The oracle is pinned against the reference itself: tests/golden/ holds
+outputs of tools/ref_glm_indexer.py and of ref_glm_chain.attn_block run in
+the build container (tests/golden/make_golden.py), and tests/test_oracle.py
+checks these functions against them.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+try:
+    import ml_dtypes  # e4m3 rounding
+    _E4M3 = ml_dtypes.float8_e4m3fn
+except Exception:  # pragma: no cover - ml_dtypes ships with the image
+    _E4M3 = None
+
+E4M3_MAX = 448.0
+
+
+# ---- bf16 / e4m3 helpers ----------------------------------------------------------------
+
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> bf16 bit pattern, round-to-nearest-even (torch's cast)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    rnd = ((u >> 16) & 1).astype(np.uint32) + np.uint32(0x7FFF)
+    return ((u + rnd) >> 16).astype(np.uint16)
+
+
+def from_bf16_bits(u: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(u, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    return from_bf16_bits(to_bf16_bits(x))
+
+
+def quantize_e4m3(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Per-row e4m3 quantisation: returns (uint8 bit patterns [T, D], scale [T] fp32)."""
+    x = np.asarray(x, dtype=np.float32)
+    amax = np.abs(x).max(axis=-1)
+    scale = np.where(amax > 0, amax / np.float32(E4M3_MAX), np.float32(1.0)).astype(np.float32)
+    q = (x / scale[..., None]).astype(np.float32)
+    bits = q.astype(_E4M3).view(np.uint8)
+    return bits, scale
+
+
+def e4m3_to_f32(bits: np.ndarray) -> np.ndarray:
+    return np.asarray(bits, dtype=np.uint8).view(_E4M3).astype(np.float32)
+
+
+def dequant_e4m3(bits: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """Key values the indexer sees: e4m3(bits) * scale, in fp32."""
+    return (e4m3_to_f32(bits) * np.asarray(scale, dtype=np.float32)[..., None]).astype(np.float32)
+
+
+# ---- the hot path ------------------------------------------------------------------------
+
+def indexer_scores(q: np.ndarray, K: np.ndarray, w: np.ndarray, D: int | None = None) -> np.ndarray:
+    """index[t] = sum_h w[h] * relu((q[h] . K[t]) * D^-0.5)  (ref_glm_chain.py:482-501).
+
+    q [H, D] fp32 (post-RoPE), K [T, D] fp32 (dequantised keys), w [H] fp32
+    (already x H^-0.5, ref_glm_chain.py:499). Returns [T] fp32."""
+    q = np.asarray(q, np.float32)
+    K = np.asarray(K, np.float32)
+    w = np.asarray(w, np.float32)
+    D = q.shape[-1] if D is None else D
+    s = np.maximum((q @ K.T) * np.float32(D ** -0.5), 0.0)
+    return (w[:, None] * s).sum(0, dtype=np.float32)
+
+
+def indexer_topk(index: np.ndarray, k: int) -> np.ndarray:
+    """The selected keys (ref_glm_chain.py:504-515): argsort(-index, stable)[:min(k,T)]."""
+    kk = min(k, index.shape[0])
+    return np.argsort(-index, kind="stable")[:kk].astype(np.int32)
+
+
+def index_drop_mask(sel: np.ndarray, T: int) -> np.ndarray:
+    """True == DROP; indices outside [0, T) unmask nothing (ref_glm_chain.py:518-529)."""
+    drop = np.ones(T, bool)
+    sel = np.asarray(sel)
+    drop[sel[(sel >= 0) & (sel < T)]] = False
+    return drop
+
+
+def canonical(sel: np.ndarray, T: int) -> np.ndarray:
+    """The selection as the ascending list of kept keys."""
+    return np.nonzero(~index_drop_mask(sel, T))[0].astype(np.int32)
+
+
+def mla_absorbed(q_abs: np.ndarray, c_kv: np.ndarray, k_rot: np.ndarray, drop: np.ndarray | None,
+                 scale: float, dtype=np.float64) -> tuple[np.ndarray, np.ndarray]:
+    """Absorbed MLA attention of one query (glm_layer_runner.cuh:251-298).
+
+    q_abs [H, L+R] (absorbed latent query | roped rope query), c_kv [T, L],
+    k_rot [T, R], drop [T] bool (True = masked) or None. Returns
+    ctx [H, L] and lse [H] (natural log of the softmax denominator of the
+    scaled scores)."""
+    L = c_kv.shape[1]
+    q = np.asarray(q_abs, dtype)
+    kv = np.asarray(c_kv, dtype)
+    kr = np.asarray(k_rot, dtype)
+    s = (q[:, :L] @ kv.T + q[:, L:] @ kr.T) * dtype(scale)  # [H, T]
+    if drop is not None and drop.any():
+        s = np.where(drop[None, :], -np.inf, s)
+    m = s.max(-1, keepdims=True)
+    p = np.exp(s - m)
+    z = p.sum(-1, keepdims=True)
+    ctx = (p @ kv) / z
+    lse = (m + np.log(z))[:, 0]
+    return ctx, lse
+
+
+def mla_sparse(q_abs, c_kv, k_rot, sel, scale, dtype=np.float64):
+    """mla_absorbed over the keys `sel` keeps (gathering only those rows)."""
+    T = c_kv.shape[0]
+    keep = canonical(sel, T)
+    return mla_absorbed(q_abs, c_kv[keep], k_rot[keep], None, scale, dtype)
+
+
+def lse_merge(os: list[np.ndarray], lses: list[np.ndarray]) -> tuple[np.ndarray, np.ndarray]:
+    """Combine partial (ctx, lse) over disjoint key sets."""
+    L = np.stack(lses)  # [S, H]
+    M = L.max(0)
+    Mf = np.where(np.isfinite(M), M, 0.0)
+    wgt = np.where(np.isfinite(L), np.exp(L - Mf), 0.0)
+    W = wgt.sum(0)
+    o = sum(wgt[i][:, None] * os[i] for i in range(len(os))) / np.where(W > 0, W, 1.0)[:, None]
+    return o, np.where(W > 0, Mf + np.log(np.where(W > 0, W, 1.0)), -np.inf)
+
+
+# ---- the substep ---------------------------------------------------------------------------
+
+def decode_step(inp: dict, k: int, mode: str = "owner", sel_in=None, dtype=np.float64):
+    """One decode token of one sequence: owner -> scores, top-k, sparse attention;
+    consumer -> attention over sel_in; dense -> over every key.
+
+    inp: c_kv [T,512] f32, k_rot [T,64] f32, q_abs [64,576] f32, q_idx [32,128]
+    f32, w_idx [32] f32, idx_bits [T,128] u8, idx_scale [T] f32, scale."""
+    T = inp["c_kv"].shape[0]
+    out = {}
+    if mode == "owner":
+        K = dequant_e4m3(inp["idx_bits"], inp["idx_scale"])
+        idx = indexer_scores(inp["q_idx"], K, inp["w_idx"])
+        sel = indexer_topk(idx, k)
+        out.update(index=idx, sel=sel)
+    elif mode == "consumer":
+        if sel_in is None:
+            raise RuntimeError("shared layer with no published indices")
+        sel = np.asarray(sel_in)
+    else:
+        sel = np.arange(T, dtype=np.int32)
+    ctx, lse = mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, inp["scale"], dtype)
+    out.update(ctx=ctx, lse=lse)
+    return out
+
+
+def prefill_rows(inp: dict, pos0: int, n_q: int, k: int, rows=None, dtype=np.float64):
+    """Per-row decode semantics of chunked prefill (run_prefill_layer_major,
+    glm_layer_runner.cuh:963-983): row i sees keys [0, pos0+i] and selects its
+    own top-k over exactly those. inp holds per-row q_abs [n_q,64,576],
+    q_idx [n_q,32,128], w_idx [n_q,32] and the full caches."""
+    K = dequant_e4m3(inp["idx_bits"], inp["idx_scale"])
+    res = []
+    for i in (range(n_q) if rows is None else rows):
+        T = pos0 + i + 1
+        idx = indexer_scores(inp["q_idx"][i], K[:T], inp["w_idx"][i])
+        sel = indexer_topk(idx, k)
+        ctx, lse = mla_sparse(inp["q_abs"][i], inp["c_kv"][:T], inp["k_rot"][:T], sel, inp["scale"], dtype)
+        res.append(dict(index=idx, sel=sel, ctx=ctx, lse=lse))
+    return res
+
+
+def sharded_decode(inp: dict, k: int, nranks: int):
+    """The sharded algorithm on one host: contiguous key shards, local top-k
+    candidates, exact global selection from the candidates (ties to the lowest
+    global index), per-shard partial attention, (o, lse) merge."""
+    T = inp["c_kv"].shape[0]
+    bounds = [(r * T // nranks, (r + 1) * T // nranks) for r in range(nranks)]
+    K = dequant_e4m3(inp["idx_bits"], inp["idx_scale"])
+    cs, ci = [], []
+    for lo, hi in bounds:
+        idx = indexer_scores(inp["q_idx"], K[lo:hi], inp["w_idx"])
+        loc = np.sort(indexer_topk(idx, k))
+        cs.append(idx[loc])
+        ci.append(loc + lo)
+    cs, ci = np.concatenate(cs), np.concatenate(ci)  # ascending global index
+    glob = np.sort(ci[indexer_topk(cs, min(k, T))])
+    os_, ls_ = [], []
+    for lo, hi in bounds:
+        mine = glob[(glob >= lo) & (glob < hi)] - lo
+        if mine.size == 0:
+            os_.append(np.zeros((inp["q_abs"].shape[0], inp["c_kv"].shape[1])))
+            ls_.append(np.full(inp["q_abs"].shape[0], -np.inf))
+            continue
+        o, l = mla_absorbed(inp["q_abs"], inp["c_kv"][lo:hi][mine], inp["k_rot"][lo:hi][mine], None,
+                            inp["scale"])
+        os_.append(o)
+        ls_.append(l)
+    ctx, lse = lse_merge(os_, ls_)
+    return dict(sel=glob, ctx=ctx, lse=lse)
+
+
+# ---- seeded inputs ------------------------------------------------------------
+
+def rope_interleave(x: np.ndarray, pos: np.ndarray, theta: float) -> np.ndarray:
+    """Interleaved-in, halves-out RoPE (ref_glm_chain.py:85-106), float64 tables."""
+    rot = x.shape[-1]
+    inv = 1.0 / (theta ** (np.arange(0, rot, 2, dtype=np.float64) / rot))
+    ang = np.asarray(pos, np.float64)[:, None] * inv[None, :]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    a, b = x[..., 0::2], x[..., 1::2]
+    return np.concatenate([a * cos - b * sin, b * cos + a * sin], axis=-1).astype(np.float32)
+
+
+def make_inputs(T: int, config: int, seq: int = 0, n_q: int = 1, theta: float = 1e6) -> dict:
+    """Seeded synthetic inputs with BASELINE's shapes and distributions.
+
+    seed = 20260801 + config + 1000 * seq. c_kv ~ N(0,1) RMS-normalised per
+    row; k_rot ~ N(0,1) roped at positions 0..T-1; q_abs, q_idx ~ N(0,1); all
+    of those rounded to bf16. Index keys ~ N(0,1) quantised to e4m3 with a
+    per-key scale; w ~ U(0,1). Arrays are float32 holding bf16-exact values;
+    n_q > 1 gives per-row queries for prefill."""
+    rng = np.random.default_rng(20260801 + config + 1000 * seq)
+    ckv = rng.standard_normal((T, 512), dtype=np.float32)
+    ckv = ckv / np.sqrt((ckv * ckv).mean(-1, keepdims=True) + 1e-6)
+    krot = rope_interleave(rng.standard_normal((T, 64), dtype=np.float32), np.arange(T), theta)
+    shape_q = (n_q,) if n_q > 1 else ()
+    q_abs = rng.standard_normal(shape_q + (64, 576), dtype=np.float32)
+    q_idx = rng.standard_normal(shape_q + (32, 128), dtype=np.float32)
+    w = rng.uniform(0.0, 1.0, shape_q + (32,)).astype(np.float32)
+    bits, scale = quantize_e4m3(rng.standard_normal((T, 128), dtype=np.float32))
+    return dict(c_kv=bf16_round(ckv), k_rot=bf16_round(krot), q_abs=bf16_round(q_abs),
+                q_idx=bf16_round(q_idx), w_idx=w, idx_bits=bits, idx_scale=scale,
+                scale=1.0 / 16.0)
+
+
+def bf16_ulp_error(ref: np.ndarray, got: np.ndarray) -> float:
+    """Max |got - ref| in units of one bf16 ulp at the tensor's scale, 2^-8 max|ref|
+    (the metric of the reference's layer test, src/test_glm_layer.cu:141-200)."""
+    ref = np.asarray(ref, np.float64)
+    got = np.asarray(got, np.float64)
+    unit = 2.0 ** -8 * np.abs(ref).max()
+    return float(np.abs(got - ref).max() / unit) if unit > 0 else float(np.abs(got - ref).max())

@@ -1,0 +1,427 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the oracle.
+
+Tolerances, from the reference's own gates and BASELINE:
+  * index scores: max |gpu - oracle| <= 1e-5 * max|oracle| (the reference's
+    fp32 indexer gate, src/test_glm_indexer.cu:167);
+  * selection: bit-exact sets wherever the oracle's score is farther than that
+    tolerance from the k-th score; top-k on identical scores: bit-exact;
+  * attention: |gpu - oracle| <= 2 bf16 ulp of the output scale,
+    2 * 2^-8 * max|oracle| (src/test_glm_layer.cu:141-200), fp32 accumulation;
+    the arithmetic gate uses the GPU's own selection (the reference's
+    forced-selection gate), the end-to-end one the oracle's;
+  * sparse == dense below index_topk: bit-identical (plan:337-340).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import attn_ref as o
+from windlass_b200 import _lib
+from windlass_b200 import attn as A
+
+pytestmark = pytest.mark.gpu
+
+IDX_TOL = 1e-5
+ULP_TOL = 2.0
+
+
+def dev(x, dtype):
+    return torch.from_numpy(np.ascontiguousarray(x)).to("cuda").to(dtype)
+
+
+def to_gpu(inp, batch=False):
+    """Oracle inputs (float32 arrays holding bf16 values) -> device tensors."""
+    b = (lambda x: x) if batch else (lambda x: x[None])
+    return dict(kv=A.LatentKV(dev(b(inp["c_kv"]), torch.bfloat16), dev(b(inp["k_rot"]), torch.bfloat16)),
+                keys=A.IndexKeys(dev(b(inp["idx_bits"]), torch.uint8), dev(b(inp["idx_scale"]), torch.float32)),
+                q_abs=dev(b(inp["q_abs"]), torch.bfloat16), q_idx=dev(b(inp["q_idx"]), torch.bfloat16),
+                w_idx=dev(b(inp["w_idx"]), torch.float32))
+
+
+def stack_inputs(inps):
+    keys = ("c_kv", "k_rot", "idx_bits", "idx_scale", "q_abs", "q_idx", "w_idx")
+    out = {k: np.stack([i[k] for i in inps]) for k in keys}
+    return to_gpu(out, batch=True)
+
+
+def cpu(t):
+    return t.detach().cpu().numpy()
+
+
+def assert_ulp(ref, got, tol=ULP_TOL, what=""):
+    e = o.bf16_ulp_error(ref, got)
+    assert e <= tol, f"{what}: {e:.3f} bf16 ulp > {tol}"
+
+
+def assert_sel_close(gpu_sel, ref_index, k, tol_abs):
+    """Sets agree except for keys whose oracle score is within tol of the k-th."""
+    kk = min(k, ref_index.shape[0])
+    ref = set(o.indexer_topk(ref_index, k).tolist())
+    got = set(gpu_sel[:kk].tolist())
+    assert len(got) == kk
+    thr = np.sort(ref_index)[::-1][kk - 1]
+    for t in ref ^ got:
+        assert abs(ref_index[t] - thr) <= tol_abs, (t, ref_index[t], thr)
+    return len(ref ^ got)
+
+
+def canonical_ok(sel, n, T):
+    s = sel[:n]
+    assert np.all(np.diff(s) > 0) and (n == 0 or (s[0] >= 0 and s[-1] < T))
+
+
+@pytest.fixture(autouse=True)
+def clean_device_error():
+    A.device_error(clear=True)
+    yield
+    st, word = A.device_error(clear=True)
+    assert st == _lib.WL_OK, f"device error word 0x{word:08x}"
+
+
+# ---- indexer scores -----------------------------------------------------------------------
+
+@pytest.mark.parametrize("T", [1000, 4096, 32768])
+def test_indexer_scores_vs_oracle(T):
+    inp = o.make_inputs(T, 1)
+    g = to_gpu(inp)
+    cfg = A.glm52_cfg(T)
+    idx = cpu(A.indexer_scores(cfg, g["keys"], g["q_idx"], g["w_idx"], T, _lib.Rows(1, 1, T, 0)))[0]
+    ref = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+    assert np.abs(idx - ref).max() <= IDX_TOL * np.abs(ref).max()
+
+
+def test_indexer_scores_batch_of_sequences():
+    T = 777
+    inps = [o.make_inputs(T, 4, seq=s) for s in range(3)]
+    g = stack_inputs(inps)
+    cfg = A.glm52_cfg(T)
+    idx = cpu(A.indexer_scores(cfg, g["keys"], g["q_idx"], g["w_idx"], T, _lib.Rows(3, 1, T, 0)))
+    for s, inp in enumerate(inps):
+        ref = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+        assert np.abs(idx[s] - ref).max() <= IDX_TOL * np.abs(ref).max()
+
+
+def test_indexer_negative_weights_and_relu():
+    inp = o.make_inputs(512, 5)
+    inp["w_idx"] = inp["w_idx"] - 0.5  # mixed signs, as with real weights_proj
+    g = to_gpu(inp)
+    idx = cpu(A.indexer_scores(A.glm52_cfg(512), g["keys"], g["q_idx"], g["w_idx"], 512, _lib.Rows(1, 1, 512, 0)))[0]
+    ref = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+    assert (ref < 0).any()
+    assert np.abs(idx - ref).max() <= IDX_TOL * np.abs(ref).max()
+
+
+# ---- top-k ---------------------------------------------------------------------------------
+
+def _topk_case(x, k):
+    t = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()[None]
+    sel, n = A.indexer_topk(t, k)
+    n = int(cpu(n)[0])
+    s = cpu(sel)[0][:n]
+    ref = o.indexer_topk(x, k)
+    assert n == min(k, x.shape[0])
+    canonical_ok(s, n, x.shape[0])
+    assert np.array_equal(s, np.sort(ref)), "top-k set or tie rule differs"
+
+
+@pytest.mark.parametrize("T,k", [(4096, 2048), (32768, 2048), (131072, 2048), (5000, 1), (70000, 4095),
+                                 (2048, 2048), (1000, 2048), (1, 2048)])
+def test_topk_random_exact(T, k):
+    rng = np.random.default_rng(T + k)
+    _topk_case(rng.standard_normal(T).astype(np.float32), k)
+
+
+def test_topk_ties_resolve_to_lowest_index():
+    rng = np.random.default_rng(7)
+    x = rng.integers(0, 5, 10000).astype(np.float32)  # massive ties at the boundary
+    _topk_case(x, 3000)
+    _topk_case(np.zeros(9000, np.float32), 2048)
+
+
+def test_topk_signed_zero_and_negatives():
+    rng = np.random.default_rng(8)
+    x = rng.choice(np.array([-0.0, 0.0, -1.5, 2.0, -np.inf], np.float32), 6000)
+    _topk_case(x, 2048)
+    _topk_case(-np.abs(rng.standard_normal(6000)).astype(np.float32), 100)
+
+
+def test_topk_candidate_index_mapping():
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal(3000).astype(np.float32)
+    cand = (np.arange(3000) * 3 + 11).astype(np.int32)
+    t = torch.from_numpy(x).cuda()[None]
+    sel, n = A.indexer_topk(t, 500, cand_idx=torch.from_numpy(cand).cuda()[None])
+    ref = np.sort(cand[o.indexer_topk(x, 500)])
+    assert np.array_equal(cpu(sel)[0], ref)
+
+
+def test_topk_on_gpu_scores_is_bit_exact():
+    T = 32768
+    inp = o.make_inputs(T, 2)
+    g = to_gpu(inp)
+    idx = A.indexer_scores(A.glm52_cfg(T), g["keys"], g["q_idx"], g["w_idx"], T, _lib.Rows(1, 1, T, 0))
+    sel, n = A.indexer_topk(idx, 2048)
+    assert np.array_equal(cpu(sel)[0], np.sort(o.indexer_topk(cpu(idx)[0], 2048)))
+
+
+# ---- list normalisation (the index-mask semantics) ------------------------------------------
+
+def test_normalize_matches_mask_semantics():
+    rng = np.random.default_rng(10)
+    T = 5000
+    lst = np.concatenate([rng.integers(-50, T + 50, 3000), [T, T + 3, -1, 0, 0, T - 1]]).astype(np.int32)
+    out, n = A.sel_normalize(torch.from_numpy(lst).cuda()[None], T)
+    n = int(cpu(n)[0])
+    assert np.array_equal(cpu(out)[0][:n], o.canonical(lst, T))
+
+
+# ---- attention ---------------------------------------------------------------------------
+
+def _attn(cfg, g, sel_np=None, split_keys=0, max_splits=1):
+    T = g["kv"].T
+    sel = None if sel_np is None else torch.from_numpy(np.ascontiguousarray(sel_np, np.int32)).cuda()[None]
+    rows = _lib.Rows(1, 1, T, 0)
+    op, lp = A.mla_sparse_attn(cfg, g["kv"], g["q_abs"], rows, sel=sel,
+                               sel_n=None if sel is None else sel.shape[1], split_keys=split_keys,
+                               max_splits=max_splits)
+    if max_splits == 1:
+        return cpu(op)[0, 0], cpu(lp)[0, 0]
+    ctx, lse = A.lse_merge(op, lp)
+    return cpu(ctx)[0], cpu(lse)[0]
+
+
+@pytest.mark.parametrize("T", [1, 100, 1024, 3000])
+def test_attention_dense_vs_oracle(T):
+    inp = o.make_inputs(T, 0)
+    g = to_gpu(inp)
+    ctx, lse = _attn(A.glm52_cfg(T), g)
+    rc, rl = o.mla_absorbed(inp["q_abs"], inp["c_kv"], inp["k_rot"], None, 1 / 16)
+    assert_ulp(rc, ctx, what="ctx")
+    assert np.abs(lse - rl).max() < 1e-3
+
+
+def test_attention_sparse_list_vs_oracle():
+    T = 4096
+    inp = o.make_inputs(T, 1)
+    g = to_gpu(inp)
+    rng = np.random.default_rng(3)
+    sel = np.sort(rng.choice(T, 2048, replace=False)).astype(np.int32)
+    ctx, lse = _attn(A.glm52_cfg(T), g, sel)
+    rc, rl = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
+    assert_ulp(rc, ctx, what="ctx")
+    assert np.abs(lse - rl).max() < 1e-3
+
+
+def test_split_k_merge_vs_single_cta():
+    T = 4096
+    inp = o.make_inputs(T, 1)
+    g = to_gpu(inp)
+    sel = np.arange(0, T, 2, dtype=np.int32)
+    c1, l1 = _attn(A.glm52_cfg(T), g, sel)
+    c16, l16 = _attn(A.glm52_cfg(T), g, sel, split_keys=128, max_splits=16)
+    rc, _ = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
+    assert_ulp(rc, c1, what="single")
+    assert_ulp(rc, c16, what="split")
+    assert np.abs(l1 - l16).max() < 1e-4
+
+
+def test_attention_key_window():
+    """Keys [lo, hi) of a global list, cache row 0 = key lo (the sharded layout)."""
+    T = 3000
+    inp = o.make_inputs(T, 2)
+    lo, hi = 1000, 2200
+    g = to_gpu(dict(inp, c_kv=inp["c_kv"][lo:hi], k_rot=inp["k_rot"][lo:hi]))
+    sel = np.arange(0, T, 3, dtype=np.int32)
+    selt = torch.from_numpy(sel).cuda()[None]
+    op, lp = A.mla_sparse_attn(A.glm52_cfg(T), g["kv"], g["q_abs"], _lib.Rows(1, 1, T, 0), sel=selt,
+                               sel_n=sel.shape[0], win=(lo, hi))
+    mine = sel[(sel >= lo) & (sel < hi)]
+    rc, rl = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], mine, 1 / 16)
+    assert_ulp(rc, cpu(op)[0, 0])
+    assert np.abs(cpu(lp)[0, 0] - rl).max() < 1e-3
+
+
+# ---- the substep (wl_attn_decode) ----------------------------------------------------------
+
+def _decode(cfg, g, **kw):
+    return A.attn_decode(cfg, g["kv"], g["q_abs"], keys=g["keys"], q_idx=g["q_idx"], w_idx=g["w_idx"], **kw)
+
+
+def test_config0_sparse_equals_dense_bit_identical():
+    """T = 1024 <= index_topk: the owner's selection is every key and the sparse
+    path must be bit-identical to the dense one (plan:337-340)."""
+    T = 1024
+    inp = o.make_inputs(T, 0)
+    g = to_gpu(inp)
+    cfg = A.glm52_cfg(T)
+    own = _decode(cfg, g)
+    den = _decode(cfg, g, mode=_lib.WL_MODE_DENSE)
+    assert cpu(own["sel"])[0].tolist() == list(range(T))
+    assert torch.equal(own["ctx"], den["ctx"]) and torch.equal(own["lse"], den["lse"])
+    # shuffled full list through a consumer (normalised) is bit-identical too
+    perm = np.random.default_rng(0).permutation(T).astype(np.int32)
+    con = _decode(cfg, g, mode=_lib.WL_MODE_CONSUMER, sel_in=torch.from_numpy(perm).cuda()[None])
+    assert torch.equal(con["ctx"], den["ctx"])
+    rc, _ = o.mla_absorbed(inp["q_abs"], inp["c_kv"], inp["k_rot"], None, 1 / 16)
+    assert_ulp(rc, cpu(den["ctx"])[0])
+
+
+def test_config0_negative_controls():
+    T = 1024
+    inp = o.make_inputs(T, 0)
+    g = to_gpu(inp)
+    cfg = A.glm52_cfg(T)
+    den = _decode(cfg, g, mode=_lib.WL_MODE_DENSE)
+    minus = np.array([i for i in range(T) if i != 5], np.int32)
+    drop = _decode(cfg, g, mode=_lib.WL_MODE_CONSUMER, sel_in=torch.from_numpy(minus).cuda()[None],
+                   canonical=True)
+    assert not torch.equal(drop["ctx"], den["ctx"]), "dropping one key must change the output"
+    # non-causal and negative entries unmask nothing and write nothing
+    nc = np.concatenate([np.arange(T - 1), [T + 3, -1]]).astype(np.int32)
+    a = _decode(cfg, g, mode=_lib.WL_MODE_CONSUMER, sel_in=torch.from_numpy(nc).cuda()[None])
+    b = _decode(cfg, g, mode=_lib.WL_MODE_CONSUMER,
+                sel_in=torch.from_numpy(np.arange(T - 1, dtype=np.int32)).cuda()[None], canonical=True)
+    assert torch.equal(a["ctx"], b["ctx"])
+
+
+@pytest.mark.parametrize("T,config", [(4096, 1), (32768, 2)])
+def test_decode_owner_and_consumer(T, config):
+    inp = o.make_inputs(T, config)
+    g = to_gpu(inp)
+    cfg = A.glm52_cfg(T)
+    idx_out = torch.empty(1, T, dtype=torch.float32, device="cuda")
+    own = _decode(cfg, g, index_out=idx_out)
+    ref_index = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+    gi = cpu(idx_out)[0]
+    assert np.abs(gi - ref_index).max() <= IDX_TOL * np.abs(ref_index).max()
+    sel = cpu(own["sel"])[0]
+    assert int(cpu(own["sel_n"])[0]) == 2048
+    canonical_ok(sel, 2048, T)
+    assert_sel_close(sel, ref_index, 2048, IDX_TOL * np.abs(ref_index).max())
+    assert np.array_equal(sel, np.sort(o.indexer_topk(gi, 2048)))  # exact on its own scores
+    # arithmetic gate: the oracle over the GPU's selection
+    rc, rl = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
+    assert_ulp(rc, cpu(own["ctx"])[0], what="owner ctx")
+    assert np.abs(cpu(own["lse"])[0] - rl).max() < 1e-3
+    # end-to-end gate: the oracle's own selection
+    full = o.decode_step(inp, 2048)
+    assert_ulp(full["ctx"], cpu(own["ctx"])[0], what="owner ctx vs oracle selection")
+    # a consuming layer (its own latent cache) reusing the owner's selection
+    inp2 = o.make_inputs(T, config, seq=1)
+    g2 = to_gpu(inp2)
+    con = A.attn_decode(cfg, g2["kv"], g2["q_abs"], mode=_lib.WL_MODE_CONSUMER, sel_in=own["sel"],
+                        sel_n_in=own["sel_n"], canonical=True)
+    rc2, _ = o.mla_sparse(inp2["q_abs"], inp2["c_kv"], inp2["k_rot"], sel, 1 / 16)
+    assert_ulp(rc2, cpu(con["ctx"])[0], what="consumer ctx")
+
+
+def test_batched_decode_eight_sequences():
+    T = 8192
+    inps = [o.make_inputs(T, 4, seq=s) for s in range(8)]
+    g = stack_inputs(inps)
+    out = _decode(A.glm52_cfg(T), g)
+    for s, inp in enumerate(inps):
+        sel = cpu(out["sel"])[s]
+        canonical_ok(sel, 2048, T)
+        rc, _ = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
+        assert_ulp(rc, cpu(out["ctx"])[s], what=f"seq {s}")
+        ref_index = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+        assert_sel_close(sel, ref_index, 2048, IDX_TOL * np.abs(ref_index).max())
+
+
+def test_layer_group_index_share():
+    """Owner layer publishes; three shared layers reuse the selection unchanged;
+    a shared layer before any owner raises (glm_layer_runner.cuh:485-517)."""
+    T = 4096
+    cfg = A.glm52_cfg(T)
+    share = A.IndexShare()
+    g0 = to_gpu(o.make_inputs(T, 1))
+    with pytest.raises(RuntimeError, match="no published indices"):
+        A.run_attention(cfg, 1, False, share, g0["kv"], g0["q_abs"])
+    out0 = A.run_attention(cfg, 0, True, share, g0["kv"], g0["q_abs"], g0["keys"], g0["q_idx"], g0["w_idx"])
+    assert share.producer == 0
+    sel = cpu(out0["sel_out"])[0]
+    for layer in (1, 2, 3):
+        inp = o.make_inputs(T, 1, seq=layer)
+        g = to_gpu(inp)
+        out = A.run_attention(cfg, layer, False, share, g["kv"], g["q_abs"])
+        assert share.producer == 0
+        rc, _ = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
+        assert_ulp(rc, cpu(out["ctx"])[0], what=f"layer {layer}")
+    dense = A.IndexShare(dense=True)
+    out = A.run_attention(cfg, 7, False, dense, g0["kv"], g0["q_abs"])
+    rc, _ = o.mla_absorbed(o.make_inputs(T, 1)["q_abs"], o.make_inputs(T, 1)["c_kv"],
+                           o.make_inputs(T, 1)["k_rot"], None, 1 / 16)
+    assert_ulp(rc, cpu(out["ctx"])[0], what="dense mode")
+
+
+# ---- chunked prefill -------------------------------------------------------------------------
+
+def _prefill_inputs(pos0, n_q, config):
+    inp = o.make_inputs(pos0 + n_q, config, n_q=n_q)
+    g = to_gpu(dict(inp, q_abs=inp["q_abs"][:, None], q_idx=inp["q_idx"][:, None], w_idx=inp["w_idx"][:, None]))
+    g["q_abs"], g["q_idx"], g["w_idx"] = (dev(inp["q_abs"], torch.bfloat16), dev(inp["q_idx"], torch.bfloat16),
+                                          dev(inp["w_idx"], torch.float32))
+    return inp, g
+
+
+@pytest.mark.parametrize("pos0,n_q,k", [(192, 64, 128), (0, 40, 16), (300, 17, 2048)])
+def test_prefill_rows_vs_oracle(pos0, n_q, k):
+    inp, g = _prefill_inputs(pos0, n_q, 3)
+    T = pos0 + n_q
+    cfg = A.glm52_cfg(T, index_topk=k)
+    idx_out = torch.empty(n_q, T, dtype=torch.float32, device="cuda")
+    out = A.attn_prefill(cfg, g["kv"], g["q_abs"], pos0, keys=g["keys"], q_idx=g["q_idx"], w_idx=g["w_idx"],
+                         index_out=idx_out)
+    K = o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"])
+    sel_all, n_all, ctx_all = cpu(out["sel"]), cpu(out["sel_n"]), cpu(out["ctx"])
+    gidx = cpu(idx_out)
+    for i in range(n_q):
+        L = pos0 + i + 1
+        ref_index = o.indexer_scores(inp["q_idx"][i], K[:L], inp["w_idx"][i])
+        assert np.abs(gidx[i, :L] - ref_index).max() <= IDX_TOL * np.abs(ref_index).max()
+        n = int(n_all[i])
+        assert n == min(k, L)
+        sel = sel_all[i, :n]
+        canonical_ok(sel, n, L)
+        assert_sel_close(sel, ref_index, k, IDX_TOL * np.abs(ref_index).max())
+        rc, _ = o.mla_sparse(inp["q_abs"][i], inp["c_kv"][:L], inp["k_rot"][:L], sel, 1 / 16)
+        assert_ulp(rc, ctx_all[i], what=f"row {i}")
+
+
+def test_prefill_config3_full_size_properties():
+    """BASELINE config 3 (4096 rows on a 4096-token prefix, top-2048) at full
+    size: counts, causality, canonical lists; spot rows against the oracle."""
+    pos0, n_q = 4096, 4096
+    inp, g = _prefill_inputs(pos0, n_q, 3)
+    T = pos0 + n_q
+    cfg = A.glm52_cfg(T)
+    out = A.attn_prefill(cfg, g["kv"], g["q_abs"], pos0, keys=g["keys"], q_idx=g["q_idx"], w_idx=g["w_idx"])
+    n = cpu(out["sel_n"])
+    assert np.all(n == 2048)
+    sel = cpu(out["sel"])
+    assert np.all(np.diff(sel, axis=1) > 0)
+    assert np.all(sel.max(1) <= pos0 + np.arange(n_q)) and sel.min() >= 0
+    assert np.isfinite(cpu(out["ctx"])).all()
+    K = o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"])
+    for i in (0, 1, 777, 2048, 4095):
+        L = pos0 + i + 1
+        ref_index = o.indexer_scores(inp["q_idx"][i], K[:L], inp["w_idx"][i])
+        assert_sel_close(sel[i], ref_index, 2048, IDX_TOL * np.abs(ref_index).max())
+        rc, _ = o.mla_sparse(inp["q_abs"][i], inp["c_kv"][:L], inp["k_rot"][:L], sel[i], 1 / 16)
+        assert_ulp(rc, cpu(out["ctx"])[i], what=f"row {i}")
+
+
+def test_prefill_consumer_and_dense():
+    pos0, n_q = 100, 50
+    inp, g = _prefill_inputs(pos0, n_q, 3)
+    T = pos0 + n_q
+    cfg = A.glm52_cfg(T, index_topk=64)
+    own = A.attn_prefill(cfg, g["kv"], g["q_abs"], pos0, keys=g["keys"], q_idx=g["q_idx"], w_idx=g["w_idx"])
+    con = A.attn_prefill(cfg, g["kv"], g["q_abs"], pos0, mode=_lib.WL_MODE_CONSUMER, sel_in=own["sel"],
+                         sel_n_in=own["sel_n"], canonical=True)
+    assert torch.equal(own["ctx"], con["ctx"])
+    den = A.attn_prefill(A.glm52_cfg(T, index_topk=4096), g["kv"], g["q_abs"], pos0, mode=_lib.WL_MODE_DENSE)
+    big = A.attn_prefill(A.glm52_cfg(T, index_topk=4096), g["kv"], g["q_abs"], pos0, keys=g["keys"],
+                         q_idx=g["q_idx"], w_idx=g["w_idx"])
+    assert torch.equal(den["ctx"], big["ctx"]), "k >= T: sparse prefill must equal dense bit for bit"

@@ -1,0 +1,403 @@
+"""Python host interface of the attention substep, shaped like the reference.
+
+The reference's interface for this path is ``run_attention`` with an
+``IndexShare`` (src/glm_layer_runner.cuh:485-527) and, on the numpy side,
+``indexer_scores`` / ``indexer_topk`` / ``index_drop_mask`` / ``IndexShare``
+(tools/ref_glm_chain.py:445-529). This module keeps those names, argument
+meanings and error behaviour (a shared layer with nothing published raises
+``RuntimeError``) and runs every piece through the C ABI of ``libwl_attn.so``.
+PyTorch only supplies device memory and the current CUDA stream.
+
+All tensors are CUDA tensors: bf16 latent cache / queries, uint8 (fp8-e4m3
+bit patterns) index keys, fp32 scales, weights and outputs, int32 selections.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import (AttnCfg, DecodeIO, IndexCache, IndexShareC, LatentCache, PrefillIO, Rows,
+                   Shard, check, lib)
+
+N_HEADS, KV_LORA, ROPE, IDX_H, IDX_D, INDEX_TOPK = 64, 512, 64, 32, 128, 2048
+D_QK = KV_LORA + ROPE
+
+
+def glm52_cfg(T_max: int, index_topk: int = INDEX_TOPK) -> AttnCfg:
+    cfg = AttnCfg()
+    lib().wl_attn_cfg_glm52(C.byref(cfg), int(T_max))
+    cfg.index_topk = int(index_topk)
+    return cfg
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+_ws: dict[int, torch.Tensor] = {}
+
+
+def workspace(nbytes: int, device: torch.device | None = None) -> torch.Tensor:
+    """A per-device caller-owned scratch buffer of at least ``nbytes``."""
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index
+    buf = _ws.get(dev)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=f"cuda:{dev}")
+        _ws[dev] = buf
+    return buf
+
+
+@dataclass
+class LatentKV:
+    """One layer's latent cache: c_kv [S, T, 512] and k_rot [S, T, 64] bf16
+    views (S sequences). ``packed(kv)`` splits a [S, T, 576] tensor."""
+    c_kv: torch.Tensor
+    k_rot: torch.Tensor
+
+    @staticmethod
+    def packed(kv: torch.Tensor) -> "LatentKV":
+        if kv.dim() == 2:
+            kv = kv.unsqueeze(0)
+        return LatentKV(kv[..., :KV_LORA], kv[..., KV_LORA:])
+
+    def c(self) -> LatentCache:
+        ckv, krt = self.c_kv, self.k_rot
+        if ckv.dim() == 2:
+            ckv, krt = ckv.unsqueeze(0), krt.unsqueeze(0)
+        _need(ckv, torch.bfloat16, "c_kv")
+        _need(krt, torch.bfloat16, "k_rot")
+        if ckv.stride(-1) != 1 or krt.stride(-1) != 1:
+            raise ValueError("latent rows must be contiguous")
+        return LatentCache(ckv.data_ptr(), ckv.stride(-2), ckv.stride(0), krt.data_ptr(),
+                           krt.stride(-2), krt.stride(0))
+
+    @property
+    def T(self) -> int:
+        return self.c_kv.shape[-2]
+
+
+@dataclass
+class IndexKeys:
+    """An owning layer's indexer key cache: keys [S, T, 128] uint8 (e4m3 bits),
+    scale [S, T] fp32."""
+    keys: torch.Tensor
+    scale: torch.Tensor
+
+    def c(self) -> IndexCache:
+        k, s = self.keys, self.scale
+        if k.dim() == 2:
+            k, s = k.unsqueeze(0), s.unsqueeze(0)
+        _need(k, torch.uint8, "index keys")
+        _need(s, torch.float32, "index scale")
+        if k.stride(-1) != 1 or k.stride(-2) != IDX_D or s.stride(-1) != 1:
+            raise ValueError("index keys must be packed [T, 128] rows with contiguous scales")
+        return IndexCache(k.data_ptr(), k.stride(0), s.data_ptr(), s.stride(0))
+
+
+# ---- the individual kernels ------------------------------------------------------------
+
+def indexer_scores(cfg: AttnCfg, keys: IndexKeys, q_idx: torch.Tensor, w_idx: torch.Tensor,
+                   T: int, rows: Rows, out: torch.Tensor | None = None) -> torch.Tensor:
+    """index[r, t] for t < len(r) (fp32 [n_rows, T]); entries past len(r) are unspecified."""
+    _need(q_idx, torch.bfloat16, "q_idx")
+    _need(w_idx, torch.float32, "w_idx")
+    if out is None:
+        out = torch.empty(rows.n_rows, T, dtype=torch.float32, device=q_idx.device)
+    check(lib().wl_indexer_scores(C.byref(cfg), C.byref(keys.c()), T, C.byref(rows),
+                                  _ptr(q_idx.contiguous()), _ptr(w_idx.contiguous()), _ptr(out),
+                                  out.stride(0), _stream()), "wl_indexer_scores")
+    return out
+
+
+def indexer_topk(index: torch.Tensor, k: int, rows: Rows | None = None, T: int | None = None,
+                 cand_idx: torch.Tensor | None = None):
+    """Exact top-min(k, len) per row, canonical (ascending). Returns (sel, n)."""
+    _need(index, torch.float32, "index")
+    T = index.shape[1] if T is None else T
+    rows = rows or Rows(index.shape[0], 1, T, 0)
+    kk = min(k, T)
+    sel = torch.full((rows.n_rows, kk), -1, dtype=torch.int32, device=index.device)
+    n = torch.empty(rows.n_rows, dtype=torch.int32, device=index.device)
+    check(lib().wl_indexer_topk(_ptr(index), index.stride(0), C.byref(rows), T, k, _ptr(cand_idx),
+                                _ptr(sel), kk, _ptr(n), _stream()), "wl_indexer_topk")
+    return sel, n
+
+
+def sel_normalize(sel_in: torch.Tensor, T: int, n_in: torch.Tensor | None = None,
+                  rows: Rows | None = None):
+    """Canonical list of the keys an arbitrary list keeps (the mask semantics)."""
+    _need(sel_in, torch.int32, "sel_in")
+    rows = rows or Rows(sel_in.shape[0], 1, T, 0)
+    out = torch.full((rows.n_rows, T), -1, dtype=torch.int32, device=sel_in.device)
+    n = torch.empty(rows.n_rows, dtype=torch.int32, device=sel_in.device)
+    check(lib().wl_sel_normalize(_ptr(sel_in), sel_in.stride(0), _ptr(n_in), sel_in.shape[1],
+                                 C.byref(rows), T, _ptr(out), out.stride(0), _ptr(n), _stream()),
+          "wl_sel_normalize")
+    return out, n
+
+
+def mla_sparse_attn(cfg: AttnCfg, kv: LatentKV, q_abs: torch.Tensor, rows: Rows,
+                    sel: torch.Tensor | None = None, sel_n: torch.Tensor | int | None = None,
+                    win: tuple[int, int] | None = None, split_keys: int = 0,
+                    max_splits: int = 1):
+    """Partials (o [n_rows, max_splits, 64, 512], lse [n_rows, max_splits, 64])."""
+    _need(q_abs, torch.bfloat16, "q_abs")
+    T = kv.T
+    lo, hi = win if win is not None else (0, T)
+    o = torch.empty(rows.n_rows, max_splits, N_HEADS, KV_LORA, dtype=torch.float32, device=q_abs.device)
+    lse = torch.empty(rows.n_rows, max_splits, N_HEADS, dtype=torch.float32, device=q_abs.device)
+    n_dev = sel_n if isinstance(sel_n, torch.Tensor) else None
+    n_host = int(sel_n) if isinstance(sel_n, int) else (sel.shape[1] if sel is not None else 0)
+    check(lib().wl_mla_sparse_attn(C.byref(cfg), C.byref(kv.c()), T, C.byref(rows),
+                                   _ptr(q_abs.contiguous()), _ptr(sel),
+                                   sel.stride(0) if sel is not None else 0, _ptr(n_dev), n_host,
+                                   lo, hi, split_keys, _ptr(o), _ptr(lse), max_splits, _stream()),
+          "wl_mla_sparse_attn")
+    return o, lse
+
+
+def lse_merge(o_part: torch.Tensor, lse_part: torch.Tensor):
+    """Merge [R, S, H, D] partials into (ctx [R, H, D], lse [R, H])."""
+    R, S, H, D = o_part.shape
+    ctx = torch.empty(R, H, D, dtype=torch.float32, device=o_part.device)
+    lse = torch.empty(R, H, dtype=torch.float32, device=o_part.device)
+    check(lib().wl_lse_merge(_ptr(o_part), _ptr(lse_part), R, S, S * H * D, H * D, S * H, H, H, D,
+                             _ptr(ctx), _ptr(lse), _stream()), "wl_lse_merge")
+    return ctx, lse
+
+
+# ---- the substep ----------------------------------------------------------------------------
+
+def decode_io(cfg: AttnCfg, kv: LatentKV, q_abs: torch.Tensor, *, keys: IndexKeys | None = None,
+              q_idx: torch.Tensor | None = None, w_idx: torch.Tensor | None = None,
+              mode: int = _lib.WL_MODE_OWNER, sel_in: torch.Tensor | None = None,
+              sel_n_in: torch.Tensor | None = None, sel_n: int | None = None,
+              canonical: bool = False, sel_out: torch.Tensor | None = None,
+              sel_n_out: torch.Tensor | None = None, index_out: torch.Tensor | None = None,
+              ctx: torch.Tensor | None = None, lse: torch.Tensor | None = None) -> tuple[DecodeIO, dict]:
+    """Fill a DecodeIO; returns it with the tensors it points to (keep them alive)."""
+    B = q_abs.shape[0]
+    T = kv.T
+    dev = q_abs.device
+    kk = min(cfg.index_topk, T)
+    if ctx is None:
+        ctx = torch.empty(B, N_HEADS, KV_LORA, dtype=torch.float32, device=dev)
+    if lse is None:
+        lse = torch.empty(B, N_HEADS, dtype=torch.float32, device=dev)
+    if mode == _lib.WL_MODE_OWNER:
+        if sel_out is None:
+            sel_out = torch.empty(B, kk, dtype=torch.int32, device=dev)
+        if sel_n_out is None:
+            sel_n_out = torch.empty(B, dtype=torch.int32, device=dev)
+    io = DecodeIO()
+    io.batch, io.T = B, T
+    io.latent = kv.c()
+    if keys is not None:
+        io.index = keys.c()
+    io.q_abs = _ptr(q_abs)
+    io.q_idx = _ptr(q_idx)
+    io.w_idx = _ptr(w_idx)
+    io.mode = mode
+    io.sel_flags = _lib.WL_SEL_CANONICAL if canonical else 0
+    io.sel_out = _ptr(sel_out)
+    io.sel_n_out = _ptr(sel_n_out)
+    io.sel_in = _ptr(sel_in)
+    io.sel_n_in = _ptr(sel_n_in)
+    io.sel_n = int(sel_n if sel_n is not None else (sel_in.shape[1] if sel_in is not None else 0))
+    if sel_out is not None:
+        io.sel_stride = sel_out.stride(0)
+    elif sel_in is not None:
+        io.sel_stride = sel_in.stride(0)
+    io.index_out = _ptr(index_out)
+    io.index_stride = index_out.stride(0) if index_out is not None else 0
+    io.ctx = _ptr(ctx)
+    io.lse = _ptr(lse)
+    keep = dict(ctx=ctx, lse=lse, sel_out=sel_out, sel_n_out=sel_n_out, index_out=index_out,
+                q_abs=q_abs, q_idx=q_idx, w_idx=w_idx, sel_in=sel_in, sel_n_in=sel_n_in, kv=kv,
+                keys=keys)
+    return io, keep
+
+
+def attn_decode(cfg: AttnCfg, kv: LatentKV, q_abs: torch.Tensor, **kw) -> dict:
+    """One decode token per sequence through ``wl_attn_decode``.
+
+    Returns the output tensors: ctx [B,64,512], lse [B,64] and, for an owner,
+    sel [B,k'] (canonical) with counts sel_n [B]."""
+    io, keep = decode_io(cfg, kv, q_abs, **kw)
+    nbytes = lib().wl_attn_workspace_bytes(C.byref(cfg), io.T, io.batch)
+    ws = workspace(nbytes, q_abs.device)
+    check(lib().wl_attn_decode(C.byref(cfg), C.byref(io), _ptr(ws), ws.numel(), _stream()),
+          "wl_attn_decode")
+    return keep
+
+
+class IndexShare:
+    """``prev_topk_indices`` threaded through the layer loop
+    (glm_layer_runner.cuh:485-517; tools/ref_glm_chain.py:445-462).
+
+    Owners publish their raw selection; shared layers read it unchanged (no
+    consume-and-clear); a shared layer with nothing published raises
+    ``RuntimeError``. ``dense`` is the standalone-layer test mode."""
+
+    def __init__(self, dense: bool = False):
+        self.c = IndexShareC()
+        self.c.dense = int(dense)
+        lib().wl_index_share_reset(C.byref(self.c))
+        self._keep: tuple = ()
+
+    def reset(self) -> None:
+        lib().wl_index_share_reset(C.byref(self.c))
+        self._keep = ()
+
+    @property
+    def producer(self) -> int | None:
+        p = self.c.producer
+        return None if p == 0xFFFFFFFF else p
+
+    @property
+    def dense(self) -> bool:
+        return bool(self.c.dense)
+
+    def publish(self, layer: int, idx: torch.Tensor, n: torch.Tensor) -> None:
+        lib().wl_index_share_publish(C.byref(self.c), layer, _ptr(idx), _ptr(n), idx.stride(0),
+                                     idx.shape[1])
+        self._keep = (idx, n)
+
+    @property
+    def indices(self):
+        return self._keep[0] if self._keep else None
+
+    def require(self, layer: int) -> None:
+        st = lib().wl_index_share_require(C.byref(self.c), layer)
+        if st == _lib.WL_ERR_NO_INDICES:
+            raise RuntimeError(
+                f'layer {layer} is "shared" and has no published indices; its group leader '
+                "must run first (IndexShare is empty)")
+        check(st, "IndexShare.require")
+
+
+def run_attention(cfg: AttnCfg, layer: int, owner: bool, share: IndexShare, kv: LatentKV,
+                  q_abs: torch.Tensor, keys: IndexKeys | None = None,
+                  q_idx: torch.Tensor | None = None, w_idx: torch.Tensor | None = None) -> dict:
+    """The hot block of run_attention (glm_layer_runner.cuh:582-644) for one
+    decode token per sequence, through ``wl_attn_layer_decode``."""
+    B, T = q_abs.shape[0], kv.T
+    kk = min(cfg.index_topk, T)
+    dev = q_abs.device
+    sel_out = sel_n_out = None
+    if owner:
+        sel_out = torch.empty(B, kk, dtype=torch.int32, device=dev)
+        sel_n_out = torch.empty(B, dtype=torch.int32, device=dev)
+    io, keep = decode_io(cfg, kv, q_abs, keys=keys, q_idx=q_idx, w_idx=w_idx,
+                         mode=_lib.WL_MODE_OWNER if owner else _lib.WL_MODE_CONSUMER,
+                         sel_out=sel_out, sel_n_out=sel_n_out)
+    nbytes = lib().wl_attn_workspace_bytes(C.byref(cfg), T, B)
+    ws = workspace(nbytes, dev)
+    st = lib().wl_attn_layer_decode(C.byref(cfg), C.byref(io), int(owner), layer, C.byref(share.c),
+                                    _ptr(ws), ws.numel(), _stream())
+    if st == _lib.WL_ERR_NO_INDICES:
+        share.require(layer)  # raises with the reference's message
+    check(st, "wl_attn_layer_decode")
+    if owner:
+        share._keep = (sel_out, sel_n_out)
+    return keep
+
+
+def attn_prefill(cfg: AttnCfg, kv: LatentKV, q_abs: torch.Tensor, pos0: int, *,
+                 keys: IndexKeys | None = None, q_idx: torch.Tensor | None = None,
+                 w_idx: torch.Tensor | None = None, mode: int = _lib.WL_MODE_OWNER,
+                 sel_in: torch.Tensor | None = None, sel_n_in: torch.Tensor | None = None,
+                 canonical: bool = False, index_out: torch.Tensor | None = None) -> dict:
+    """Chunked prefill of n_q rows after a pos0-token prefix (row i causal over
+    keys [0, pos0+i]) through ``wl_attn_prefill``."""
+    n_q = q_abs.shape[0]
+    T = pos0 + n_q
+    dev = q_abs.device
+    kk = min(cfg.index_topk, T)
+    ctx = torch.empty(n_q, N_HEADS, KV_LORA, dtype=torch.float32, device=dev)
+    lse = torch.empty(n_q, N_HEADS, dtype=torch.float32, device=dev)
+    sel_out = sel_n_out = None
+    if mode == _lib.WL_MODE_OWNER:
+        sel_out = torch.full((n_q, kk), -1, dtype=torch.int32, device=dev)
+        sel_n_out = torch.empty(n_q, dtype=torch.int32, device=dev)
+    io = PrefillIO()
+    io.n_q, io.pos0 = n_q, pos0
+    io.latent = kv.c()
+    if keys is not None:
+        io.index = keys.c()
+    io.q_abs, io.q_idx, io.w_idx = _ptr(q_abs), _ptr(q_idx), _ptr(w_idx)
+    io.mode = mode
+    io.sel_flags = _lib.WL_SEL_CANONICAL if canonical else 0
+    io.sel_out, io.sel_n_out = _ptr(sel_out), _ptr(sel_n_out)
+    io.sel_in, io.sel_n_in = _ptr(sel_in), _ptr(sel_n_in)
+    io.sel_stride = sel_out.stride(0) if sel_out is not None else (sel_in.stride(0) if sel_in is not None else 0)
+    io.index_out = _ptr(index_out)
+    io.index_stride = index_out.stride(0) if index_out is not None else 0
+    io.ctx, io.lse = _ptr(ctx), _ptr(lse)
+    nbytes = lib().wl_attn_prefill_workspace_bytes(C.byref(cfg), n_q, T)
+    ws = workspace(nbytes, dev)
+    check(lib().wl_attn_prefill(C.byref(cfg), C.byref(io), _ptr(ws), ws.numel(), _stream()),
+          "wl_attn_prefill")
+    return dict(ctx=ctx, lse=lse, sel=sel_out, sel_n=sel_n_out)
+
+
+def device_error(clear: bool = True) -> tuple[int, int]:
+    """(status, raw word) of the library's device-side error word."""
+    w = C.c_uint32(0)
+    st = lib().wl_device_error(int(clear), C.byref(w))
+    return st, w.value
+
+
+# ---- KV-sequence sharding ---------------------------------------------------------------------
+
+class Comm:
+    """NCCL communicator of the library, bootstrapped through torch.distributed."""
+
+    def __init__(self, rank: int, world: int, group=None):
+        import torch.distributed as dist
+        uid = (C.c_uint8 * 128)()
+        if rank == 0:
+            check(lib().wl_comm_unique_id(uid), "wl_comm_unique_id")
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        uid = (C.c_uint8 * 128).from_buffer_copy(obj[0])
+        h = C.c_void_p()
+        check(lib().wl_comm_create(uid, world, rank, C.byref(h)), "wl_comm_create")
+        self.h, self.rank, self.world = h, rank, world
+
+    def close(self) -> None:
+        if self.h:
+            lib().wl_comm_destroy(self.h)
+            self.h = None
+
+
+def attn_decode_sharded(cfg: AttnCfg, comm: Comm, t0: int, T_global: int, kv: LatentKV,
+                        q_abs: torch.Tensor, **kw) -> dict:
+    """Decode with this rank holding keys [t0, t0 + kv.T) of every cache."""
+    B = q_abs.shape[0]
+    dev = q_abs.device
+    kg = min(cfg.index_topk, T_global)
+    if kw.get("mode", _lib.WL_MODE_OWNER) == _lib.WL_MODE_OWNER:
+        kw.setdefault("sel_out", torch.full((B, kg), -1, dtype=torch.int32, device=dev))
+        kw.setdefault("sel_n_out", torch.empty(B, dtype=torch.int32, device=dev))
+    io, keep = decode_io(cfg, kv, q_abs, **kw)
+    shard = Shard(t0, T_global)
+    nbytes = lib().wl_attn_sharded_workspace_bytes(C.byref(cfg), kv.T, B, comm.world)
+    ws = workspace(nbytes, dev)
+    check(lib().wl_attn_decode_sharded(C.byref(cfg), C.byref(io), C.byref(shard), comm.h, _ptr(ws),
+                                       ws.numel(), _stream()), "wl_attn_decode_sharded")
+    return keep

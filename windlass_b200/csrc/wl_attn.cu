@@ -1,0 +1,829 @@
+// wl_attn.cu — host side of the C ABI declared in include/wl_attn.h, plus the
+// single translation unit that holds every kernel of the library (so the
+// device error word is one symbol).
+//
+// The orchestration mirrors the hot block of the reference's run_attention
+// (src/glm_layer_runner.cuh:582-644):
+//   owner    -> indexer scores -> top-k -> (publish) -> sparse attention
+//   consumer -> (require) -> [normalise list] -> sparse attention
+//   dense    -> attention over every key
+// followed by the split-K (o, lse) merge. All launches go on the caller's
+// stream; nothing allocates; every failure is a status code.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <nccl.h>
+
+#include "../../include/wl_attn.h"
+#include "indexer.cuh"
+#include "mla_attn.cuh"
+#include "topk.cuh"
+
+namespace {
+
+using wl::AttnLayout;
+constexpr int kMaxSplits = 16;   // split-K CTAs per decode row
+constexpr int kMaxDevices = 64;
+
+#define WL_CUDA_TRY(expr)                                           \
+    do {                                                            \
+        cudaError_t e_ = (expr);                                    \
+        if (e_ != cudaSuccess) {                                    \
+            std::fprintf(stderr, "wl_attn: %s failed: %s\n", #expr, \
+                         cudaGetErrorString(e_));                   \
+            return WL_ERR_CUDA;                                     \
+        }                                                           \
+    } while (0)
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
+
+bool cfg_supported(const wl_attn_cfg* c) {
+    return c && c->n_heads == wl::AT_H && c->kv_lora == wl::AT_DV && c->rope_dim == wl::AT_D - wl::AT_DV &&
+           c->idx_heads == wl::IDX_H && c->idx_dim == wl::IDX_D && c->index_topk > 0 && c->T_max > 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Per-device one-time kernel attributes (dynamic shared memory opt-in).
+std::mutex g_attr_mu;
+bool g_attr_done[kMaxDevices];
+
+int ensure_attrs() {
+    int dev = 0;
+    WL_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return WL_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    if (g_attr_done[dev]) return WL_OK;
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_scores_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::IdxLayout<1>::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_scores_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::IdxLayout<8>::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     AttnLayout::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::sel_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024));
+    g_attr_done[dev] = true;
+    return WL_OK;
+}
+
+int rows_ok(const wl_rows* r, int32_t T) {
+    if (!r || r->n_rows <= 0 || r->rows_per_seq <= 0 || r->len0 < 0 || r->len_step < 0 || T <= 0)
+        return WL_ERR_ARG;
+    return WL_OK;
+}
+
+// Keys per split so that at most kMaxSplits CTAs cover n entries.
+int split_keys_for(long long n) {
+    long long per = ceil_div(n > 0 ? n : 1, kMaxSplits);
+    per = ceil_div(per, wl::AT_TILE) * wl::AT_TILE;
+    return (int)(per < wl::AT_TILE ? wl::AT_TILE : per);
+}
+
+// ---- kernel launchers ----------------------------------------------------------
+int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t T, const wl_rows* rows,
+                   const void* q_idx, const float* w_idx, float* out, int64_t out_stride,
+                   cudaStream_t st) {
+    if (!cache || !cache->keys || !cache->scale || !q_idx || !w_idx || !out) return WL_ERR_ARG;
+    if (!aligned16(cache->keys) || !aligned16(q_idx) || (cache->keys_seq_stride & 15)) return WL_ERR_ARG;
+    if (out_stride < T) return WL_ERR_ARG;
+    wl::IdxParams p{};
+    p.keys = static_cast<const uint8_t*>(cache->keys);
+    p.keys_seq = cache->keys_seq_stride;
+    p.scale = cache->scale;
+    p.scale_seq = cache->scale_seq_stride;
+    p.T = T;
+    p.n_rows = rows->n_rows;
+    p.rows_per_seq = rows->rows_per_seq;
+    p.len0 = rows->len0;
+    p.len_step = rows->len_step;
+    p.q = static_cast<const __nv_bfloat16*>(q_idx);
+    p.w = w_idx;
+    p.out = out;
+    p.out_stride = out_stride;
+    p.qk_scale = cfg->idx_qk_scale;
+    const int ntiles = (int)ceil_div(T, wl::IDX_TILE);
+    if (rows->rows_per_seq >= rows->n_rows && rows->n_rows >= 8) {
+        // Many rows over one shared cache (prefill): 8 rows (N = 256) per MMA.
+        const int n_groups = (int)ceil_div(rows->n_rows, 8);
+        const int want_y = (int)ceil_div(4 * 148, ntiles);
+        const int gpc = (int)ceil_div(n_groups, want_y < 1 ? 1 : want_y);
+        p.groups_per_cta = gpc;
+        dim3 grid(ntiles, (unsigned)ceil_div(n_groups, gpc));
+        wl::indexer_scores_kernel<8><<<grid, 128, wl::IdxLayout<8>::BYTES, st>>>(p);
+    } else {
+        // One row per group; rows of different sequences never share a CTA.
+        p.groups_per_cta = 1;
+        if (rows->n_rows > 65535) return WL_ERR_ARG;
+        dim3 grid(ntiles, rows->n_rows);
+        wl::indexer_scores_kernel<1><<<grid, 128, wl::IdxLayout<1>::BYTES, st>>>(p);
+    }
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+}
+
+int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, int32_t T, int32_t k,
+                const int32_t* cand_idx, int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
+                cudaStream_t st) {
+    if (!index || !sel_out || k <= 0) return WL_ERR_ARG;
+    if (sel_stride < (k < T ? k : T)) return WL_ERR_ARG;
+    wl::TopkParams p{};
+    p.in = index;
+    p.in_stride = index_stride;
+    p.n_rows = rows->n_rows;
+    p.rows_per_seq = rows->rows_per_seq;
+    p.len0 = rows->len0;
+    p.len_step = rows->len_step;
+    p.T = T;
+    p.k = k;
+    p.cand_idx = cand_idx;
+    p.out = sel_out;
+    p.out_stride = sel_stride;
+    p.n_out = sel_n_out;
+    wl::topk_kernel<<<rows->n_rows, wl::TOPK_THREADS, 0, st>>>(p);
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+}
+
+int launch_normalize(const int32_t* in, int64_t in_stride, const int32_t* n_in_dev, int32_t n_in,
+                     const wl_rows* rows, int32_t T, int32_t* out, int64_t out_stride, int32_t* n_out,
+                     cudaStream_t st) {
+    if (!in || !out) return WL_ERR_ARG;
+    const size_t smem = (size_t)ceil_div(T, 32) * 4;
+    if (smem > 200 * 1024) return WL_ERR_UNSUPPORTED;
+    wl::NormParams p{};
+    p.in = in;
+    p.in_stride = in_stride;
+    p.n_in_dev = n_in_dev;
+    p.n_in = n_in;
+    p.n_rows = rows->n_rows;
+    p.rows_per_seq = rows->rows_per_seq;
+    p.len0 = rows->len0;
+    p.len_step = rows->len_step;
+    p.T = T;
+    p.out = out;
+    p.out_stride = out_stride;
+    p.n_out = n_out;
+    wl::sel_normalize_kernel<<<rows->n_rows, wl::TOPK_THREADS, smem, st>>>(p);
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+}
+
+int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int64_t len_T,
+                const wl_rows* rows, const void* q_abs, const int32_t* sel, int64_t sel_stride,
+                const int32_t* sel_n_dev, int32_t sel_n, int64_t win_lo, int64_t win_hi, int32_t split_keys,
+                float* o_part, float* lse_part, int32_t max_splits, cudaStream_t st) {
+    if (!c || !c->c_kv || !c->k_rot || !q_abs || !o_part || !lse_part) return WL_ERR_ARG;
+    if (!aligned16(c->c_kv) || !aligned16(c->k_rot) || !aligned16(q_abs)) return WL_ERR_ARG;
+    if ((c->c_kv_row_stride & 7) || (c->k_rot_row_stride & 7) || (c->c_kv_seq_stride & 7) ||
+        (c->k_rot_seq_stride & 7))
+        return WL_ERR_ARG;
+    if (split_keys < 0 || (split_keys % wl::AT_TILE) || max_splits <= 0) return WL_ERR_ARG;
+    if (split_keys == 0 && max_splits != 1) return WL_ERR_ARG;
+    if (rows->n_rows > 65535 || max_splits > 65535) return WL_ERR_ARG;
+    wl::AttnParams p{};
+    p.c_kv = static_cast<const __nv_bfloat16*>(c->c_kv);
+    p.ckv_row = c->c_kv_row_stride;
+    p.ckv_seq = c->c_kv_seq_stride;
+    p.k_rot = static_cast<const __nv_bfloat16*>(c->k_rot);
+    p.krot_row = c->k_rot_row_stride;
+    p.krot_seq = c->k_rot_seq_stride;
+    p.T = T;
+    p.n_rows = rows->n_rows;
+    p.rows_per_seq = rows->rows_per_seq;
+    p.len0 = rows->len0;
+    p.len_step = rows->len_step;
+    p.len_T = (int)len_T;
+    p.q_abs = static_cast<const __nv_bfloat16*>(q_abs);
+    p.sel = sel;
+    p.sel_stride = sel_stride;
+    p.sel_n_dev = sel_n_dev;
+    p.sel_n = sel_n;
+    p.win_lo = win_lo;
+    p.win_hi = win_hi;
+    p.split_keys = split_keys;
+    p.max_splits = max_splits;
+    p.o_part = o_part;
+    p.lse_part = lse_part;
+    p.scale_log2 = cfg->softmax_scale * 1.4426950408889634f;
+    dim3 grid(max_splits, rows->n_rows);
+    wl::mla_sparse_attn_kernel<<<grid, 128, AttnLayout::BYTES, st>>>(p);
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+}
+
+int launch_merge(const float* o_part, const float* lse_part, int32_t n_rows, int32_t n_parts, int64_t row_stride,
+                 int64_t part_stride, int64_t lse_row_stride, int64_t lse_part_stride, int32_t n_heads,
+                 int32_t dv, float* ctx, float* lse, cudaStream_t st) {
+    if (!o_part || !lse_part || !ctx || n_rows <= 0 || n_parts <= 0 || (dv & 3) || n_heads <= 0) return WL_ERR_ARG;
+    wl::MergeParams p{o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
+                      lse_part_stride, n_heads, dv, ctx, lse};
+    wl::lse_merge_kernel<<<dim3(n_heads, n_rows), 128, 0, st>>>(p);
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+}
+
+// ---- workspace carving ---------------------------------------------------------------
+struct DecodeWs {
+    float* index;
+    int32_t* sel;
+    int32_t* cnt;
+    float* o_part;
+    float* lse_part;
+    float* lse_tmp;
+    // sharded only
+    float* cand_score;
+    int32_t* cand_idx;
+    float* cand_score_all;
+    int32_t* cand_idx_all;
+    float* cand_score_rows;
+    int32_t* cand_idx_rows;
+    float* part_send;
+    float* part_recv;
+    size_t bytes;
+};
+
+DecodeWs carve_decode(void* base, const wl_attn_cfg* cfg, int32_t T_max, int32_t batch, int32_t nranks) {
+    DecodeWs w{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> void* {
+        void* p = base ? static_cast<char*>(base) + off : nullptr;
+        off += align256(bytes);
+        return p;
+    };
+    const size_t k = (size_t)cfg->index_topk;
+    w.index = static_cast<float*>(take((size_t)batch * T_max * 4));
+    const size_t sel_cap = (size_t)(nranks > 1 ? (size_t)T_max * nranks : (size_t)T_max);
+    w.sel = static_cast<int32_t*>(take((size_t)batch * (sel_cap > k ? sel_cap : k) * 4));
+    w.cnt = static_cast<int32_t*>(take((size_t)batch * 4));
+    w.o_part = static_cast<float*>(take((size_t)batch * kMaxSplits * wl::AT_H * wl::AT_DV * 4));
+    w.lse_part = static_cast<float*>(take((size_t)batch * kMaxSplits * wl::AT_H * 4));
+    w.lse_tmp = static_cast<float*>(take((size_t)batch * wl::AT_H * 4));
+    if (nranks > 1) {
+        w.cand_score = static_cast<float*>(take((size_t)batch * k * 4));
+        w.cand_idx = static_cast<int32_t*>(take((size_t)batch * k * 4));
+        w.cand_score_all = static_cast<float*>(take((size_t)nranks * batch * k * 4));
+        w.cand_idx_all = static_cast<int32_t*>(take((size_t)nranks * batch * k * 4));
+        w.cand_score_rows = static_cast<float*>(take((size_t)nranks * batch * k * 4));
+        w.cand_idx_rows = static_cast<int32_t*>(take((size_t)nranks * batch * k * 4));
+        const size_t part = (size_t)batch * (wl::AT_H * wl::AT_DV + wl::AT_H);
+        w.part_send = static_cast<float*>(take(part * 4));
+        w.part_recv = static_cast<float*>(take((size_t)nranks * part * 4));
+    }
+    w.bytes = off + 256;  // + base alignment slack
+    return w;
+}
+
+void* align_base(void* ws) {
+    return reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+}
+
+int check_decode_io(const wl_attn_cfg* cfg, const wl_attn_decode_io* io) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (!io || io->batch <= 0 || io->T <= 0 || !io->q_abs || !io->ctx) return WL_ERR_ARG;
+    if (io->T > cfg->T_max) return WL_ERR_T_EXCEEDS_MAX;
+    if (io->mode != WL_MODE_OWNER && io->mode != WL_MODE_CONSUMER && io->mode != WL_MODE_DENSE) return WL_ERR_ARG;
+    if (io->mode == WL_MODE_OWNER && (!io->q_idx || !io->w_idx || !io->index.keys || !io->index.scale))
+        return WL_ERR_ARG;
+    if (io->mode == WL_MODE_CONSUMER) {
+        if (!io->sel_in) return WL_ERR_NO_INDICES;
+        if (!io->sel_n_in && io->sel_n < 0) return WL_ERR_ARG;
+        if (io->sel_stride <= 0) return WL_ERR_ARG;
+    }
+    return WL_OK;
+}
+
+// Gather (score, global index) of a rank's local top-k into fixed-size
+// candidate rows; slots past the local count get (-inf, INT32_MAX).
+__global__ void gather_candidates_kernel(const float* index, long long index_stride, const int* sel,
+                                         long long sel_stride, const int* cnt, int k, long long t0,
+                                         float* cs, int* ci) {
+    const int r = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= k) return;
+    const int n = cnt[r];
+    float s = -INFINITY;
+    int g = 0x7fffffff;
+    if (j < n) {
+        const int t = sel[(long long)r * sel_stride + j];
+        s = index[(long long)r * index_stride + t];
+        g = (int)(t0 + t);
+    }
+    cs[(long long)r * k + j] = s;
+    ci[(long long)r * k + j] = g;
+}
+
+__global__ void row_counts_kernel(int n_rows, int len0, int len_step, int T, int k, int* out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n_rows) return;
+    const long long l = (long long)len0 + (long long)r * len_step;
+    const int len = (int)(l < T ? l : T);
+    out[r] = len < k ? len : k;
+}
+
+// [rank][row][k] -> [row][rank*k + j]
+__global__ void candidates_to_rows_kernel(const float* s_all, const int* i_all, int nranks, int batch, int k,
+                                          float* s_rows, int* i_rows) {
+    const long long n = (long long)nranks * batch * k;
+    for (long long x = blockIdx.x * (long long)blockDim.x + threadIdx.x; x < n; x += (long long)gridDim.x * blockDim.x) {
+        const int j = (int)(x % k);
+        const int b = (int)((x / k) % batch);
+        const int rk = (int)(x / ((long long)k * batch));
+        const long long dst = (long long)b * nranks * k + (long long)rk * k + j;
+        s_rows[dst] = s_all[x];
+        i_rows[dst] = i_all[x];
+    }
+}
+
+// Pack this rank's merged (o, lse) per row: [row][64*512 + 64].
+__global__ void pack_partial_kernel(const float* ctx, const float* lse, int batch, float* out) {
+    const int per = wl::AT_H * wl::AT_DV + wl::AT_H;
+    const long long n = (long long)batch * per;
+    for (long long x = blockIdx.x * (long long)blockDim.x + threadIdx.x; x < n; x += (long long)gridDim.x * blockDim.x) {
+        const int b = (int)(x / per), e = (int)(x % per);
+        out[x] = e < wl::AT_H * wl::AT_DV ? ctx[(long long)b * wl::AT_H * wl::AT_DV + e]
+                                          : lse[(long long)b * wl::AT_H + (e - wl::AT_H * wl::AT_DV)];
+    }
+}
+
+}  // namespace
+
+struct wl_comm {
+    ncclComm_t comm;
+    int32_t nranks;
+    int32_t rank;
+};
+
+extern "C" {
+
+const char* wl_strerror(int s) {
+    switch (s) {
+        case WL_OK: return "ok";
+        case WL_ERR_ARG: return "invalid argument";
+        case WL_ERR_T_EXCEEDS_MAX: return "T exceeds the cache capacity T_max";
+        case WL_ERR_NO_INDICES: return "consumer layer has no published indexer indices";
+        case WL_ERR_CUDA: return "CUDA error";
+        case WL_ERR_NCCL: return "NCCL error";
+        case WL_ERR_TIMEOUT: return "a bounded device wait timed out";
+        case WL_ERR_WORKSPACE: return "workspace missing or too small";
+        case WL_ERR_UNSUPPORTED: return "shape not supported by the compiled kernels";
+        case WL_ERR_DEVICE: return "device-side bounds check failed";
+        default: return "unknown status";
+    }
+}
+
+int32_t wl_abi_version(void) { return WL_ABI_VERSION; }
+
+int32_t wl_struct_sizes(int64_t* out, int32_t n) {
+    const int64_t s[] = {(int64_t)sizeof(wl_attn_cfg),     (int64_t)sizeof(wl_latent_cache),
+                         (int64_t)sizeof(wl_index_cache),  (int64_t)sizeof(wl_rows),
+                         (int64_t)sizeof(wl_index_share),  (int64_t)sizeof(wl_attn_decode_io),
+                         (int64_t)sizeof(wl_attn_prefill_io), (int64_t)sizeof(wl_shard)};
+    const int32_t m = (int32_t)(sizeof(s) / sizeof(s[0]));
+    for (int32_t i = 0; i < n && i < m && out; ++i) out[i] = s[i];
+    return m;
+}
+
+void wl_attn_cfg_glm52(wl_attn_cfg* c, int32_t T_max) {
+    if (!c) return;
+    c->n_heads = 64;
+    c->kv_lora = 512;
+    c->rope_dim = 64;
+    c->idx_heads = 32;
+    c->idx_dim = 128;
+    c->index_topk = 2048;
+    c->softmax_scale = 1.0f / 16.0f;            // (192 + 64)^-0.5
+    c->idx_qk_scale = 0.08838834764831845f;     // 128^-0.5
+    c->T_max = T_max;
+}
+
+// ---- IndexShare -------------------------------------------------------------------
+void wl_index_share_reset(wl_index_share* s) {
+    if (!s) return;
+    const int32_t dense = s->dense;
+    std::memset(s, 0, sizeof(*s));
+    s->producer = UINT32_MAX;
+    s->dense = dense;  // a property of the run, not of the token
+}
+
+void wl_index_share_publish(wl_index_share* s, uint32_t layer, const int32_t* idx, const int32_t* n_dev,
+                            int64_t stride, int32_t n) {
+    if (!s) return;
+    s->idx = idx;
+    s->n_dev = n_dev;
+    s->stride = stride;
+    s->n = n;
+    s->producer = layer;
+}
+
+int wl_index_share_require(const wl_index_share* s, uint32_t layer) {
+    if (!s) return WL_ERR_ARG;
+    if (s->dense) return WL_OK;
+    if (!s->idx) {
+        std::fprintf(stderr,
+                     "wl_attn: layer %u is \"shared\" but no preceding layer published indexer indices\n",
+                     layer);
+        return WL_ERR_NO_INDICES;
+    }
+    return WL_OK;
+}
+
+// ---- kernels as entry points ------------------------------------------------------------
+int wl_indexer_scores(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t T, const wl_rows* rows,
+                      const void* q_idx, const float* w_idx, float* index_out, int64_t index_stride,
+                      void* stream) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (int e = rows_ok(rows, T)) return e;
+    if (T > cfg->T_max) return WL_ERR_T_EXCEEDS_MAX;
+    if (int e = ensure_attrs()) return e;
+    return launch_indexer(cfg, cache, T, rows, q_idx, w_idx, index_out, index_stride,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int wl_indexer_topk(const float* index, int64_t index_stride, const wl_rows* rows, int32_t T, int32_t k,
+                    const int32_t* cand_idx, int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
+                    void* stream) {
+    if (int e = rows_ok(rows, T)) return e;
+    if (index_stride < T) return WL_ERR_ARG;
+    return launch_topk(index, index_stride, rows, T, k, cand_idx, sel_out, sel_stride, sel_n_out,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int wl_sel_normalize(const int32_t* sel_in, int64_t in_stride, const int32_t* n_in_dev, int32_t n_in,
+                     const wl_rows* rows, int32_t T, int32_t* sel_out, int64_t out_stride, int32_t* n_out_dev,
+                     void* stream) {
+    if (int e = rows_ok(rows, T)) return e;
+    if (int e = ensure_attrs()) return e;
+    return launch_normalize(sel_in, in_stride, n_in_dev, n_in, rows, T, sel_out, out_stride, n_out_dev,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int wl_mla_sparse_attn(const wl_attn_cfg* cfg, const wl_latent_cache* cache, int32_t T, const wl_rows* rows,
+                       const void* q_abs, const int32_t* sel, int64_t sel_stride, const int32_t* sel_n_dev,
+                       int32_t sel_n, int64_t win_lo, int64_t win_hi, int32_t split_keys, float* o_part,
+                       float* lse_part, int32_t max_splits, void* stream) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (int e = rows_ok(rows, T)) return e;
+    if (int e = ensure_attrs()) return e;
+    // Keys are positions in [0, win_hi); rows clamp to the window's end.
+    return launch_attn(cfg, cache, T, win_hi, rows, q_abs, sel, sel_stride, sel_n_dev, sel_n, win_lo, win_hi,
+                       split_keys, o_part, lse_part, max_splits, static_cast<cudaStream_t>(stream));
+}
+
+int wl_lse_merge(const float* o_part, const float* lse_part, int32_t n_rows, int32_t n_parts, int64_t row_stride,
+                 int64_t part_stride, int64_t lse_row_stride, int64_t lse_part_stride, int32_t n_heads,
+                 int32_t kv_lora, float* ctx, float* lse, void* stream) {
+    return launch_merge(o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
+                        lse_part_stride, n_heads, kv_lora, ctx, lse, static_cast<cudaStream_t>(stream));
+}
+
+// ---- decode --------------------------------------------------------------------------
+size_t wl_attn_workspace_bytes(const wl_attn_cfg* cfg, int32_t T_max, int32_t batch) {
+    if (!cfg || T_max <= 0 || batch <= 0) return 0;
+    return carve_decode(nullptr, cfg, T_max, batch, 1).bytes;
+}
+
+static int decode_local(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, const DecodeWs& w,
+                        int64_t t0, int64_t T_global, float* ctx, float* lse, const int32_t* sel,
+                        const int32_t* cnt, int32_t sel_n, int64_t stride, long long n_max, cudaStream_t st) {
+    // Attention over the selection restricted to this cache's window [t0, t0+T),
+    // then the merge of its split-K partials.
+    const int32_t B = io->batch;
+    const wl_rows rows{B, 1, (int32_t)T_global, 0};
+    if (n_max <= 0) n_max = 1;
+    const int32_t split = split_keys_for(n_max);
+    const int32_t nsplit = (int32_t)ceil_div(n_max, split);
+    if (int e = launch_attn(cfg, &io->latent, io->T, T_global, &rows, io->q_abs, sel, stride, cnt, sel_n, t0,
+                            t0 + io->T, split, w.o_part, w.lse_part, nsplit, st))
+        return e;
+    return launch_merge(w.o_part, w.lse_part, B, nsplit, (int64_t)nsplit * wl::AT_H * wl::AT_DV,
+                        (int64_t)wl::AT_H * wl::AT_DV, (int64_t)nsplit * wl::AT_H, wl::AT_H, wl::AT_H,
+                        wl::AT_DV, ctx, lse, st);
+}
+
+// Selection for decode: returns the list/count/stride the attention consumes.
+static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, const DecodeWs& w,
+                         const int32_t** sel, const int32_t** cnt, int64_t* stride, cudaStream_t st) {
+    const int32_t B = io->batch, T = io->T;
+    const wl_rows rows{B, 1, T, 0};
+    if (io->mode == WL_MODE_OWNER) {
+        float* index = io->index_out ? io->index_out : w.index;
+        const int64_t istride = io->index_out ? io->index_stride : T;
+        if (int e = launch_indexer(cfg, &io->index, T, &rows, io->q_idx, io->w_idx, index, istride, st)) return e;
+        const int32_t kk = cfg->index_topk < T ? cfg->index_topk : T;
+        int32_t* out = io->sel_out ? io->sel_out : w.sel;
+        const int64_t ostride = io->sel_out ? io->sel_stride : kk;
+        if (io->sel_out && io->sel_stride < kk) return WL_ERR_ARG;
+        int32_t* n_out = io->sel_n_out ? io->sel_n_out : w.cnt;
+        if (int e = launch_topk(index, istride, &rows, T, cfg->index_topk, nullptr, out, ostride, n_out, st)) return e;
+        *sel = out;
+        *cnt = n_out;
+        *stride = ostride;
+        return WL_OK;
+    }
+    if (io->mode == WL_MODE_CONSUMER) {
+        if (io->sel_flags & WL_SEL_CANONICAL) {
+            *sel = io->sel_in;
+            *cnt = io->sel_n_in;  // NULL: the attention kernel takes io->sel_n
+            *stride = io->sel_stride;
+            return WL_OK;
+        }
+        const int64_t ostride = T;
+        if (int e = launch_normalize(io->sel_in, io->sel_stride, io->sel_n_in, io->sel_n, &rows, T, w.sel, ostride,
+                                     w.cnt, st))
+            return e;
+        *sel = w.sel;
+        *cnt = w.cnt;
+        *stride = ostride;
+        return WL_OK;
+    }
+    *sel = nullptr;
+    *cnt = nullptr;
+    *stride = 0;
+    return WL_OK;
+}
+
+int wl_attn_decode(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+    if (int e = check_decode_io(cfg, io)) return e;
+    const DecodeWs need = carve_decode(nullptr, cfg, io->T, io->batch, 1);
+    if (!workspace || workspace_bytes < need.bytes) return WL_ERR_WORKSPACE;
+    if (int e = ensure_attrs()) return e;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const DecodeWs w = carve_decode(align_base(workspace), cfg, io->T, io->batch, 1);
+    const int32_t* sel = nullptr;
+    const int32_t* cnt = nullptr;
+    int64_t stride = 0;
+    if (int e = decode_select(cfg, io, w, &sel, &cnt, &stride, st)) return e;
+    long long n_max = io->T;  // dense: every key
+    int32_t sel_n = 0;
+    if (io->mode == WL_MODE_OWNER) n_max = cfg->index_topk < io->T ? cfg->index_topk : io->T;
+    if (io->mode == WL_MODE_CONSUMER) {
+        const bool canon = (io->sel_flags & WL_SEL_CANONICAL) != 0;
+        n_max = canon ? (io->sel_n_in ? io->sel_stride : io->sel_n) : io->T;
+        sel_n = io->sel_n;
+    }
+    float* lse = io->lse ? io->lse : w.lse_tmp;
+    return decode_local(cfg, io, w, 0, io->T, io->ctx, lse, sel, cnt, sel_n, stride, n_max, st);
+}
+
+int wl_attn_layer_decode(const wl_attn_cfg* cfg, wl_attn_decode_io* io, int32_t owner, uint32_t layer,
+                         wl_index_share* share, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!io || !share) return WL_ERR_ARG;
+    if (owner) {
+        if (!io->sel_out || !io->sel_n_out) return WL_ERR_ARG;  // the published buffer must outlive the call
+        io->mode = WL_MODE_OWNER;
+        if (int e = wl_attn_decode(cfg, io, workspace, workspace_bytes, stream)) return e;
+        // Publish the raw selection (glm_layer_runner.cuh:604).
+        wl_index_share_publish(share, layer, io->sel_out, io->sel_n_out, io->sel_stride,
+                               cfg->index_topk < io->T ? cfg->index_topk : io->T);
+        return WL_OK;
+    }
+    if (int e = wl_index_share_require(share, layer)) return e;
+    if (share->dense) {
+        io->mode = WL_MODE_DENSE;
+    } else {
+        io->mode = WL_MODE_CONSUMER;
+        io->sel_in = share->idx;
+        io->sel_n_in = share->n_dev;
+        io->sel_n = share->n;
+        io->sel_stride = share->stride;
+        io->sel_flags = WL_SEL_CANONICAL;  // this library only publishes canonical lists
+    }
+    return wl_attn_decode(cfg, io, workspace, workspace_bytes, stream);
+}
+
+// ---- prefill ----------------------------------------------------------------------------
+static size_t prefill_ws(const wl_attn_cfg* cfg, int32_t n_q, int32_t T, void* base, float** index,
+                         int32_t** sel, int32_t** cnt, float** lse) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> void* {
+        void* p = base ? static_cast<char*>(base) + off : nullptr;
+        off += align256(bytes);
+        return p;
+    };
+    const size_t k = (size_t)(cfg->index_topk < T ? cfg->index_topk : T);
+    *index = static_cast<float*>(take((size_t)n_q * T * 4));
+    *sel = static_cast<int32_t*>(take((size_t)n_q * (size_t)T * 4 > (size_t)n_q * k * 4 ? (size_t)n_q * T * 4
+                                                                                          : (size_t)n_q * k * 4));
+    *cnt = static_cast<int32_t*>(take((size_t)n_q * 4));
+    *lse = static_cast<float*>(take((size_t)n_q * wl::AT_H * 4));
+    return off + 256;
+}
+
+size_t wl_attn_prefill_workspace_bytes(const wl_attn_cfg* cfg, int32_t n_q, int32_t T) {
+    if (!cfg || n_q <= 0 || T <= 0) return 0;
+    float* a;
+    int32_t* b;
+    int32_t* c;
+    float* d;
+    return prefill_ws(cfg, n_q, T, nullptr, &a, &b, &c, &d);
+}
+
+int wl_attn_prefill(const wl_attn_cfg* cfg, const wl_attn_prefill_io* io, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (!io || io->n_q <= 0 || io->pos0 < 0 || !io->q_abs || !io->ctx) return WL_ERR_ARG;
+    const int32_t T = io->pos0 + io->n_q;
+    if (T > cfg->T_max) return WL_ERR_T_EXCEEDS_MAX;
+    if (io->n_q > 65535) return WL_ERR_ARG;
+    if (workspace_bytes < wl_attn_prefill_workspace_bytes(cfg, io->n_q, T) || !workspace) return WL_ERR_WORKSPACE;
+    if (int e = ensure_attrs()) return e;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* w_index;
+    int32_t* w_sel;
+    int32_t* w_cnt;
+    float* w_lse;
+    prefill_ws(cfg, io->n_q, T, align_base(workspace), &w_index, &w_sel, &w_cnt, &w_lse);
+    const wl_rows rows{io->n_q, io->n_q, io->pos0 + 1, 1};
+    const int32_t* sel = nullptr;
+    const int32_t* cnt = nullptr;
+    int64_t stride = 0;
+    if (io->mode == WL_MODE_OWNER) {
+        if (!io->q_idx || !io->w_idx || !io->index.keys || !io->index.scale) return WL_ERR_ARG;
+        float* index = io->index_out ? io->index_out : w_index;
+        const int64_t istride = io->index_out ? io->index_stride : T;
+        if (int e = launch_indexer(cfg, &io->index, T, &rows, io->q_idx, io->w_idx, index, istride, st)) return e;
+        const int32_t kk = cfg->index_topk < T ? cfg->index_topk : T;
+        int32_t* out = io->sel_out ? io->sel_out : w_sel;
+        const int64_t ostride = io->sel_out ? io->sel_stride : kk;
+        if (io->sel_out && io->sel_stride < kk) return WL_ERR_ARG;
+        int32_t* n_out = io->sel_n_out ? io->sel_n_out : w_cnt;
+        if (int e = launch_topk(index, istride, &rows, T, cfg->index_topk, nullptr, out, ostride, n_out, st)) return e;
+        sel = out;
+        cnt = n_out;
+        stride = ostride;
+    } else if (io->mode == WL_MODE_CONSUMER) {
+        if (!io->sel_in) return WL_ERR_NO_INDICES;
+        if (io->sel_flags & WL_SEL_CANONICAL) {
+            sel = io->sel_in;
+            stride = io->sel_stride;
+            if (io->sel_n_in) {
+                cnt = io->sel_n_in;
+            } else {
+                // min(topk, row length) per row, as an owner of this chunk writes.
+                row_counts_kernel<<<(unsigned)ceil_div(io->n_q, 256), 256, 0, st>>>(rows.n_rows, rows.len0,
+                                                                                    rows.len_step, T,
+                                                                                    cfg->index_topk, w_cnt);
+                WL_CUDA_TRY(cudaGetLastError());
+                cnt = w_cnt;
+            }
+        } else {
+            const int32_t n_in = (int32_t)io->sel_stride;
+            if (int e = launch_normalize(io->sel_in, io->sel_stride, io->sel_n_in, n_in, &rows, T, w_sel, T, w_cnt, st))
+                return e;
+            sel = w_sel;
+            cnt = w_cnt;
+            stride = T;
+        }
+    } else if (io->mode != WL_MODE_DENSE) {
+        return WL_ERR_ARG;
+    }
+    float* lse = io->lse ? io->lse : w_lse;
+    return launch_attn(cfg, &io->latent, T, T, &rows, io->q_abs, sel, stride, cnt, 0, 0, T, 0, io->ctx, lse, 1, st);
+}
+
+// ---- sharded decode ----------------------------------------------------------------------------
+int wl_comm_unique_id(uint8_t id_out[128]) {
+    if (!id_out) return WL_ERR_ARG;
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return WL_ERR_NCCL;
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    std::memcpy(id_out, &id, 128);
+    return WL_OK;
+}
+
+int wl_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank, wl_comm** out) {
+    if (!id || !out || nranks <= 0 || rank < 0 || rank >= nranks) return WL_ERR_ARG;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, 128);
+    wl_comm* c = new wl_comm{};
+    c->nranks = nranks;
+    c->rank = rank;
+    if (ncclCommInitRank(&c->comm, nranks, uid, rank) != ncclSuccess) {
+        delete c;
+        return WL_ERR_NCCL;
+    }
+    *out = c;
+    return WL_OK;
+}
+
+int wl_comm_destroy(wl_comm* c) {
+    if (!c) return WL_ERR_ARG;
+    const ncclResult_t r = ncclCommDestroy(c->comm);
+    delete c;
+    return r == ncclSuccess ? WL_OK : WL_ERR_NCCL;
+}
+
+size_t wl_attn_sharded_workspace_bytes(const wl_attn_cfg* cfg, int32_t T_local_max, int32_t batch, int32_t nranks) {
+    if (!cfg || T_local_max <= 0 || batch <= 0 || nranks <= 0) return 0;
+    return carve_decode(nullptr, cfg, T_local_max, batch, nranks > 1 ? nranks : 2).bytes;
+}
+
+int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, const wl_shard* shard, wl_comm* comm,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+    if (int e = check_decode_io(cfg, io)) return e;
+    if (!shard || !comm || shard->t0 < 0 || shard->T_global < shard->t0 + io->T) return WL_ERR_ARG;
+    const int32_t N = comm->nranks;
+    const DecodeWs need = carve_decode(nullptr, cfg, io->T, io->batch, N > 1 ? N : 2);
+    if (!workspace || workspace_bytes < need.bytes) return WL_ERR_WORKSPACE;
+    if (int e = ensure_attrs()) return e;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const DecodeWs w = carve_decode(align_base(workspace), cfg, io->T, io->batch, N > 1 ? N : 2);
+    const int32_t B = io->batch, T = io->T, k = cfg->index_topk;
+    const int64_t Tg = shard->T_global, t0 = shard->t0;
+    const int32_t kg = (int32_t)(k < Tg ? k : Tg);
+
+    const int32_t* gsel = nullptr;
+    const int32_t* gcnt = nullptr;
+    int64_t gstride = 0;
+    if (io->mode == WL_MODE_OWNER) {
+        if (!io->sel_out || !io->sel_n_out || io->sel_stride < kg) return WL_ERR_ARG;
+        const wl_rows lrows{B, 1, T, 0};
+        float* index = w.index;
+        if (int e = launch_indexer(cfg, &io->index, T, &lrows, io->q_idx, io->w_idx, index, T, st)) return e;
+        const int32_t kl = k < T ? k : T;
+        if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st)) return e;
+        gather_candidates_kernel<<<dim3((unsigned)ceil_div(k, 256), B), 256, 0, st>>>(index, T, w.sel, kl, w.cnt, k, t0,
+                                                                                     w.cand_score, w.cand_idx);
+        WL_CUDA_TRY(cudaGetLastError());
+        if (ncclGroupStart() != ncclSuccess) return WL_ERR_NCCL;
+        if (ncclAllGather(w.cand_score, w.cand_score_all, (size_t)B * k, ncclFloat32, comm->comm, st) != ncclSuccess ||
+            ncclAllGather(w.cand_idx, w.cand_idx_all, (size_t)B * k, ncclInt32, comm->comm, st) != ncclSuccess) {
+            ncclGroupEnd();
+            return WL_ERR_NCCL;
+        }
+        if (ncclGroupEnd() != ncclSuccess) return WL_ERR_NCCL;
+        candidates_to_rows_kernel<<<256, 256, 0, st>>>(w.cand_score_all, w.cand_idx_all, N, B, k, w.cand_score_rows,
+                                                      w.cand_idx_rows);
+        WL_CUDA_TRY(cudaGetLastError());
+        // Exact global top-k over the candidates; candidate order is global
+        // key order, so position ties resolve to the lowest global index.
+        const wl_rows crows{B, 1, N * k, 0};
+        if (int e = launch_topk(w.cand_score_rows, (int64_t)N * k, &crows, N * k, kg, w.cand_idx_rows, io->sel_out,
+                                io->sel_stride, io->sel_n_out, st))
+            return e;
+        if (io->index_out) {
+            // Local scores into the caller's buffer (this rank's window).
+            for (int32_t b = 0; b < B; ++b)
+                WL_CUDA_TRY(cudaMemcpy2DAsync(io->index_out + (int64_t)b * io->index_stride, (size_t)T * 4,
+                                              index + (int64_t)b * T, (size_t)T * 4, (size_t)T * 4, 1,
+                                              cudaMemcpyDeviceToDevice, st));
+        }
+        gsel = io->sel_out;
+        gcnt = io->sel_n_out;
+        gstride = io->sel_stride;
+    } else if (io->mode == WL_MODE_CONSUMER) {
+        const wl_rows grows{B, 1, (int32_t)Tg, 0};
+        if (io->sel_flags & WL_SEL_CANONICAL) {
+            gsel = io->sel_in;
+            gcnt = io->sel_n_in;
+            gstride = io->sel_stride;
+        } else {
+            if (Tg > (int64_t)T * N) return WL_ERR_WORKSPACE;  // normalised lists need B x T_global
+            if (int e = launch_normalize(io->sel_in, io->sel_stride, io->sel_n_in, io->sel_n, &grows, (int32_t)Tg, w.sel,
+                                         (int32_t)Tg, w.cnt, st))
+                return e;
+            gsel = w.sel;
+            gcnt = w.cnt;
+            gstride = Tg;
+        }
+    }
+    // Local partial over this rank's window, merged over its splits.
+    float* lctx = w.part_recv;  // scratch: [B][64][512] then lse [B][64]
+    float* llse = w.part_recv + (size_t)B * wl::AT_H * wl::AT_DV;
+    long long n_max = Tg;
+    int32_t sel_n = 0;
+    if (io->mode == WL_MODE_OWNER) n_max = kg;
+    if (io->mode == WL_MODE_CONSUMER) {
+        n_max = (gcnt || !(io->sel_flags & WL_SEL_CANONICAL)) ? gstride : io->sel_n;
+        sel_n = io->sel_n;
+    }
+    if (int e = decode_local(cfg, io, w, t0, Tg, lctx, llse, gsel, gcnt, sel_n, gstride, n_max, st)) return e;
+    pack_partial_kernel<<<256, 256, 0, st>>>(lctx, llse, B, w.part_send);
+    WL_CUDA_TRY(cudaGetLastError());
+    const size_t per = (size_t)B * (wl::AT_H * wl::AT_DV + wl::AT_H);
+    if (ncclAllGather(w.part_send, w.part_recv, per, ncclFloat32, comm->comm, st) != ncclSuccess) return WL_ERR_NCCL;
+    // part_recv: [rank][row][64*512 + 64]
+    const int64_t rowsz = wl::AT_H * wl::AT_DV + wl::AT_H;
+    float* lse = io->lse ? io->lse : w.lse_tmp;
+    return launch_merge(w.part_recv, w.part_recv + wl::AT_H * wl::AT_DV, B, N, rowsz, (int64_t)B * rowsz, rowsz,
+                        (int64_t)B * rowsz, wl::AT_H, wl::AT_DV, io->ctx, lse, st);
+}
+
+// ---- diagnostics ---------------------------------------------------------------------------
+int wl_device_error(int32_t clear, uint32_t* detail) {
+    WL_CUDA_TRY(cudaDeviceSynchronize());
+    unsigned w = 0;
+    WL_CUDA_TRY(cudaMemcpyFromSymbol(&w, wl::g_err_word, sizeof(w)));
+    if (detail) *detail = w;
+    if (clear) {
+        const unsigned z = 0;
+        WL_CUDA_TRY(cudaMemcpyToSymbol(wl::g_err_word, &z, sizeof(z)));
+    }
+    if (w == 0) return WL_OK;
+    const unsigned code = w >> 24;
+    return code == wl::ERRC_TIMEOUT ? WL_ERR_TIMEOUT : WL_ERR_DEVICE;
+}
+
+}  // extern "C"
