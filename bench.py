@@ -255,14 +255,15 @@ def main():
 
         def step(i=0):
             _lib.check(L.wl_attn_decode_sharded(C.byref(cfg), C.byref(io), C.byref(shard), comm.h, ws.data_ptr(),
-                                                nbytes, stream.cuda_stream))
+                                                nbytes, torch.cuda.current_stream().cuda_stream))
         launches_per_step = 9
     else:
         nbytes = L.wl_attn_workspace_bytes(C.byref(cfg), T, B)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
 
         def step(i=0):
-            _lib.check(L.wl_attn_decode(C.byref(cfg), C.byref(io), ws.data_ptr(), nbytes, stream.cuda_stream))
+            _lib.check(L.wl_attn_decode(C.byref(cfg), C.byref(io), ws.data_ptr(), nbytes,
+                                        torch.cuda.current_stream().cuda_stream))
         launches_per_step = 4
 
     for _ in range(max(args.warmup, 3)):
@@ -317,9 +318,19 @@ def main():
     for _ in range(3):
         e2e_step()
     torch.cuda.synchronize()
+    e2e_run = e2e_step
+    if graph is not None:
+        ge = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ge):
+            e2e_step()
+        torch.cuda.synchronize()
+        e2e_run = lambda i: ge.replay()  # noqa: E731
+        for _ in range(3):
+            e2e_run(0)
+        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    ms_e2e = elapsed_ms(torch, e2e_step, args.steps, stream)
+    ms_e2e = elapsed_ms(torch, e2e_run, args.steps, stream)
     t_e2e = torch.tensor([ms_e2e / args.steps], device=device)
     if world > 1:
         dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
@@ -406,32 +417,35 @@ def kernel_breakdown(torch, A, _lib, cfg, data, steps, stream):
     lse = torch.empty(B, 64, dtype=torch.float32, device=dev)
     rows = _lib.Rows(B, 1, T, 0)
     kc, lc = data["keys"].c(), data["kv"].c()
-    st = stream.cuda_stream
     calls = {
-        "indexer_scores": lambda: L.wl_indexer_scores(C.byref(cfg), C.byref(kc), T, C.byref(rows),
+        "indexer_scores": lambda st: L.wl_indexer_scores(C.byref(cfg), C.byref(kc), T, C.byref(rows),
                                                       data["q_idx"].data_ptr(), data["w_idx"].data_ptr(),
                                                       index.data_ptr(), T, st),
-        "topk": lambda: L.wl_indexer_topk(index.data_ptr(), T, C.byref(rows), T, K, None, sel.data_ptr(), K,
+        "topk": lambda st: L.wl_indexer_topk(index.data_ptr(), T, C.byref(rows), T, K, None, sel.data_ptr(), K,
                                           cnt.data_ptr(), st),
-        "mla_sparse_attn": lambda: L.wl_mla_sparse_attn(C.byref(cfg), C.byref(lc), T, C.byref(rows),
+        "mla_sparse_attn": lambda st: L.wl_mla_sparse_attn(C.byref(cfg), C.byref(lc), T, C.byref(rows),
                                                         data["q_abs"].data_ptr(), sel.data_ptr(), K,
                                                         cnt.data_ptr(), 0, 0, T, 128, o_part.data_ptr(),
                                                         l_part.data_ptr(), S, st),
-        "lse_merge": lambda: L.wl_lse_merge(o_part.data_ptr(), l_part.data_ptr(), B, S, S * 64 * 512, 64 * 512,
+        "lse_merge": lambda st: L.wl_lse_merge(o_part.data_ptr(), l_part.data_ptr(), B, S, S * 64 * 512, 64 * 512,
                                             S * 64, 64, 64, 512, ctx.data_ptr(), lse.data_ptr(), st),
     }
-    n = max(5, min(steps, 50))
-    ev = {k: [] for k in calls}
-    for it in range(n + 2):
-        for name, fn in calls.items():
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            _lib.check(fn(), name)
-            e.record(stream)
-            if it >= 2:
-                ev[name].append((s, e))
-    torch.cuda.synchronize()
-    us = {k: statistics.mean(s.elapsed_time(e) for s, e in v) * 1e3 for k, v in ev.items()}
+    st_now = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    reps = 20
+    us = {}
+    for name, fn in calls.items():
+        _lib.check(fn(st_now()), name)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                _lib.check(fn(st_now()), name)
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        n = 5
+        ms = elapsed_ms(torch, lambda i: g.replay(), n, stream)
+        us[name] = ms / (n * reps) * 1e3
     # algorithmic bytes per launch
     algo = {
         "indexer_scores": B * T * (128 + 4 + 4) + B * (32 * 128 * 2 + 32 * 4),
@@ -472,23 +486,24 @@ def side_configs(torch, A, _lib, device, stream):
             ios.append((io, keep, io2, keep2))
         res = {}
         for mode in (0, 1):
-            graphs = []
+            fns = []
             for i in range(n_inst):
                 io = ios[i][0] if mode == 0 else ios[i][2]
-                fn = lambda io=io: _lib.check(L.wl_attn_decode(C.byref(cfg), C.byref(io), ws.data_ptr(), nbytes,
-                                                               stream.cuda_stream))
-                fn()
-                torch.cuda.synchronize()
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    fn()
-                graphs.append(g)
-            for i in range(3 * n_inst):
-                graphs[i % n_inst].replay()
+                fns.append(lambda io=io: _lib.check(L.wl_attn_decode(C.byref(cfg), C.byref(io), ws.data_ptr(),
+                                                                     nbytes, torch.cuda.current_stream().cuda_stream)))
+            for f in fns:
+                f()
             torch.cuda.synchronize()
-            steps = 20 * n_inst
-            ms = elapsed_ms(torch, lambda i: graphs[i % n_inst].replay(), steps, stream)
-            us = ms / steps * 1e3
+            g = torch.cuda.CUDAGraph()  # one graph = one step on each instance, round robin
+            with torch.cuda.graph(g):
+                for f in fns:
+                    f()
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            reps = 20
+            ms = elapsed_ms(torch, lambda i: g.replay(), reps, stream)
+            us = ms / (reps * n_inst) * 1e3
             algo = (T * 132 if mode == 0 else 0) + min(2048, T) * 1152
             res["owner" if mode == 0 else "consumer"] = {"us_per_layer": round(us, 2),
                                                          "algo_bytes": algo,

@@ -222,7 +222,8 @@ def test_split_k_merge_vs_single_cta():
     rc, _ = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
     assert_ulp(rc, c1, what="single")
     assert_ulp(rc, c16, what="split")
-    assert np.abs(l1 - l16).max() < 1e-4
+    # lse: the per-split bf16 rounding of P differs; 1e-3 absolute (as vs the oracle)
+    assert np.abs(l1 - l16).max() < 1e-3
 
 
 def test_attention_key_window():

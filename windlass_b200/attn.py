@@ -226,7 +226,8 @@ def decode_io(cfg: AttnCfg, kv: LatentKV, q_abs: torch.Tensor, *, keys: IndexKey
     io.index_stride = index_out.stride(0) if index_out is not None else 0
     io.ctx = _ptr(ctx)
     io.lse = _ptr(lse)
-    keep = dict(ctx=ctx, lse=lse, sel_out=sel_out, sel_n_out=sel_n_out, index_out=index_out,
+    keep = dict(ctx=ctx, lse=lse, sel=sel_out, sel_n=sel_n_out, sel_out=sel_out, sel_n_out=sel_n_out,
+                index_out=index_out,
                 q_abs=q_abs, q_idx=q_idx, w_idx=w_idx, sel_in=sel_in, sel_n_in=sel_n_in, kv=kv,
                 keys=keys)
     return io, keep
