@@ -417,12 +417,13 @@ def kernel_breakdown(torch, A, _lib, cfg, data, steps, stream):
     lse = torch.empty(B, 64, dtype=torch.float32, device=dev)
     rows = _lib.Rows(B, 1, T, 0)
     kc, lc = data["keys"].c(), data["kv"].c()
+    tws = torch.empty(L.wl_indexer_topk_workspace_bytes(B, T), dtype=torch.uint8, device=dev)
     calls = {
         "indexer_scores": lambda st: L.wl_indexer_scores(C.byref(cfg), C.byref(kc), T, C.byref(rows),
                                                       data["q_idx"].data_ptr(), data["w_idx"].data_ptr(),
                                                       index.data_ptr(), T, st),
         "topk": lambda st: L.wl_indexer_topk(index.data_ptr(), T, C.byref(rows), T, K, None, sel.data_ptr(), K,
-                                          cnt.data_ptr(), st),
+                                             cnt.data_ptr(), tws.data_ptr(), tws.numel(), st),
         "mla_sparse_attn": lambda st: L.wl_mla_sparse_attn(C.byref(cfg), C.byref(lc), T, C.byref(rows),
                                                         data["q_abs"].data_ptr(), sel.data_ptr(), K,
                                                         cnt.data_ptr(), 0, 0, T, 128, o_part.data_ptr(),

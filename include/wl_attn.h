@@ -220,7 +220,10 @@ int wl_indexer_scores(const wl_attn_cfg* cfg, const wl_index_cache* cache,
 int wl_indexer_topk(const float* index, int64_t index_stride, const wl_rows* rows,
                     int32_t T, int32_t k, const int32_t* cand_idx,
                     int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
-                    void* stream);
+                    void* workspace, size_t workspace_bytes, void* stream);
+/* Workspace that lets wl_indexer_topk split rows longer than 40960 keys over
+ * many CTAs (without it such rows run one CTA each). */
+size_t wl_indexer_topk_workspace_bytes(int32_t n_rows, int32_t T);
 
 /* a5 semantics: turn an arbitrary index list (any order, duplicates, entries
  * outside [0, len(r))) into the canonical list of the keys it keeps. Same

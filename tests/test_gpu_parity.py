@@ -426,3 +426,31 @@ def test_prefill_consumer_and_dense():
     big = A.attn_prefill(A.glm52_cfg(T, index_topk=4096), g["kv"], g["q_abs"], pos0, keys=g["keys"],
                          q_idx=g["q_idx"], w_idx=g["w_idx"])
     assert torch.equal(den["ctx"], big["ctx"]), "k >= T: sparse prefill must equal dense bit for bit"
+
+
+def test_decode_long_context_multi_cta_topk():
+    """T above the single-CTA top-k limit: the multi-CTA top-k's set must equal
+    numpy's top-k of the GPU's own scores exactly, and the attention must match."""
+    T, B = 50000, 2
+    inps = [o.make_inputs(T, 4, seq=s) for s in range(B)]
+    g = stack_inputs(inps)
+    cfg = A.glm52_cfg(T)
+    idx_out = torch.empty(B, T, dtype=torch.float32, device="cuda")
+    out = _decode(cfg, g, index_out=idx_out)
+    for s, inp in enumerate(inps):
+        sel = cpu(out["sel"])[s]
+        gi = cpu(idx_out)[s]
+        canonical_ok(sel, 2048, T)
+        assert np.array_equal(sel, np.sort(o.indexer_topk(gi, 2048)))
+        ref_index = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+        assert np.abs(gi - ref_index).max() <= IDX_TOL * np.abs(ref_index).max()
+        rc, _ = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
+        assert_ulp(rc, cpu(out["ctx"])[s], what=f"seq {s}")
+
+
+def test_topk_multi_cta_with_heavy_ties():
+    rng = np.random.default_rng(11)
+    _topk_case(rng.integers(0, 3, 100000).astype(np.float32), 2048)
+    x = np.zeros(60000, np.float32)
+    x[rng.choice(60000, 100, replace=False)] = 1.0
+    _topk_case(x, 2048)

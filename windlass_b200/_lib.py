@@ -87,7 +87,8 @@ SIGNATURES = {
     "wl_attn_prefill": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(PrefillIO), vp, C.c_size_t, vp]),
     "wl_indexer_scores": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(IndexCache), i32,
                                     C.POINTER(Rows), vp, vp, vp, i64, vp]),
-    "wl_indexer_topk": (C.c_int, [vp, i64, C.POINTER(Rows), i32, i32, vp, vp, i64, vp, vp]),
+    "wl_indexer_topk": (C.c_int, [vp, i64, C.POINTER(Rows), i32, i32, vp, vp, i64, vp, vp, C.c_size_t, vp]),
+    "wl_indexer_topk_workspace_bytes": (C.c_size_t, [i32, i32]),
     "wl_sel_normalize": (C.c_int, [vp, i64, vp, i32, C.POINTER(Rows), i32, vp, i64, vp, vp]),
     "wl_mla_sparse_attn": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(LatentCache), i32,
                                      C.POINTER(Rows), vp, vp, i64, vp, i32, i64, i64, i32, vp,

@@ -132,8 +132,10 @@ def indexer_topk(index: torch.Tensor, k: int, rows: Rows | None = None, T: int |
     kk = min(k, T)
     sel = torch.full((rows.n_rows, kk), -1, dtype=torch.int32, device=index.device)
     n = torch.empty(rows.n_rows, dtype=torch.int32, device=index.device)
+    nbytes = lib().wl_indexer_topk_workspace_bytes(rows.n_rows, T)
+    ws = workspace(nbytes, index.device)
     check(lib().wl_indexer_topk(_ptr(index), index.stride(0), C.byref(rows), T, k, _ptr(cand_idx),
-                                _ptr(sel), kk, _ptr(n), _stream()), "wl_indexer_topk")
+                                _ptr(sel), kk, _ptr(n), _ptr(ws), ws.numel(), _stream()), "wl_indexer_topk")
     return sel, n
 
 

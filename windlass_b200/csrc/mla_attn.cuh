@@ -47,7 +47,7 @@ struct AttnLayout {
     static constexpr uint32_t OFF_ROWIDX = OFF_ALPHA + AT_H * 4;
     static constexpr uint32_t OFF_BAR = OFF_ROWIDX + AT_TILE * 4;
     static constexpr uint32_t OFF_MISC = OFF_BAR + 16;
-    static constexpr uint32_t BYTES = OFF_MISC + 32 + 1024;
+    static constexpr uint32_t BYTES = OFF_MISC + 64 + 1024;
     static constexpr uint32_t TMEM_COLS = 512;  // S: [0,64)  O^T: [64, 320)
     static constexpr uint32_t IDESC_QK = idesc_bf16(128, 64, 0, 0);
     static constexpr uint32_t IDESC_PV = idesc_bf16(128, 64, 1, 1);
@@ -95,16 +95,6 @@ __device__ __forceinline__ void warp_transpose_reduce64(float* v, float& out0, f
     out1 = v[1];
 }
 
-__device__ __forceinline__ int lower_bound_i32(const int* a, int n, long long key) {
-    int lo = 0, hi = n;
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if ((long long)a[mid] < key) lo = mid + 1;
-        else hi = mid;
-    }
-    return lo;
-}
-
 __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     using L = AttnLayout;
     extern __shared__ uint8_t smem_raw[];
@@ -118,7 +108,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     float* alpha = reinterpret_cast<float*>(smem + L::OFF_ALPHA);
     int* row_idx = reinterpret_cast<int*>(smem + L::OFF_ROWIDX);
     uint64_t* bar_mma = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-    int* misc = reinterpret_cast<int*>(smem + L::OFF_MISC);  // [0]=cb [1]=ce [2]=tmem [3]=rescale
+    int* misc = reinterpret_cast<int*>(smem + L::OFF_MISC);  // [0]=cb [1]=ce [2]=tmem [3]=rescale [4,5]=e0,e1
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = blockIdx.y, s = blockIdx.x;
@@ -127,29 +117,57 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     const long long len = lraw < p.len_T ? lraw : p.len_T;
     const int* list = p.sel ? p.sel + (long long)r * p.sel_stride : nullptr;
 
-    if (tid == 0) {
+    // Entry range [e0, e1) of the list inside the key window. A window that
+    // covers the whole row needs no search (canonical lists lie in [0, len));
+    // otherwise warps 0 and 1 each run a 32-ary lower-bound search.
+    {
         const long long lo_key = p.win_lo > 0 ? p.win_lo : 0;
         const long long hi_key = p.win_hi < len ? p.win_hi : len;
-        long long e0, e1;
         if (!list) {
-            e0 = lo_key;
-            e1 = hi_key > lo_key ? hi_key : lo_key;
+            if (tid == 0) {
+                misc[4] = (int)lo_key;
+                misc[5] = (int)(hi_key > lo_key ? hi_key : lo_key);
+            }
         } else {
-            const int n = p.sel_n_dev ? p.sel_n_dev[r] : p.sel_n;
-            e0 = lower_bound_i32(list, n, lo_key);
-            e1 = lower_bound_i32(list, n, hi_key);
+            const int n = p.sel_n_dev ? __ldg(p.sel_n_dev + r) : p.sel_n;
+            if (p.win_lo <= 0 && p.win_hi >= len) {
+                if (tid == 0) {
+                    misc[4] = 0;
+                    misc[5] = n;
+                }
+            } else if (warp < 2) {
+                const long long key = warp == 0 ? lo_key : hi_key;
+                // lower bound: first position whose key is >= `key` (or n)
+                int lo = 0, hi = n;
+                while (hi > lo) {
+                    const int step = (hi - lo + 31) / 32;
+                    const int pos = lo + lane * step;
+                    const bool less = pos < hi && (long long)__ldg(list + pos) < key;
+                    const int cnt = __popc(__ballot_sync(0xffffffffu, less));  // ascending list
+                    if (cnt == 0) break;
+                    const int nlo = lo + (cnt - 1) * step + 1;
+                    hi = min(hi, lo + cnt * step);
+                    lo = nlo;
+                }
+                if (lane == 0) misc[4 + warp] = lo;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const long long e0 = misc[4];
+            long long e1 = misc[5];
             if (e1 < e0) e1 = e0;
+            long long cb, ce;
+            if (p.split_keys > 0) {
+                cb = e0 + (long long)s * p.split_keys;
+                ce = cb + p.split_keys < e1 ? cb + p.split_keys : e1;
+            } else {
+                cb = e0;
+                ce = (s == 0) ? e1 : e0;
+            }
+            misc[0] = (int)cb;
+            misc[1] = (int)(ce > cb ? ce : cb);
         }
-        long long cb, ce;
-        if (p.split_keys > 0) {
-            cb = e0 + (long long)s * p.split_keys;
-            ce = cb + p.split_keys < e1 ? cb + p.split_keys : e1;
-        } else {
-            cb = e0;
-            ce = (s == 0) ? e1 : e0;
-        }
-        misc[0] = (int)cb;
-        misc[1] = (int)(ce > cb ? ce : cb);
     }
     __syncthreads();
     const int cb = misc[0], ce = misc[1];
@@ -351,6 +369,8 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     }
 
     if (ok) {
+        if (tid < AT_H) alpha[tid] = 1.f / l_run[tid];  // reuse: 1/l per head
+        __syncthreads();
         // o[h][c] = O^T[c][h] / l[h]; lane = c within chunk q.
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
@@ -363,7 +383,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int h = hf * 32 + i;
-                    o_out[h * AT_DV + c] = ov[i] / l_run[h];
+                    o_out[h * AT_DV + c] = ov[i] * alpha[h];
                 }
             }
         }
@@ -390,34 +410,34 @@ struct MergeParams {
     float* lse;
 };
 
-// grid (n_heads, n_rows), 128 threads; dv multiple of 4.
-__global__ void __launch_bounds__(128) lse_merge_kernel(MergeParams p) {
-    const int h = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+// grid (n_heads, dv / 128, n_rows), 32 threads: lane l owns 4 latent columns.
+// Up to 32 parts: lane s holds part s's lse; all parts' columns load at once.
+__global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
+    const int h = blockIdx.x, q = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
     const float* lp = p.lse_part + (long long)r * p.lse_row_stride + h;
-    float M = -INFINITY;
-    for (int s = 0; s < p.n_parts; ++s) M = fmaxf(M, lp[(long long)s * p.lse_part_stride]);
-    float W = 0.f;
-    if (M != -INFINITY)
-        for (int s = 0; s < p.n_parts; ++s) W += exp2f((lp[(long long)s * p.lse_part_stride] - M) * 1.4426950408889634f);
-    float* out = p.ctx + ((long long)r * p.n_heads + h) * p.dv;
-    for (int c4 = tid; c4 < p.dv / 4; c4 += 128) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (M != -INFINITY) {
-            for (int s = 0; s < p.n_parts; ++s) {
-                const float ls = lp[(long long)s * p.lse_part_stride];
-                if (ls == -INFINITY) continue;
-                const float wgt = exp2f((ls - M) * 1.4426950408889634f) / W;
-                const float4 v = *reinterpret_cast<const float4*>(
-                    p.o_part + (long long)r * p.row_stride + (long long)s * p.part_stride + (long long)h * p.dv + c4 * 4);
-                acc.x = fmaf(wgt, v.x, acc.x);
-                acc.y = fmaf(wgt, v.y, acc.y);
-                acc.z = fmaf(wgt, v.z, acc.z);
-                acc.w = fmaf(wgt, v.w, acc.w);
-            }
-        }
-        reinterpret_cast<float4*>(out)[c4] = acc;
+    const float ls = lane < p.n_parts ? lp[(long long)lane * p.lse_part_stride] : -INFINITY;
+    float M = ls;
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float wl = (M == -INFINITY || ls == -INFINITY) ? 0.f : exp2f((ls - M) * 1.4426950408889634f);
+    float W = wl;
+    for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+    const int c = q * 128 + lane * 4;
+    const float* base = p.o_part + (long long)r * p.row_stride + (long long)h * p.dv + c;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = 0; s < p.n_parts; ++s) {
+        const float w = __shfl_sync(0xffffffffu, wl, s) * inv;
+        if (w == 0.f) continue;  // uniform: empty parts are never read
+        const float4 v = *reinterpret_cast<const float4*>(base + (long long)s * p.part_stride);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
     }
-    if (tid == 0 && p.lse) p.lse[(long long)r * p.n_heads + h] = (M == -INFINITY) ? -INFINITY : M + logf(W);
+    *reinterpret_cast<float4*>(p.ctx + ((long long)r * p.n_heads + h) * p.dv + c) = acc;
+    if (q == 0 && lane == 0 && p.lse)
+        p.lse[(long long)r * p.n_heads + h] = (W > 0.f) ? M + logf(W) : -INFINITY;
 }
 
 }  // namespace wl

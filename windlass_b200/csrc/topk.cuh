@@ -29,10 +29,11 @@ __device__ __forceinline__ uint32_t ordered_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Exclusive scan over the block (blockDim.x == 1024). Returns the exclusive
-// prefix of `v`; *total gets the block sum. `sh` holds >= 33 words.
+// Exclusive scan over the block (blockDim.x a multiple of 32, <= 1024).
+// Returns the exclusive prefix of `v`; *total gets the block sum. `sh` holds
+// >= 33 words.
 __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* sh, uint32_t* total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint32_t x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -42,7 +43,7 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* sh, ui
     if (lane == 31) sh[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        const uint32_t w = sh[lane];
+        const uint32_t w = lane < nw ? sh[lane] : 0u;
         uint32_t z = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -59,6 +60,119 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* sh, ui
     return r;
 }
 
+// Find the bin b (scanning from the top) where the running count crosses
+// `need`: count(bins > b) < need <= count(bins >= b). Every thread returns
+// (b, count(bins > b)). Two levels, bank-conflict free: warps sum groups of 32
+// bins (coalesced reads; `h` may be global or shared), warp 0 scans the group
+// sums from the top and then the 32 bins of the crossing group.
+// nb a multiple of 32 and <= 32 * 1024; `coarse` holds nb / 32 words.
+__device__ __forceinline__ void find_bin_from_top(const uint32_t* h, int nb, uint32_t need, uint32_t* coarse,
+                                                  uint32_t* sel, uint32_t* out_bin, uint32_t* out_above) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int ng = nb >> 5;
+    for (int g = warp; g < ng; g += nw) {
+        uint32_t v = h[g * 32 + lane];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) coarse[g] = v;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int per = (ng + 31) >> 5;  // consecutive groups (from the top) per lane
+        uint32_t mine = 0;
+        for (int j = 0; j < per; ++j) {
+            const int jj = (j + lane) % per;  // rotated reads
+            const int g = ng - 1 - (lane * per + jj);
+            if (g >= 0) mine += coarse[g];
+        }
+        uint32_t incl = mine;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint32_t excl = incl - mine;
+        const unsigned who = __ballot_sync(0xffffffffu, excl < need && need <= incl);
+        const int src = __ffs(who) - 1;
+        int gsel = 0;
+        uint32_t above_g = 0;
+        if (lane == src) {
+            uint32_t run = excl;
+            for (int j = 0; j < per; ++j) {
+                const int g = ng - 1 - (lane * per + j);
+                if (g < 0) break;
+                const uint32_t c = coarse[g];
+                if (run < need && need <= run + c) {
+                    gsel = g;
+                    above_g = run;
+                    break;
+                }
+                run += c;
+            }
+        }
+        gsel = __shfl_sync(0xffffffffu, gsel, src);
+        above_g = __shfl_sync(0xffffffffu, above_g, src);
+        // bins of the group from the top: lane l holds bin gsel*32 + 31 - l
+        const uint32_t c = h[gsel * 32 + 31 - lane];
+        uint32_t inc = c;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
+        }
+        const uint32_t ex = above_g + inc - c;
+        const unsigned hit = __ballot_sync(0xffffffffu, ex < need && need <= ex + c);
+        const int l = __ffs(hit) - 1;
+        if (lane == l) {
+            sel[0] = (uint32_t)(gsel * 32 + 31 - l);
+            sel[1] = ex;
+        }
+    }
+    __syncthreads();
+    *out_bin = sel[0];
+    *out_above = sel[1];
+    __syncthreads();
+}
+
+// Writes the selected elements of one row segment in index order: `gt_b0` /
+// `eq_b0` are the counts of keys > thr / == thr before the segment; output
+// position = (#gt before) + min(#eq before, need).
+template <int NT>
+__device__ __forceinline__ void emit_segment(const float* in, const int* cidx, int lo, int hi, uint32_t thr,
+                                             uint32_t need, uint32_t gt_b0, uint32_t eq_b0, uint32_t total_gt,
+                                             int* out, uint32_t* scan_sh) {
+    const int tid = threadIdx.x;
+#pragma unroll 1
+    for (int base = lo; base < hi; base += 4 * NT) {
+        const int i0 = base + tid * 4;
+        uint32_t flags = 0, ngt = 0, neq = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = i0 + j;
+            if (i < hi) {
+                const uint32_t u = ordered_key(in[i]);
+                if (u > thr) { flags |= 1u << (2 * j); ++ngt; }
+                else if (u == thr) { flags |= 2u << (2 * j); ++neq; }
+            }
+        }
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan((neq << 16) | ngt, scan_sh, &tot);
+        uint32_t gt_b = gt_b0 + (ex & 0xffffu);
+        uint32_t eq_b = eq_b0 + (ex >> 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = i0 + j;
+            if (flags & (1u << (2 * j))) {
+                out[gt_b + min(eq_b, need)] = cidx ? cidx[i] : i;
+                ++gt_b;
+            } else if (flags & (2u << (2 * j))) {
+                if (eq_b < need) out[gt_b + eq_b] = cidx ? cidx[i] : i;
+                ++eq_b;
+            }
+        }
+        gt_b0 += tot & 0xffffu;
+        eq_b0 += tot >> 16;
+        if (gt_b0 >= total_gt && eq_b0 >= need) break;  // uniform: nothing left to emit
+    }
+}
+
 struct TopkParams {
     const float* in;
     long long in_stride;
@@ -70,16 +184,21 @@ struct TopkParams {
     int* n_out;  // optional [n_rows]
 };
 
+// One CTA per row. Rows of up to TOPK_SMEM_MAX elements are staged once in
+// shared memory and every pass reads them from there.
+constexpr int TOPK_SMEM_MAX = 40960;
+
 __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(TopkParams p) {
+    extern __shared__ float srow[];
     __shared__ uint32_t hist[2048];
     __shared__ uint32_t scan_sh[33];
-    __shared__ uint32_t sel_bin, sel_above;
+    __shared__ uint32_t coarse[64], sel2[2];
 
     const int r = blockIdx.x, tid = threadIdx.x;
     const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
     const int len = (int)(lraw < p.T ? lraw : p.T);
     const int kk = min(p.k, len);
-    const float* in = p.in + (long long)r * p.in_stride;
+    const float* gin = p.in + (long long)r * p.in_stride;
     const int* cidx = p.cand_idx ? p.cand_idx + (long long)r * p.in_stride : nullptr;
     int* out = p.out + (long long)r * p.out_stride;
     if (p.n_out && tid == 0) p.n_out[r] = kk;
@@ -88,6 +207,12 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(TopkParams p) {
         for (int i = tid; i < len; i += TOPK_THREADS) out[i] = cidx ? cidx[i] : i;
         return;
     }
+    const bool staged = len <= TOPK_SMEM_MAX;
+    if (staged) {
+        for (int i = tid; i < len; i += TOPK_THREADS) srow[i] = gin[i];
+        __syncthreads();
+    }
+    const float* in = staged ? srow : gin;
 
     // ---- radix select: 3 passes, 11/11/10 bits ----
     uint32_t prefix = 0, mask_hi = 0, remaining = (uint32_t)kk;
@@ -102,66 +227,225 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(TopkParams p) {
             if ((u & mask_hi) == prefix) atomicAdd(&hist[(u >> shift) & (uint32_t)(nb - 1)], 1u);
         }
         __syncthreads();
-        // Bins from the top: thread t owns bins nb-1-t*per .. (per bins).
-        const int per = nb / TOPK_THREADS;
-        uint32_t mine = 0;
-        for (int j = 0; j < per; ++j) mine += hist[nb - 1 - tid * per - j];
-        uint32_t tot;
-        uint32_t above = block_excl_scan(mine, scan_sh, &tot);
-        for (int j = 0; j < per; ++j) {
-            const int b = nb - 1 - tid * per - j;
-            const uint32_t c = hist[b];
-            if (above < remaining && remaining <= above + c) {
-                sel_bin = (uint32_t)b;
-                sel_above = above;
-            }
-            above += c;
-        }
-        __syncthreads();
-        prefix |= sel_bin << shift;
+        uint32_t b, above;
+        find_bin_from_top(hist, nb, remaining, coarse, sel2, &b, &above);
+        prefix |= b << shift;
         mask_hi |= (uint32_t)(nb - 1) << shift;
-        remaining -= sel_above;
+        remaining -= above;
+    }
+    // `prefix` is the k-th key; `remaining` (>= 1) keys equal to it are taken.
+    emit_segment<TOPK_THREADS>(in, cidx, 0, len, prefix, remaining, 0, 0, (uint32_t)kk - remaining, out, scan_sh);
+}
+
+// ---- multi-CTA top-k for long rows (decode) -------------------------------------------
+// The first-level histogram (top HBITS bits of every score key) arrives from
+// the indexer's epilogue (or topk_hist_kernel). Then:
+//   partition (C CTAs / row): find the bin b1 that holds the k-th key; count
+//             the keys above it per chunk; append the keys in b1 to a per-row
+//             candidate list (buffered in shared memory, one global
+//             reservation per buffer);
+//   threshold (1 CTA / row):  finish the radix select on the candidates
+//             (remaining 19 bits) -> exact k-th key `thr` and how many keys
+//             equal to it are taken; per-chunk output offsets of the keys
+//             > thr and == thr (exclusive scans over chunks);
+//   emit      (C CTAs / row): rescan each chunk and write its selected keys at
+//             their final positions, ascending.
+constexpr int HBITS = 13;  // first-level histogram: bits 31..19 of the key
+constexpr int HB = 1 << HBITS;
+constexpr int TOPKM_THREADS = 256;
+constexpr int TOPKM_CHUNK_MAX = 4096;   // candidates a partition CTA buffers in shared memory
+constexpr int TOPKM_PART_SMEM = 2 * TOPKM_CHUNK_MAX * 4;
+constexpr int TOPKM_CAND_SMEM = 16384;  // candidates the threshold kernel stages in shared memory
+constexpr int TOPKM_THR_SMEM = (1024 + 2 * TOPKM_CAND_SMEM) * 4;
+
+struct TopkMParams {
+    const float* in;
+    long long in_stride;
+    int n_rows, rows_per_seq, len0, len_step, T, k;
+    int* out;
+    long long out_stride;
+    int* n_out;
+    const unsigned* hist;  // [rows][HB]
+    int chunk, n_chunks;
+    unsigned* cand_key;
+    int* cand_pos;
+    long long cand_stride;
+    unsigned* cand_n;  // [rows], zero on entry
+    unsigned* cnt_gt;  // [rows][n_chunks]
+    unsigned* cnt_eq;  // [rows][n_chunks]
+    unsigned* thr;     // [rows][2]: threshold key, need
+};
+
+__device__ __forceinline__ int topk_row_len(const TopkMParams& p, int r) {
+    const long long l = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
+    return (int)(l < p.T ? l : p.T);
+}
+
+__global__ void __launch_bounds__(TOPKM_THREADS) topk_partition_kernel(TopkMParams p) {
+    extern __shared__ uint32_t dyn[];  // candidate buffer: keys, positions
+    uint32_t* ckey = dyn;
+    int* cpos = reinterpret_cast<int*>(ckey + TOPKM_CHUNK_MAX);
+    __shared__ uint32_t coarse[HB / 32], sel2[2];
+    __shared__ uint32_t warp_gt[TOPKM_THREADS / 32], n_loc, g_base;
+    const int c = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+    const int len = topk_row_len(p, r);
+    const int kk = min(p.k, len);
+    if (kk >= len) return;
+    if (tid == 0) n_loc = 0;
+    uint32_t b1, above;
+    find_bin_from_top(p.hist + (long long)r * HB, HB, (uint32_t)kk, coarse, sel2, &b1, &above);
+    const float* in = p.in + (long long)r * p.in_stride;
+    const int lo = c * p.chunk, hi = min(len, lo + p.chunk);
+    unsigned* gk = p.cand_key + (long long)r * p.cand_stride;
+    int* gp = p.cand_pos + (long long)r * p.cand_stride;
+    uint32_t gt = 0;
+    int iter = 0;
+    for (int base = lo; base < hi; base += TOPKM_THREADS, ++iter) {
+        const int i = base + tid;
+        uint32_t key = 0;
+        bool cand = false;
+        if (i < hi) {
+            key = ordered_key(in[i]);
+            const uint32_t bin = key >> (32 - HBITS);
+            gt += bin > b1;
+            cand = bin == b1;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, cand);
+        if (m) {
+            unsigned wbase = 0;
+            if (lane == 0) wbase = atomicAdd(&n_loc, (unsigned)__popc(m));
+            wbase = __shfl_sync(0xffffffffu, wbase, 0);
+            if (cand) {
+                const unsigned slot = wbase + __popc(m & ((1u << lane) - 1u));
+                ckey[slot] = key;
+                cpos[slot] = i;
+            }
+        }
+        // flush when the buffer may be full, and at the end (uniform condition)
+        if ((iter + 1) % (TOPKM_CHUNK_MAX / TOPKM_THREADS) == 0 || base + TOPKM_THREADS >= hi) {
+            __syncthreads();
+            const unsigned nl = n_loc;
+            if (tid == 0 && nl) g_base = atomicAdd(p.cand_n + r, nl);
+            __syncthreads();
+            for (unsigned j = tid; j < nl; j += TOPKM_THREADS) {
+                gk[g_base + j] = ckey[j];
+                gp[g_base + j] = cpos[j];
+            }
+            __syncthreads();
+            if (tid == 0) n_loc = 0;
+            __syncthreads();
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) gt += __shfl_xor_sync(0xffffffffu, gt, o);
+    if (lane == 0) warp_gt[tid >> 5] = gt;
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t t = 0;
+        for (int w = 0; w < TOPKM_THREADS / 32; ++w) t += warp_gt[w];
+        p.cnt_gt[(long long)r * p.n_chunks + c] = t;
+    }
+}
+
+__global__ void __launch_bounds__(TOPK_THREADS) topk_threshold_kernel(TopkMParams p) {
+    extern __shared__ uint32_t dyn[];  // 1024-bin histogram, then staged candidates
+    uint32_t* h = dyn;
+    uint32_t* sk = dyn + 1024;
+    int* spos = reinterpret_cast<int*>(sk + TOPKM_CAND_SMEM);
+    __shared__ uint32_t scan_sh[33];
+    __shared__ uint32_t coarse[HB / 32], sel2[2];
+    __shared__ uint32_t cg[TOPK_THREADS], ce[TOPK_THREADS];
+    const int r = blockIdx.x, tid = threadIdx.x;
+    const int len = topk_row_len(p, r);
+    const int kk = min(p.k, len);
+    if (kk >= len) return;
+    uint32_t b1, above1;
+    find_bin_from_top(p.hist + (long long)r * HB, HB, (uint32_t)kk, coarse, sel2, &b1, &above1);
+    const unsigned m = p.cand_n[r];
+    const bool staged = m <= (unsigned)TOPKM_CAND_SMEM;
+    const unsigned* ck = staged ? sk : p.cand_key + (long long)r * p.cand_stride;
+    const int* cp = staged ? spos : p.cand_pos + (long long)r * p.cand_stride;
+    if (staged) {
+        const unsigned* gk = p.cand_key + (long long)r * p.cand_stride;
+        const int* gp = p.cand_pos + (long long)r * p.cand_stride;
+        for (unsigned i = tid; i < m; i += TOPK_THREADS) {
+            sk[i] = gk[i];
+            spos[i] = gp[i];
+        }
         __syncthreads();
     }
-    const uint32_t thr = prefix;
-    const uint32_t need = remaining;  // >= 1 elements equal to thr to take
-    const uint32_t total_gt = (uint32_t)kk - need;
-
-    // ---- ordered emission: 4 consecutive elements per thread per round ----
-    uint32_t carry_gt = 0, carry_eq = 0;
+    // Remaining 19 bits in two passes (10 + 9) over the candidates.
+    uint32_t prefix = b1 << (32 - HBITS), mask_hi = ~0u << (32 - HBITS), remaining = (uint32_t)kk - above1;
 #pragma unroll 1
-    for (int base = 0; base < len; base += 4 * TOPK_THREADS) {
-        const int i0 = base + tid * 4;
-        uint32_t flags = 0;  // bit 2j: gt, bit 2j+1: eq
-        uint32_t ngt = 0, neq = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = i0 + j;
-            if (i < len) {
-                const uint32_t u = ordered_key(in[i]);
-                if (u > thr) { flags |= 1u << (2 * j); ++ngt; }
-                else if (u == thr) { flags |= 2u << (2 * j); ++neq; }
-            }
+    for (int pass = 0; pass < 2; ++pass) {
+        const int shift = pass == 0 ? 9 : 0;
+        const int nb = pass == 0 ? 1024 : 512;
+        for (int i = tid; i < 1024; i += TOPK_THREADS) h[i] = 0;
+        __syncthreads();
+        for (unsigned i = tid; i < m; i += TOPK_THREADS) {
+            const uint32_t u = ck[i];
+            if ((u & mask_hi) == prefix) atomicAdd(&h[(u >> shift) & (uint32_t)(nb - 1)], 1u);
         }
-        uint32_t tot;
-        const uint32_t ex = block_excl_scan((neq << 16) | ngt, scan_sh, &tot);
-        uint32_t gt_b = carry_gt + (ex & 0xffffu);
-        uint32_t eq_b = carry_eq + (ex >> 16);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = i0 + j;
-            if (flags & (1u << (2 * j))) {
-                out[gt_b + min(eq_b, need)] = cidx ? cidx[i] : i;
-                ++gt_b;
-            } else if (flags & (2u << (2 * j))) {
-                if (eq_b < need) out[gt_b + eq_b] = cidx ? cidx[i] : i;
-                ++eq_b;
-            }
-        }
-        carry_gt += tot & 0xffffu;
-        carry_eq += tot >> 16;
-        if (carry_gt >= total_gt && carry_eq >= need) break;  // uniform
+        __syncthreads();
+        uint32_t b, above;
+        find_bin_from_top(h, 1024, remaining, coarse, sel2, &b, &above);
+        prefix |= b << shift;
+        mask_hi |= (uint32_t)(nb - 1) << shift;
+        remaining -= above;
     }
+    const uint32_t thr = prefix, need = remaining;
+    // Per-chunk counts of candidate keys > thr and == thr.
+    for (int i = tid; i < p.n_chunks; i += TOPK_THREADS) {
+        cg[i] = 0;
+        ce[i] = 0;
+    }
+    __syncthreads();
+    for (unsigned base = 0; base < m; base += TOPK_THREADS) {
+        const unsigned i = base + tid;
+        int c = -1;
+        uint32_t u = 0;
+        if (i < m) {
+            u = ck[i];
+            c = cp[i] / p.chunk;
+        }
+        // lanes grouped by (chunk, class): one shared atomic per group
+        const int cls = (i < m) ? (u > thr ? 1 : (u == thr ? 2 : 0)) : 0;
+        const unsigned peers = __match_any_sync(0xffffffffu, (c << 2) | cls);
+        if (cls && (tid & 31) == __ffs(peers) - 1) atomicAdd(cls == 1 ? &cg[c] : &ce[c], (unsigned)__popc(peers));
+    }
+    __syncthreads();
+    const int c = tid;
+    const uint32_t g = c < p.n_chunks ? p.cnt_gt[(long long)r * p.n_chunks + c] + cg[c] : 0u;
+    const uint32_t e = c < p.n_chunks ? ce[c] : 0u;
+    uint32_t tot;
+    const uint32_t bg = block_excl_scan(g, scan_sh, &tot);
+    const uint32_t be = block_excl_scan(e, scan_sh, &tot);
+    if (c < p.n_chunks) {
+        p.cnt_gt[(long long)r * p.n_chunks + c] = bg;
+        p.cnt_eq[(long long)r * p.n_chunks + c] = be;
+    }
+    if (tid == 0) {
+        p.thr[2 * r] = thr;
+        p.thr[2 * r + 1] = need;
+    }
+}
+
+__global__ void __launch_bounds__(TOPKM_THREADS) topk_emit_kernel(TopkMParams p) {
+    __shared__ uint32_t scan_sh[33];
+    const int c = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+    const int len = topk_row_len(p, r);
+    const int kk = min(p.k, len);
+    int* out = p.out + (long long)r * p.out_stride;
+    if (c == 0 && tid == 0 && p.n_out) p.n_out[r] = kk;
+    const int lo = c * p.chunk, hi = min(len, lo + p.chunk);
+    if (kk >= len) {
+        for (int i = lo + tid; i < hi; i += TOPKM_THREADS) out[i] = i;
+        return;
+    }
+    if (lo >= hi) return;
+    const float* in = p.in + (long long)r * p.in_stride;
+    const uint32_t thr = p.thr[2 * r], need = p.thr[2 * r + 1];
+    emit_segment<TOPKM_THREADS>(in, nullptr, lo, hi, thr, need, p.cnt_gt[(long long)r * p.n_chunks + c],
+                                p.cnt_eq[(long long)r * p.n_chunks + c], 0xFFFFFFFFu, out, scan_sh);
 }
 
 // ---- normalisation of an arbitrary index list ---------------------------------

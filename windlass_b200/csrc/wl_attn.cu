@@ -45,9 +45,16 @@ bool cfg_supported(const wl_attn_cfg* c) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Per-device one-time kernel attributes (dynamic shared memory opt-in).
+// Per-device one-time kernel attributes (dynamic shared memory opt-in) and SM count.
 std::mutex g_attr_mu;
 bool g_attr_done[kMaxDevices];
+int g_sm_count[kMaxDevices];
+
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+    return g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
+}
 
 int ensure_attrs() {
     int dev = 0;
@@ -63,6 +70,15 @@ int ensure_attrs() {
                                      AttnLayout::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::sel_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      200 * 1024));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::TOPK_SMEM_MAX * 4));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_partition_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::TOPKM_PART_SMEM));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::TOPKM_THR_SMEM));
+    int sms = 0;
+    WL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    g_sm_count[dev] = sms;
     g_attr_done[dev] = true;
     return WL_OK;
 }
@@ -122,11 +138,118 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
     return WL_OK;
 }
 
+// Rows longer than this use the multi-CTA top-k (which needs a workspace).
+constexpr int kTopkMultiMin = wl::TOPK_SMEM_MAX + 1;
+constexpr int kTopkMaxChunks = 1024;
+
+struct TopkWs {
+    unsigned* hist;  // [rows][HB] then cand_n [rows] (one contiguous block, zeroed per call)
+    unsigned* cand_n;
+    unsigned* cand_key;
+    int* cand_pos;
+    unsigned* cnt_gt;
+    unsigned* cnt_eq;
+    unsigned* thr;
+    long long cand_stride;
+};
+
+size_t topk_ws_bytes(int32_t rows, int32_t T) {
+    return align256((size_t)rows * (wl::HB + 1) * 4) + 2 * align256((size_t)rows * T * 4) +
+           2 * align256((size_t)rows * kTopkMaxChunks * 4) + align256((size_t)rows * 8) + 256;
+}
+
+TopkWs topk_ws_carve(void* base, int32_t rows, int32_t T) {
+    TopkWs w{};
+    char* b = static_cast<char*>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        void* p = b + off;
+        off += align256(bytes);
+        return p;
+    };
+    w.hist = static_cast<unsigned*>(take((size_t)rows * (wl::HB + 1) * 4));
+    w.cand_n = w.hist + (size_t)rows * wl::HB;
+    w.cand_key = static_cast<unsigned*>(take((size_t)rows * T * 4));
+    w.cand_pos = static_cast<int*>(take((size_t)rows * T * 4));
+    w.cnt_gt = static_cast<unsigned*>(take((size_t)rows * kTopkMaxChunks * 4));
+    w.cnt_eq = static_cast<unsigned*>(take((size_t)rows * kTopkMaxChunks * 4));
+    w.thr = static_cast<unsigned*>(take((size_t)rows * 8));
+    w.cand_stride = T;
+    return w;
+}
+
+// First-level histogram (top HBITS bits of the score keys) when the indexer
+// did not fuse it.
+__global__ void topk_hist_kernel(const float* in, long long in_stride, int len0, int len_step, int rows_per_seq,
+                                 int T, unsigned* hist) {
+    const int r = blockIdx.y;
+    const long long l = (long long)len0 + (long long)(r % rows_per_seq) * len_step;
+    const int len = (int)(l < T ? l : T);
+    const float* row = in + (long long)r * in_stride;
+    unsigned* hrow = hist + (long long)r * wl::HB;
+    for (long long base = blockIdx.x * (long long)blockDim.x; base < len; base += (long long)gridDim.x * blockDim.x) {
+        const long long i = base + threadIdx.x;
+        const bool valid = i < len;
+        const uint32_t b = valid ? wl::ordered_key(row[i]) >> (32 - wl::HBITS) : 0xFFFFFFFFu;
+        const unsigned peers = __match_any_sync(0xffffffffu, b);
+        if (valid && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(hrow + b, (unsigned)__popc(peers));
+    }
+}
+
+int max_row_len(const wl_rows* rows, int32_t T) {
+    const int last = (rows->rows_per_seq < rows->n_rows ? rows->rows_per_seq : rows->n_rows) - 1;
+    const long long l = (long long)rows->len0 + (long long)last * rows->len_step;
+    return (int)(l < T ? l : T);
+}
+
+// hist_ready: the histogram block of `ws` already holds this call's
+// first-level histogram (fused into the indexer) and cand_n is zero.
 int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, int32_t T, int32_t k,
                 const int32_t* cand_idx, int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
-                cudaStream_t st) {
+                cudaStream_t st, const TopkWs* ws = nullptr, bool hist_ready = false) {
     if (!index || !sel_out || k <= 0) return WL_ERR_ARG;
     if (sel_stride < (k < T ? k : T)) return WL_ERR_ARG;
+    const int lmax = max_row_len(rows, T);
+    if (ws && !cand_idx && lmax >= kTopkMultiMin && rows->n_rows <= 65535) {
+        wl::TopkMParams p{};
+        p.in = index;
+        p.in_stride = index_stride;
+        p.n_rows = rows->n_rows;
+        p.rows_per_seq = rows->rows_per_seq;
+        p.len0 = rows->len0;
+        p.len_step = rows->len_step;
+        p.T = T;
+        p.k = k;
+        p.out = sel_out;
+        p.out_stride = sel_stride;
+        p.n_out = sel_n_out;
+        p.hist = ws->hist;
+        // ~2 waves of 256-thread CTAs over all rows, chunks a multiple of 1024.
+        long long chunk = ceil_div(ceil_div((long long)lmax * rows->n_rows, 2LL * sm_count()), 1024) * 1024;
+        if (chunk < 2048) chunk = 2048;
+        if (ceil_div(lmax, chunk) > kTopkMaxChunks) chunk = ceil_div(ceil_div(lmax, kTopkMaxChunks), 1024) * 1024;
+        p.chunk = (int)chunk;
+        p.n_chunks = (int)ceil_div(lmax, chunk);
+        p.cand_key = ws->cand_key;
+        p.cand_pos = ws->cand_pos;
+        p.cand_stride = ws->cand_stride;
+        p.cand_n = ws->cand_n;
+        p.cnt_gt = ws->cnt_gt;
+        p.cnt_eq = ws->cnt_eq;
+        p.thr = ws->thr;
+        if (!hist_ready) {
+            WL_CUDA_TRY(cudaMemsetAsync(ws->hist, 0, (size_t)rows->n_rows * (wl::HB + 1) * 4, st));
+            topk_hist_kernel<<<dim3((unsigned)ceil_div(lmax, 8192), rows->n_rows), 256, 0, st>>>(
+                index, index_stride, rows->len0, rows->len_step, rows->rows_per_seq, T, ws->hist);
+            WL_CUDA_TRY(cudaGetLastError());
+        }
+        const dim3 g(p.n_chunks, rows->n_rows);
+        wl::topk_partition_kernel<<<g, wl::TOPKM_THREADS, wl::TOPKM_PART_SMEM, st>>>(p);
+        wl::topk_threshold_kernel<<<rows->n_rows, wl::TOPK_THREADS, wl::TOPKM_THR_SMEM, st>>>(p);
+        wl::topk_emit_kernel<<<g, wl::TOPKM_THREADS, 0, st>>>(p);
+        WL_CUDA_TRY(cudaGetLastError());
+        return WL_OK;
+    }
     wl::TopkParams p{};
     p.in = index;
     p.in_stride = index_stride;
@@ -140,7 +263,8 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
     p.out = sel_out;
     p.out_stride = sel_stride;
     p.n_out = sel_n_out;
-    wl::topk_kernel<<<rows->n_rows, wl::TOPK_THREADS, 0, st>>>(p);
+    const size_t smem = lmax <= wl::TOPK_SMEM_MAX ? (size_t)lmax * 4 : 0;
+    wl::topk_kernel<<<rows->n_rows, wl::TOPK_THREADS, smem, st>>>(p);
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
@@ -215,10 +339,12 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
 int launch_merge(const float* o_part, const float* lse_part, int32_t n_rows, int32_t n_parts, int64_t row_stride,
                  int64_t part_stride, int64_t lse_row_stride, int64_t lse_part_stride, int32_t n_heads,
                  int32_t dv, float* ctx, float* lse, cudaStream_t st) {
-    if (!o_part || !lse_part || !ctx || n_rows <= 0 || n_parts <= 0 || (dv & 3) || n_heads <= 0) return WL_ERR_ARG;
+    if (!o_part || !lse_part || !ctx || n_rows <= 0 || n_parts <= 0 || n_parts > 32 || (dv % 128) ||
+        n_heads <= 0 || n_rows > 65535)
+        return WL_ERR_ARG;
     wl::MergeParams p{o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
                       lse_part_stride, n_heads, dv, ctx, lse};
-    wl::lse_merge_kernel<<<dim3(n_heads, n_rows), 128, 0, st>>>(p);
+    wl::lse_merge_kernel<<<dim3(n_heads, dv / 128, n_rows), 32, 0, st>>>(p);
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
@@ -240,6 +366,7 @@ struct DecodeWs {
     int32_t* cand_idx_rows;
     float* part_send;
     float* part_recv;
+    TopkWs topk;
     size_t bytes;
 };
 
@@ -259,6 +386,10 @@ DecodeWs carve_decode(void* base, const wl_attn_cfg* cfg, int32_t T_max, int32_t
     w.o_part = static_cast<float*>(take((size_t)batch * kMaxSplits * wl::AT_H * wl::AT_DV * 4));
     w.lse_part = static_cast<float*>(take((size_t)batch * kMaxSplits * wl::AT_H * 4));
     w.lse_tmp = static_cast<float*>(take((size_t)batch * wl::AT_H * 4));
+    {
+        void* tb = take(topk_ws_bytes(batch, T_max));
+        if (base) w.topk = topk_ws_carve(tb, batch, T_max);
+    }
     if (nranks > 1) {
         w.cand_score = static_cast<float*>(take((size_t)batch * k * 4));
         w.cand_idx = static_cast<int32_t*>(take((size_t)batch * k * 4));
@@ -440,13 +571,22 @@ int wl_indexer_scores(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32
                           static_cast<cudaStream_t>(stream));
 }
 
+size_t wl_indexer_topk_workspace_bytes(int32_t n_rows, int32_t T) {
+    if (n_rows <= 0 || T <= 0) return 0;
+    return topk_ws_bytes(n_rows, T);
+}
+
 int wl_indexer_topk(const float* index, int64_t index_stride, const wl_rows* rows, int32_t T, int32_t k,
                     const int32_t* cand_idx, int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
-                    void* stream) {
+                    void* workspace, size_t workspace_bytes, void* stream) {
     if (int e = rows_ok(rows, T)) return e;
     if (index_stride < T) return WL_ERR_ARG;
+    if (int e = ensure_attrs()) return e;
+    TopkWs ws{};
+    const bool use_ws = workspace && workspace_bytes >= topk_ws_bytes(rows->n_rows, T);
+    if (use_ws) ws = topk_ws_carve(align_base(workspace), rows->n_rows, T);
     return launch_topk(index, index_stride, rows, T, k, cand_idx, sel_out, sel_stride, sel_n_out,
-                       static_cast<cudaStream_t>(stream));
+                       static_cast<cudaStream_t>(stream), use_ws ? &ws : nullptr, false);
 }
 
 int wl_sel_normalize(const int32_t* sel_in, int64_t in_stride, const int32_t* n_in_dev, int32_t n_in,
@@ -515,7 +655,8 @@ static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, co
         const int64_t ostride = io->sel_out ? io->sel_stride : kk;
         if (io->sel_out && io->sel_stride < kk) return WL_ERR_ARG;
         int32_t* n_out = io->sel_n_out ? io->sel_n_out : w.cnt;
-        if (int e = launch_topk(index, istride, &rows, T, cfg->index_topk, nullptr, out, ostride, n_out, st)) return e;
+        if (int e = launch_topk(index, istride, &rows, T, cfg->index_topk, nullptr, out, ostride, n_out, st, &w.topk))
+            return e;
         *sel = out;
         *cnt = n_out;
         *stride = ostride;
@@ -743,7 +884,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         float* index = w.index;
         if (int e = launch_indexer(cfg, &io->index, T, &lrows, io->q_idx, io->w_idx, index, T, st)) return e;
         const int32_t kl = k < T ? k : T;
-        if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st)) return e;
+        if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st, &w.topk)) return e;
         gather_candidates_kernel<<<dim3((unsigned)ceil_div(k, 256), B), 256, 0, st>>>(index, T, w.sel, kl, w.cnt, k, t0,
                                                                                      w.cand_score, w.cand_idx);
         WL_CUDA_TRY(cudaGetLastError());
