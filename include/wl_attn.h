@@ -283,6 +283,17 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io,
                            const wl_shard* shard, wl_comm* comm,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode attention (consumer with a canonical list, or dense) for callers
+ * that cannot allocate device memory: no workspace argument, no allocation.
+ * No counterpart in the reference. Its split-K scratch is a fixed array
+ * inside the library (about 8.4 MB on every GPU that loads it, for at most 4
+ * sequences per call); larger batches return WL_ERR_WORKSPACE, owner mode
+ * and non-canonical lists WL_ERR_UNSUPPORTED. The first call on a device
+ * looks up the array's device address, so make that first call before any
+ * stream capture. All calls share the array: calls that overlap on the GPU
+ * (different streams, or different host threads) race and must not. */
+int wl_attn_decode_noalloc(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, void* stream);
+
 /* ---- diagnostics ------------------------------------------------------------ */
 /* Device-side error word of the calling thread's current device: bounds-check
  * failures and bounded-wait timeouts of any kernel of this library set it.

@@ -101,6 +101,7 @@ SIGNATURES = {
     "wl_attn_decode_sharded": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(DecodeIO),
                                          C.POINTER(Shard), vp, vp, C.c_size_t, vp]),
     "wl_device_error": (C.c_int, [i32, C.POINTER(u32)]),
+    "wl_attn_decode_noalloc": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(DecodeIO), vp]),
 }
 
 _lib = None

@@ -952,6 +952,66 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
                         (int64_t)B * rowsz, wl::AT_H, wl::AT_DV, io->ctx, lse, st);
 }
 
+// ---- decode attention without any allocation ------------------------------------------
+// For callers that cannot allocate device memory at all (for example code that
+// runs where cudaMalloc is not allowed, or an embedding runtime that owns every
+// allocation and hands out only input/output buffers): the split-K partials of
+// the decode attention live in this fixed array instead of a caller workspace.
+// Every GPU that loads the library holds it until the process exits.
+constexpr int kNoAllocMaxRows = 4;
+constexpr size_t kNoAllocPartFloats = (size_t)kNoAllocMaxRows * kMaxSplits * wl::AT_H * wl::AT_DV;
+constexpr size_t kNoAllocLseFloats = (size_t)kNoAllocMaxRows * kMaxSplits * wl::AT_H;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocPartFloats + kNoAllocLseFloats +
+                                                         (size_t)kNoAllocMaxRows * wl::AT_H];
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[kMaxDevices];
+
+int wl_attn_decode_noalloc(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, void* stream) {
+    if (int e = check_decode_io(cfg, io)) return e;
+    if (io->mode == WL_MODE_OWNER) return WL_ERR_UNSUPPORTED;  // the indexer and top-k need T-sized scratch
+    if (io->mode == WL_MODE_CONSUMER && !(io->sel_flags & WL_SEL_CANONICAL)) return WL_ERR_UNSUPPORTED;
+    if (io->batch > kNoAllocMaxRows) {
+        std::fprintf(stderr, "wl_attn_decode_noalloc: batch %d exceeds the fixed scratch's maximum of %d rows\n",
+                     io->batch, kNoAllocMaxRows);
+        return WL_ERR_WORKSPACE;
+    }
+    if (int e = ensure_attrs()) return e;
+    int dev = 0;
+    WL_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return WL_ERR_CUDA;
+    float* base = nullptr;
+    {
+        // First call on this device: resolve the array's device address (the
+        // host-side name is only a stand-in). Later calls reuse it.
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* p = nullptr;
+            WL_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            g_noalloc_ptr[dev] = static_cast<float*>(p);
+        }
+        base = g_noalloc_ptr[dev];
+    }
+    // Every partial slot the attention kernel may touch is written by it
+    // (empty splits write zeros and -inf), so nothing needs clearing.
+    DecodeWs w{};
+    w.o_part = base;
+    w.lse_part = base + kNoAllocPartFloats;
+    w.lse_tmp = base + kNoAllocPartFloats + kNoAllocLseFloats;
+    long long n_max = io->T;
+    int32_t sel_n = 0;
+    const int32_t* sel = nullptr;
+    int64_t stride = 0;
+    if (io->mode == WL_MODE_CONSUMER) {
+        sel = io->sel_in;
+        stride = io->sel_stride;
+        n_max = io->sel_n_in ? io->sel_stride : io->sel_n;
+        sel_n = io->sel_n;
+    }
+    float* lse = io->lse ? io->lse : w.lse_tmp;
+    return decode_local(cfg, io, w, 0, io->T, io->ctx, lse, sel, io->sel_n_in, sel_n, stride, n_max,
+                        static_cast<cudaStream_t>(stream));
+}
+
 // ---- diagnostics ---------------------------------------------------------------------------
 int wl_device_error(int32_t clear, uint32_t* detail) {
     WL_CUDA_TRY(cudaDeviceSynchronize());
