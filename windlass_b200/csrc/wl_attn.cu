@@ -72,6 +72,8 @@ int ensure_attrs() {
                                      200 * 1024));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::TOPK_SMEM_MAX * 4));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::IdxStreamLayout::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_partition_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::TOPKM_PART_SMEM));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -99,7 +101,7 @@ int split_keys_for(long long n) {
 // ---- kernel launchers ----------------------------------------------------------
 int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t T, const wl_rows* rows,
                    const void* q_idx, const float* w_idx, float* out, int64_t out_stride,
-                   cudaStream_t st) {
+                   cudaStream_t st, unsigned* hist = nullptr) {
     if (!cache || !cache->keys || !cache->scale || !q_idx || !w_idx || !out) return WL_ERR_ARG;
     if (!aligned16(cache->keys) || !aligned16(q_idx) || (cache->keys_seq_stride & 15)) return WL_ERR_ARG;
     if (out_stride < T) return WL_ERR_ARG;
@@ -118,6 +120,7 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
     p.out = out;
     p.out_stride = out_stride;
     p.qk_scale = cfg->idx_qk_scale;
+    p.scale_bulk = aligned16(cache->scale) && ((cache->scale_seq_stride * 4) % 16 == 0);
     const int ntiles = (int)ceil_div(T, wl::IDX_TILE);
     if (rows->rows_per_seq >= rows->n_rows && rows->n_rows >= 8) {
         // Many rows over one shared cache (prefill): 8 rows (N = 256) per MMA.
@@ -128,11 +131,15 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
         dim3 grid(ntiles, (unsigned)ceil_div(n_groups, gpc));
         wl::indexer_scores_kernel<8><<<grid, 128, wl::IdxLayout<8>::BYTES, st>>>(p);
     } else {
-        // One row per group; rows of different sequences never share a CTA.
-        p.groups_per_cta = 1;
+        // Decode: each row streams its own cache; at most one CTA per SM in
+        // total, each over a contiguous range of tiles.
         if (rows->n_rows > 65535) return WL_ERR_ARG;
-        dim3 grid(ntiles, rows->n_rows);
-        wl::indexer_scores_kernel<1><<<grid, 128, wl::IdxLayout<1>::BYTES, st>>>(p);
+        int cpr = sm_count() / rows->n_rows;
+        if (cpr < 1) cpr = 1;
+        if (cpr > ntiles) cpr = ntiles;
+        const int tpc = (int)ceil_div(ntiles, cpr);
+        dim3 grid((unsigned)ceil_div(ntiles, tpc), rows->n_rows);
+        wl::indexer_stream_kernel<<<grid, wl::IDX_STREAM_THREADS, wl::IdxStreamLayout::BYTES, st>>>(p, hist, tpc);
     }
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
@@ -141,6 +148,7 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
 // Rows longer than this use the multi-CTA top-k (which needs a workspace).
 constexpr int kTopkMultiMin = wl::TOPK_SMEM_MAX + 1;
 constexpr int kTopkMaxChunks = 1024;
+static_assert(wl::TOPK_HIST_BITS == wl::HBITS, "indexer-fused histogram and top-k agree on bits");
 
 struct TopkWs {
     unsigned* hist;  // [rows][HB] then cand_n [rows] (one contiguous block, zeroed per call)
@@ -649,13 +657,18 @@ static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, co
     if (io->mode == WL_MODE_OWNER) {
         float* index = io->index_out ? io->index_out : w.index;
         const int64_t istride = io->index_out ? io->index_stride : T;
-        if (int e = launch_indexer(cfg, &io->index, T, &rows, io->q_idx, io->w_idx, index, istride, st)) return e;
+        const bool fuse = T >= kTopkMultiMin && cfg->index_topk < T;
+        if (fuse) WL_CUDA_TRY(cudaMemsetAsync(w.topk.hist, 0, (size_t)B * (wl::HB + 1) * 4, st));
+        if (int e = launch_indexer(cfg, &io->index, T, &rows, io->q_idx, io->w_idx, index, istride, st,
+                                   fuse ? w.topk.hist : nullptr))
+            return e;
         const int32_t kk = cfg->index_topk < T ? cfg->index_topk : T;
         int32_t* out = io->sel_out ? io->sel_out : w.sel;
         const int64_t ostride = io->sel_out ? io->sel_stride : kk;
         if (io->sel_out && io->sel_stride < kk) return WL_ERR_ARG;
         int32_t* n_out = io->sel_n_out ? io->sel_n_out : w.cnt;
-        if (int e = launch_topk(index, istride, &rows, T, cfg->index_topk, nullptr, out, ostride, n_out, st, &w.topk))
+        if (int e = launch_topk(index, istride, &rows, T, cfg->index_topk, nullptr, out, ostride, n_out, st, &w.topk,
+                                fuse))
             return e;
         *sel = out;
         *cnt = n_out;
@@ -882,9 +895,13 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         if (!io->sel_out || !io->sel_n_out || io->sel_stride < kg) return WL_ERR_ARG;
         const wl_rows lrows{B, 1, T, 0};
         float* index = w.index;
-        if (int e = launch_indexer(cfg, &io->index, T, &lrows, io->q_idx, io->w_idx, index, T, st)) return e;
+        const bool fuse = T >= kTopkMultiMin && k < T;
+        if (fuse) WL_CUDA_TRY(cudaMemsetAsync(w.topk.hist, 0, (size_t)B * (wl::HB + 1) * 4, st));
+        if (int e = launch_indexer(cfg, &io->index, T, &lrows, io->q_idx, io->w_idx, index, T, st,
+                                   fuse ? w.topk.hist : nullptr))
+            return e;
         const int32_t kl = k < T ? k : T;
-        if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st, &w.topk)) return e;
+        if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st, &w.topk, fuse)) return e;
         gather_candidates_kernel<<<dim3((unsigned)ceil_div(k, 256), B), 256, 0, st>>>(index, T, w.sel, kl, w.cnt, k, t0,
                                                                                      w.cand_score, w.cand_idx);
         WL_CUDA_TRY(cudaGetLastError());
@@ -951,6 +968,12 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     return launch_merge(w.part_recv, w.part_recv + wl::AT_H * wl::AT_DV, B, N, rowsz, (int64_t)B * rowsz, rowsz,
                         (int64_t)B * rowsz, wl::AT_H, wl::AT_DV, io->ctx, lse, st);
 }
+
+#ifdef WL_TRACE
+int wl_trace_set(long long* buf) {
+    return cudaMemcpyToSymbol(wl::g_trace, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
+}
+#endif
 
 // ---- decode attention without any allocation ------------------------------------------
 // For callers that cannot allocate device memory at all (for example code that
