@@ -376,10 +376,16 @@ def main():
             "extras": extras,
         }
         print(json.dumps(line), flush=True)
-    if comm is not None:
-        comm.close()
     if world > 1:
-        dist.destroy_process_group()
+        # Multi-rank teardown: graphs that captured NCCL work keep the
+        # communicator referenced, and destroying it (or the process group)
+        # under them can block. Everything is printed and synchronised, so the
+        # ranks leave directly after a final barrier.
+        torch.cuda.synchronize()
+        dist.barrier()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 def load_peaks():
