@@ -425,15 +425,26 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
     const int c = q * 128 + lane * 4;
     const float* base = p.o_part + (long long)r * p.row_stride + (long long)h * p.dv + c;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int s = 0; s < p.n_parts; ++s) {
-        const float w = __shfl_sync(0xffffffffu, wl, s) * inv;
-        if (w == 0.f) continue;  // uniform: empty parts are never read
-        const float4 v = *reinterpret_cast<const float4*>(base + (long long)s * p.part_stride);
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
+    // Parts in groups of 8: all loads of a group are issued before any use.
+    for (int s0 = 0; s0 < p.n_parts; s0 += 8) {
+        float4 v[8];
+        float wv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int s = s0 + j;
+            wv[j] = __shfl_sync(0xffffffffu, wl, s & 31) * inv;
+            const bool use = s < p.n_parts && wv[j] != 0.f;  // empty parts are never read
+            v[j] = use ? *reinterpret_cast<const float4*>(base + (long long)s * p.part_stride)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (!use) wv[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            acc.x = fmaf(wv[j], v[j].x, acc.x);
+            acc.y = fmaf(wv[j], v[j].y, acc.y);
+            acc.z = fmaf(wv[j], v[j].z, acc.z);
+            acc.w = fmaf(wv[j], v[j].w, acc.w);
+        }
     }
     *reinterpret_cast<float4*>(p.ctx + ((long long)r * p.n_heads + h) * p.dv + c) = acc;
     if (q == 0 && lane == 0 && p.lse)

@@ -299,42 +299,52 @@ __global__ void __launch_bounds__(TOPKM_THREADS) topk_partition_kernel(TopkMPara
     unsigned* gk = p.cand_key + (long long)r * p.cand_stride;
     int* gp = p.cand_pos + (long long)r * p.cand_stride;
     uint32_t gt = 0;
-    int iter = 0;
-    for (int base = lo; base < hi; base += TOPKM_THREADS, ++iter) {
-        const int i = base + tid;
-        uint32_t key = 0;
-        bool cand = false;
-        if (i < hi) {
-            key = ordered_key(in[i]);
-            const uint32_t bin = key >> (32 - HBITS);
-            gt += bin > b1;
-            cand = bin == b1;
+    // Rounds of TOPKM_CHUNK_MAX elements: 16 independent loads per thread
+    // first, then classification and candidate appends; a round can fill the
+    // shared buffer at most once, so each round ends with one flush.
+    constexpr int PER = TOPKM_CHUNK_MAX / TOPKM_THREADS;
+#pragma unroll 1
+    for (int base = lo; base < hi; base += TOPKM_CHUNK_MAX) {
+        float x[PER];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int i = base + j * TOPKM_THREADS + tid;
+            x[j] = i < hi ? in[i] : 0.f;
         }
-        const unsigned m = __ballot_sync(0xffffffffu, cand);
-        if (m) {
-            unsigned wbase = 0;
-            if (lane == 0) wbase = atomicAdd(&n_loc, (unsigned)__popc(m));
-            wbase = __shfl_sync(0xffffffffu, wbase, 0);
-            if (cand) {
-                const unsigned slot = wbase + __popc(m & ((1u << lane) - 1u));
-                ckey[slot] = key;
-                cpos[slot] = i;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int i = base + j * TOPKM_THREADS + tid;
+            uint32_t key = 0;
+            bool cand = false;
+            if (i < hi) {
+                key = ordered_key(x[j]);
+                const uint32_t bin = key >> (32 - HBITS);
+                gt += bin > b1;
+                cand = bin == b1;
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, cand);
+            if (m) {
+                unsigned wbase = 0;
+                if (lane == 0) wbase = atomicAdd(&n_loc, (unsigned)__popc(m));
+                wbase = __shfl_sync(0xffffffffu, wbase, 0);
+                if (cand) {
+                    const unsigned slot = wbase + __popc(m & ((1u << lane) - 1u));
+                    ckey[slot] = key;
+                    cpos[slot] = i;
+                }
             }
         }
-        // flush when the buffer may be full, and at the end (uniform condition)
-        if ((iter + 1) % (TOPKM_CHUNK_MAX / TOPKM_THREADS) == 0 || base + TOPKM_THREADS >= hi) {
-            __syncthreads();
-            const unsigned nl = n_loc;
-            if (tid == 0 && nl) g_base = atomicAdd(p.cand_n + r, nl);
-            __syncthreads();
-            for (unsigned j = tid; j < nl; j += TOPKM_THREADS) {
-                gk[g_base + j] = ckey[j];
-                gp[g_base + j] = cpos[j];
-            }
-            __syncthreads();
-            if (tid == 0) n_loc = 0;
-            __syncthreads();
+        __syncthreads();
+        const unsigned nl = n_loc;
+        if (tid == 0 && nl) g_base = atomicAdd(p.cand_n + r, nl);
+        __syncthreads();
+        for (unsigned j = tid; j < nl; j += TOPKM_THREADS) {
+            gk[g_base + j] = ckey[j];
+            gp[g_base + j] = cpos[j];
         }
+        __syncthreads();
+        if (tid == 0) n_loc = 0;
+        __syncthreads();
     }
     for (int o = 16; o > 0; o >>= 1) gt += __shfl_xor_sync(0xffffffffu, gt, o);
     if (lane == 0) warp_gt[tid >> 5] = gt;
