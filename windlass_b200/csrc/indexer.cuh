@@ -203,62 +203,49 @@ __global__ void __launch_bounds__(128) indexer_scores_kernel(IdxParams p) {
 
 namespace wl {
 
-// ---- decode form: persistent, warp-specialised ------------------------------------------
+// ---- decode form: persistent, warp-specialised, fp8 tensor cores ---------------------------
 // One CTA per SM streams a contiguous range of 128-key tiles of one row's
-// cache. Roles (14 warps), connected by mbarriers only — no block-wide barrier
-// in the tile loop, so each role runs at its own rate:
-//   warp 0       TMA producer: fp8 keys + scales of tile i into ring stage i % IDX_NS
-//   warp 1       MMA issuer:   tcgen05.mma (M = 128 keys, N = 32 heads, K = 128) into
-//                              accumulator set i % IDX_NACC; the 8 K-steps go to
-//                              IDX_KSPLIT independent accumulators so the tensor pipe
-//                              overlaps them instead of chaining them on one
-//   warps 2-9    converters:   e4m3 -> fp16 into A tile i % IDX_NA (128B-swizzled, K-major)
-//   warps 10-13  epilogue:     sum the partial accumulators of one key, scale, relu,
-//                              head-weighted sum, store (+ fused histogram)
+// cache. Roles (6 warps), connected by mbarriers only:
+//   warp 0      TMA producer: the tile's fp8 keys as one 128 x 128-byte box with
+//               128B swizzle (a tensor-map load; rows past the cache end read as
+//               zero) plus its scales (bulk copy) into ring stage i % IDX_NS
+//   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4 straight on the fp8 keys
+//               (M = 128 keys, N = 32 heads, K = 32 per instruction), two chains
+//               per tile — the query's hi and lo e4m3 terms — into TMEM
+//   warps 2-5   epilogue:     tcgen05.ld both chains of one key, combine, scale,
+//               relu, head-weighted sum, store (+ fused top-k histogram)
 //
-// Operand types: tcgen05 kind::f16 with fp16 A and B. A key is widened to fp16
-// holding e4m3 * 2^-8 by bit placement alone (exact for every finite code; the
-// 2^8 goes into the per-key scale). The bf16 query is scaled per head by a power
-// of two (its largest element lands in [2^14, 2^15)) and converted to fp16 —
-// exact for every element the scale keeps in fp16's normal range, i.e. all but
-// those below 2^-28 of the head's largest, whose contribution is far below fp32
-// rounding of the dot product. The scale is undone in the head weight:
-// w_h * relu(x / s_h) = (w_h / s_h) * relu(x) for s_h > 0, exact for a power of two.
+// The query in e4m3: per head, q * s_h (s_h a power of two putting the head's
+// largest element in [128, 256)) = hi + lo / 32 with hi = e4m3(q s_h) and
+// lo = e4m3((q s_h - hi) * 32). Every bf16 element is reproduced to within
+// 2^-22 of the head's largest element (exactly for all but elements more than
+// ~2^-14 below it), far inside fp32 rounding of the 128-term dot product. The
+// head weight absorbs 1/s_h: w_h relu(x / s_h) = (w_h / s_h) relu(x), s_h > 0.
 //
 // The epilogue can also accumulate, per row, the histogram of the top
 // TOPK_HIST_BITS bits of the order-preserving score keys (warp-aggregated
 // global atomics) — the first radix pass of the top-k, fused here so that no
 // kernel re-reads the scores for it.
-constexpr int IDX_NS = 4;      // TMA stages
-constexpr int IDX_NA = 2;      // fp16 A tiles
-constexpr int IDX_NACC = 4;    // accumulator sets in flight
-constexpr int IDX_KSPLIT = 4;  // independent partial accumulators per tile
-constexpr int IDX_STREAM_THREADS = 448;
-constexpr int IDX_CONV = 256;  // converter threads
-// Scale rows in flight between a converter writing tile i and the epilogue of
-// tile i reading it: converters lead the MMA by at most IDX_NA tiles and the
-// MMA leads the epilogue by at most IDX_NACC.
-constexpr int IDX_NSC = IDX_NA + IDX_NACC + 1;
+constexpr int IDX_NS = 8;    // TMA stages (keys + scales)
+constexpr int IDX_NACC = 4;  // accumulator sets (hi, lo) in flight
+constexpr int IDX_STREAM_THREADS = 192;
 constexpr int TOPK_HIST_BITS = 13;
 constexpr int TOPK_HIST_BINS = 1 << TOPK_HIST_BITS;
 
 struct IdxStreamLayout {
-    static constexpr uint32_t A_TILE = IDX_TILE * IDX_D * 2;   // 32 KB
-    static constexpr uint32_t A_CHUNK = IDX_TILE * 128;
-    static constexpr uint32_t Q_CHUNK = IDX_H * 128;           // 4 KB
-    static constexpr uint32_t K8_TILE = IDX_TILE * IDX_D;      // 16 KB
-    static constexpr uint32_t STAGE = K8_TILE + IDX_TILE * 4;  // + the tile's scales
-    static constexpr uint32_t OFF_A = 0;
-    static constexpr uint32_t OFF_Q = OFF_A + IDX_NA * A_TILE;
-    static constexpr uint32_t OFF_K8 = OFF_Q + 2 * Q_CHUNK;
-    static constexpr uint32_t OFF_W = OFF_K8 + IDX_NS * STAGE;
-    static constexpr uint32_t OFF_SC = OFF_W + IDX_H * 4;  // [IDX_NSC][128] scale * qk_scale * 2^8
-    static constexpr uint32_t OFF_BAR = OFF_SC + IDX_NSC * IDX_TILE * 4;
-    static constexpr int N_BARS = 2 * IDX_NS + 2 * IDX_NA + 2 * IDX_NACC;
+    static constexpr uint32_t K8_TILE = IDX_TILE * IDX_D;  // 16 KB, 128B-swizzled (1024-aligned)
+    static constexpr uint32_t QT = IDX_H * IDX_D;          // one e4m3 query term, 4 KB
+    static constexpr uint32_t OFF_K8 = 0;
+    static constexpr uint32_t OFF_Q = OFF_K8 + IDX_NS * K8_TILE;  // hi, lo
+    static constexpr uint32_t OFF_SC = OFF_Q + 2 * QT;             // [IDX_NS][128] scales
+    static constexpr uint32_t OFF_W = OFF_SC + IDX_NS * IDX_TILE * 4;
+    static constexpr uint32_t OFF_BAR = OFF_W + IDX_H * 4;
+    static constexpr int N_BARS = 2 * IDX_NS + 2 * IDX_NACC;  // full, empty, acc_full, acc_empty
     static constexpr uint32_t OFF_SLOT = OFF_BAR + N_BARS * 8;
     static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;
-    static constexpr uint32_t TMEM_COLS = 32 * IDX_KSPLIT * IDX_NACC;  // 512
-    static constexpr uint32_t IDESC = idesc_f16(128, IDX_H);
+    static constexpr uint32_t TMEM_COLS = 64 * IDX_NACC;  // 256
+    // kind::f8f6f4: E4M3 A and B (format 0), fp32 D; M = 128, N = 32
+    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(IDX_H >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 };
 
 __device__ __forceinline__ uint32_t score_key(float f) {
@@ -267,18 +254,30 @@ __device__ __forceinline__ uint32_t score_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Four e4m3 codes (one word) -> four fp16 (two words) holding e4m3 * 2^-8,
-// exactly, by bit placement alone: the fp16 pattern (b & 0x80) << 8 |
-// (b & 0x7F) << 7 puts e4m3's sign, 4 exponent and 3 mantissa bits into
-// fp16's fields, which is the e4m3 value times 2^(7-15) for normal codes and,
-// because 2^-8 also maps e4m3 subnormals (m * 2^-9) onto fp16 subnormals
-// ((m << 7) * 2^-24), for every finite code. NaN codes are not valid keys.
-__device__ __forceinline__ void e4m3x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    const uint32_t x01 = __byte_perm(w, 0u, 0x4140);  // [b0, 0, b1, 0]
-    const uint32_t x23 = __byte_perm(w, 0u, 0x4342);  // [b2, 0, b3, 0]
-    lo = ((x01 << 7) & 0x3F803F80u) | ((x01 << 8) & 0x80008000u);
-    hi = ((x23 << 7) & 0x3F803F80u) | ((x23 << 8) & 0x80008000u);
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
+
+__device__ __forceinline__ void tma_load3d(void* dst, const CUtensorMap* tm, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// The key cache as a uint8 tensor {128 bytes, T keys, sequences} (strides
+// 128 and keys_seq bytes), loaded in {128, 128, 1} boxes with 128B swizzle:
+// key rows at or past T read as zero.
+struct IdxStreamParams {
+    CUtensorMap tm_keys;
+};
 
 #ifdef WL_TRACE
 __device__ long long* g_trace;
@@ -293,20 +292,17 @@ __device__ long long* g_trace;
 #endif
 
 __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
-    indexer_stream_kernel(IdxParams p, unsigned* hist, int tiles_per_cta) {
+    indexer_stream_kernel(IdxParams p, const __grid_constant__ IdxStreamParams sp, unsigned* hist, int tiles_per_cta) {
     using L = IdxStreamLayout;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t sA = smem_u32(smem + L::OFF_A);
-    const uint32_t sQ = smem_u32(smem + L::OFF_Q);
     uint8_t* k8 = smem + L::OFF_K8;
+    uint8_t* sQ = smem + L::OFF_Q;
     float* sW = reinterpret_cast<float*>(smem + L::OFF_W);
-    float* sc_s = reinterpret_cast<float*>(smem + L::OFF_SC);
+    float* sSc = reinterpret_cast<float*>(smem + L::OFF_SC);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* empty = full + IDX_NS;
-    uint64_t* a_full = empty + IDX_NS;     // converters -> MMA       (per A tile)
-    uint64_t* a_free = a_full + IDX_NA;    // MMA commit -> converters (per A tile)
-    uint64_t* acc_full = a_free + IDX_NA;  // MMA commit -> epilogue   (per accumulator set)
+    uint64_t* acc_full = empty + IDX_NS;
     uint64_t* acc_empty = acc_full + IDX_NACC;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_SLOT);
 
@@ -318,7 +314,6 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
     const int tb = blockIdx.x * tiles_per_cta;
     const int n = min(tb + tiles_per_cta, ntiles) - tb;
     if (n <= 0) return;
-    const uint8_t* keys = p.keys + (long long)seq * p.keys_seq;
     const float* scale = p.scale + (long long)seq * p.scale_seq;
     float* out = p.out + (long long)r * p.out_stride;
     unsigned* hrow = hist ? hist + (long long)r * TOPK_HIST_BINS : nullptr;
@@ -326,11 +321,7 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < IDX_NS; ++s) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, IDX_CONV);
-        }
-        for (int b = 0; b < IDX_NA; ++b) {
-            mbar_init(a_full + b, IDX_CONV);
-            mbar_init(a_free + b, 1);
+            mbar_init(empty + s, 1 + 128);  // the MMA's commit + the epilogue's scale reads
         }
         for (int b = 0; b < IDX_NACC; ++b) {
             mbar_init(acc_full + b, 1);
@@ -339,7 +330,7 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);  // warp 1 allocates and frees
-    // Query -> fp16 with a per-head power-of-two scale; 14 warps over 32 heads.
+    // Query -> two e4m3 terms per head (6 warps over 32 heads).
     for (int h = warp; h < IDX_H; h += IDX_STREAM_THREADS / 32) {
         const __nv_bfloat16* qh = p.q + ((long long)r * IDX_H + h) * IDX_D;
         float x[4];
@@ -350,16 +341,26 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
             mx = fmaxf(mx, fabsf(x[e]));
         }
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        // 2^(14 - floor(log2 mx)): the largest element lands in [2^14, 2^15).
+        // s_h = 2^(7 - floor(log2 mx)): the largest element lands in [128, 256).
         const int ex = mx > 0.f ? max(((__float_as_int(mx) >> 23) & 0xff) - 127, -100) : 0;
-        const float s_h = __int_as_float((127 + 14 - ex) << 23);
-        const __half2 a = __floats2half2_rn(x[0] * s_h, x[1] * s_h), b = __floats2half2_rn(x[2] * s_h, x[3] * s_h);
-        const uint32_t e0 = (uint32_t)lane * 4u, chunk = e0 >> 6, byte = (e0 & 63u) * 2u;
-        const uint32_t addr = sQ + chunk * L::Q_CHUNK + (uint32_t)h * 128u + ((((byte >> 4) ^ (uint32_t)h) & 7u) << 4) +
-                              (byte & 15u);
-        asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(*reinterpret_cast<const uint32_t*>(&a)),
-                     "r"(*reinterpret_cast<const uint32_t*>(&b))
-                     : "memory");
+        const float s_h = __int_as_float((127 + 7 - ex) << 23);
+        uint32_t hi4 = 0, lo4 = 0;
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+            const float a0 = x[e] * s_h, a1 = x[e + 1] * s_h;
+            const __nv_fp8x2_storage_t h2 = __nv_cvt_float2_to_fp8x2(make_float2(a0, a1), __NV_SATFINITE, __NV_E4M3);
+            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(h2, __NV_E4M3);
+            const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+            const __nv_fp8x2_storage_t l2 =
+                __nv_cvt_float2_to_fp8x2(make_float2((a0 - hf.x) * 32.f, (a1 - hf.y) * 32.f), __NV_SATFINITE, __NV_E4M3);
+            hi4 |= (uint32_t)h2 << (8 * e);
+            lo4 |= (uint32_t)l2 << (8 * e);
+        }
+        // 4 codes = 4 bytes at byte lane*4 of the 128-byte row h, 128B-swizzled
+        const uint32_t byte = (uint32_t)lane * 4u;
+        const uint32_t off = (uint32_t)h * 128u + ((((byte >> 4) ^ (uint32_t)h) & 7u) << 4) + (byte & 15u);
+        *reinterpret_cast<uint32_t*>(sQ + off) = hi4;
+        *reinterpret_cast<uint32_t*>(sQ + L::QT + off) = lo4;
         if (lane == 0) sW[h] = __ldg(p.w + (long long)r * IDX_H + h) / s_h;
     }
     fence_proxy_async_smem();
@@ -379,107 +380,64 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
                 const int t0 = (tb + i) * IDX_TILE;
                 const int nk = min(IDX_TILE, len - t0);
                 const bool sc_bulk = sc_bulk_all && (nk & 3) == 0;
-                mbar_expect_tx(full + s, (uint32_t)nk * IDX_D + (sc_bulk ? (uint32_t)nk * 4u : 0u));
-                bulk_g2s(k8 + s * L::STAGE, keys + (long long)t0 * IDX_D, (uint32_t)nk * IDX_D, full + s);
-                if (sc_bulk) bulk_g2s(k8 + s * L::STAGE + L::K8_TILE, scale + t0, (uint32_t)nk * 4u, full + s);
+                mbar_expect_tx(full + s, L::K8_TILE + (sc_bulk ? (uint32_t)nk * 4u : 0u));
+                tma_load3d(k8 + s * L::K8_TILE, &sp.tm_keys, 0, t0, seq, full + s);
+                if (sc_bulk) bulk_g2s(sSc + s * IDX_TILE, scale + t0, (uint32_t)nk * 4u, full + s);
             }
             __syncwarp();
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (whole warp loops, lane 0 issues) ----------------
+        const uint32_t sQa = smem_u32(sQ);
         for (int i = 0; i < n; ++i) {
-            const int b = i % IDX_NA, a = i % IDX_NACC;
-            if (!mbar_wait(a_full + b, (uint32_t)(i / IDX_NA) & 1u, 11)) break;
+            const int s = i % IDX_NS, a = i % IDX_NACC;
+            if (!mbar_wait(full + s, (uint32_t)(i / IDX_NS) & 1u, 11)) break;
             if (i >= IDX_NACC && !mbar_wait(acc_empty + a, (uint32_t)(i / IDX_NACC - 1) & 1u, 12)) break;
             tc_fence_after();
             if (lane == 0) {
                 WL_TR(3, i);
-                const uint32_t d0 = tmem + (uint32_t)(a * 32 * IDX_KSPLIT);
+                const uint32_t sA = smem_u32(k8 + s * L::K8_TILE);
+                const uint32_t d = tmem + (uint32_t)(a * 64);
 #pragma unroll
-                for (int kk = 0; kk < IDX_D / 16; ++kk) {
-                    const uint32_t c = kk >> 2, ko = (kk & 3) * 32;
-                    const uint64_t ad = desc_sw128(sA + (uint32_t)b * L::A_TILE + c * L::A_CHUNK + ko, 16, 1024);
-                    const uint64_t bd = desc_sw128(sQ + c * L::Q_CHUNK + ko, 16, 1024);
-                    const int part = kk % IDX_KSPLIT;
-                    mma_bf16(d0 + (uint32_t)(part * 32), ad, bd, L::IDESC, kk >= IDX_KSPLIT ? 1u : 0u);
+                for (int kk = 0; kk < IDX_D / 32; ++kk) {
+                    const uint64_t ad = desc_sw128(sA + kk * 32, 16, 1024);
+                    mma_f8(d, ad, desc_sw128(sQa + kk * 32, 16, 1024), L::IDESC, kk > 0 ? 1u : 0u);
+                    mma_f8(d + 32, ad, desc_sw128(sQa + L::QT + kk * 32, 16, 1024), L::IDESC, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(a_free + b);
                 mma_commit(acc_full + a);
+                mma_commit(empty + s);  // keys consumed
                 WL_TR(4, i);
             }
             __syncwarp();
         }
-    } else if (warp < 10) {
-        // ---------------- converters ----------------
-        const int ct = tid - 64;  // 0..255
-        const int piece = ct & 7, rbase = ct >> 3;  // 8 threads per 128-byte key row, 32 rows per pass
-        for (int i = 0; i < n; ++i) {
-            const int s = i % IDX_NS, b = i % IDX_NA;
-            const int t0 = (tb + i) * IDX_TILE;
-            const int nk = min(IDX_TILE, len - t0);
-            if (!mbar_wait(full + s, (uint32_t)(i / IDX_NS) & 1u, 13)) break;
-            if (i >= IDX_NA && !mbar_wait(a_free + b, (uint32_t)(i / IDX_NA - 1) & 1u, 14)) break;
-            if (ct == 0) WL_TR(1, i);
-            if (ct < IDX_TILE) {
-                float sv = 0.f;
-                if (ct < nk)
-                    sv = (sc_bulk_all && (nk & 3) == 0)
-                             ? reinterpret_cast<const float*>(k8 + s * L::STAGE + L::K8_TILE)[ct]
-                             : __ldg(scale + t0 + ct);
-                sc_s[(i % IDX_NSC) * IDX_TILE + ct] = sv * p.qk_scale * 256.f;  // undo the 2^-8 of the keys
-            }
-            const uint4* src = reinterpret_cast<const uint4*>(k8 + s * L::STAGE) + piece;
-            uint4 v[4];
-#pragma unroll
-            for (int ps = 0; ps < 4; ++ps) v[ps] = src[(ps * 32 + rbase) * 8];  // all loads first
-            uint8_t* dA = smem + L::OFF_A + b * L::A_TILE;
-            const uint32_t chunk = (uint32_t)piece >> 2, c16 = ((uint32_t)piece & 3u) * 2u;
-            const bool sw = piece >= 4;  // pieces 4..7 store hi first: 8 distinct bank groups per row
-#pragma unroll
-            for (int ps = 0; ps < 4; ++ps) {
-                const int row = ps * 32 + rbase;
-                uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-                if (row < nk) {
-                    e4m3x4_to_f16x4(v[ps].x, lo.x, lo.y);
-                    e4m3x4_to_f16x4(v[ps].y, lo.z, lo.w);
-                    e4m3x4_to_f16x4(v[ps].z, hi.x, hi.y);
-                    e4m3x4_to_f16x4(v[ps].w, hi.z, hi.w);
-                }
-                uint8_t* base = dA + chunk * L::A_CHUNK;
-                *reinterpret_cast<uint4*>(base + sw128_off(row, c16 + (sw ? 1u : 0u))) = sw ? hi : lo;
-                *reinterpret_cast<uint4*>(base + sw128_off(row, c16 + (sw ? 0u : 1u))) = sw ? lo : hi;
-            }
-            mbar_arrive(empty + s);  // stage read (its loads were consumed above)
-            fence_proxy_async_smem();
-            mbar_arrive(a_full + b);
-            if (ct == 0) WL_TR(2, i);
-        }
     } else {
-        // ---------------- epilogue ----------------
-        const int quarter = warp & 3;  // warps 10..13 cover TMEM lane quarters 2,3,0,1
+        // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----------------
+        const int quarter = warp & 3;
         const int key = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         for (int i = 0; i < n; ++i) {
-            const int a = i % IDX_NACC;
+            const int s = i % IDX_NS, a = i % IDX_NACC;
+            const int t0 = (tb + i) * IDX_TILE;
+            const int nk = min(IDX_TILE, len - t0);
             if (!mbar_wait(acc_full + a, (uint32_t)(i / IDX_NACC) & 1u, 15)) break;
             if (key == 0) WL_TR(5, i);
             tc_fence_after();
-            const float sc = sc_s[(i % IDX_NSC) * IDX_TILE + key];  // read before releasing the set
-            float acc[32], part[32];
-            const uint32_t d0 = tmem + lane_base + (uint32_t)(a * 32 * IDX_KSPLIT);
-            tmem_ld32(d0, acc);
-#pragma unroll
-            for (int k = 1; k < IDX_KSPLIT; ++k) {
-                tmem_ld32(d0 + (uint32_t)(k * 32), part);
-#pragma unroll
-                for (int h = 0; h < 32; ++h) acc[h] += part[h];
-            }
+            float sc = 0.f;
+            // the scales arrived with the keys: observe that copy's barrier too
+            if (sc_bulk_all && (nk & 3) == 0 && !mbar_wait(full + s, (uint32_t)(i / IDX_NS) & 1u, 16)) break;
+            if (key < nk)
+                sc = (sc_bulk_all && (nk & 3) == 0) ? sSc[s * IDX_TILE + key] : __ldg(scale + t0 + key);
+            sc *= p.qk_scale;
+            float hi[32], lo[32];
+            tmem_ld32(tmem + lane_base + (uint32_t)(a * 64), hi);
+            tmem_ld32(tmem + lane_base + (uint32_t)(a * 64 + 32), lo);
             tc_fence_before();
             mbar_arrive(acc_empty + a);
+            mbar_arrive(empty + s);
             float v = 0.f;
 #pragma unroll
-            for (int h = 0; h < 32; ++h) v = fmaf(sW[h], fmaxf(acc[h] * sc, 0.f), v);
-            const int t = (tb + i) * IDX_TILE + key;
+            for (int h = 0; h < 32; ++h) v = fmaf(sW[h], fmaxf(fmaf(lo[h], 0.03125f, hi[h]) * sc, 0.f), v);
+            const int t = t0 + key;
             const bool valid = t < len;
             if (valid) out[t] = v;
             if (key == 0) WL_TR(6, i);

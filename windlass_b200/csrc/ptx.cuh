@@ -7,6 +7,7 @@
 // unwinds (waits for its own copies, frees TMEM, returns). Nothing here traps.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>

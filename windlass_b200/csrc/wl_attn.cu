@@ -85,6 +85,43 @@ int ensure_attrs() {
     return WL_OK;
 }
 
+// cuTensorMapEncodeTiled, fetched once from the driver through the runtime
+// (the library links only the CUDA runtime).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(f);
+    }();
+    return fn;
+}
+
+// The fp8 key cache as {128 bytes, T keys, n_seq sequences}, 128x128-byte boxes,
+// 128B swizzle, zero fill past T.
+int encode_keys_map(CUtensorMap* tm, const void* keys, int32_t T, int n_seq, int64_t seq_stride) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return WL_ERR_CUDA;
+    if (n_seq > 1 && (seq_stride < (int64_t)T * 128 || (seq_stride & 15))) return WL_ERR_ARG;
+    const cuuint64_t dims[3] = {128, (cuuint64_t)T, (cuuint64_t)n_seq};
+    const cuuint64_t strides[2] = {128, (cuuint64_t)(n_seq > 1 ? seq_stride : (int64_t)T * 128)};
+    const cuuint32_t box[3] = {128, 128, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(keys), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::fprintf(stderr, "wl_attn: cuTensorMapEncodeTiled failed (%d)\n", (int)r);
+        return WL_ERR_CUDA;
+    }
+    return WL_OK;
+}
+
 int rows_ok(const wl_rows* r, int32_t T) {
     if (!r || r->n_rows <= 0 || r->rows_per_seq <= 0 || r->len0 < 0 || r->len_step < 0 || T <= 0)
         return WL_ERR_ARG;
@@ -139,7 +176,11 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
         if (cpr > ntiles) cpr = ntiles;
         const int tpc = (int)ceil_div(ntiles, cpr);
         dim3 grid((unsigned)ceil_div(ntiles, tpc), rows->n_rows);
-        wl::indexer_stream_kernel<<<grid, wl::IDX_STREAM_THREADS, wl::IdxStreamLayout::BYTES, st>>>(p, hist, tpc);
+        wl::IdxStreamParams sp{};
+        const int n_seq = (int)ceil_div(rows->n_rows, rows->rows_per_seq);
+        const int e = encode_keys_map(&sp.tm_keys, cache->keys, T, n_seq, cache->keys_seq_stride);
+        if (e != WL_OK) return e;
+        wl::indexer_stream_kernel<<<grid, wl::IDX_STREAM_THREADS, wl::IdxStreamLayout::BYTES, st>>>(p, sp, hist, tpc);
     }
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
