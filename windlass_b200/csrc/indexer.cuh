@@ -7,7 +7,7 @@
 // the key cache in fp8-e4m3 plus a per-key fp32 scale. The [H,T] score array
 // the reference writes to global memory and reads back never leaves TMEM here.
 //
-// Layout of the work (one CTA = 4 warps = one 128-key tile):
+// Prefill form (many query rows over one cache; one CTA = 4 warps = one 128-key tile):
 //   * the TMA engine streams the tile's 16 KB of fp8 keys into shared memory
 //     (cp.async.bulk, one contiguous copy: rows are packed 128-byte lines);
 //   * each thread widens one key row e4m3 -> bf16 (exact) into a 128B-swizzled
@@ -39,7 +39,6 @@ struct IdxParams {
     long long out_stride;
     float qk_scale;
     int groups_per_cta;
-    int scale_bulk;  // scale rows may be fetched by the TMA engine (16-byte aligned)
 };
 
 __device__ __forceinline__ int rows_len(int r, int rows_per_seq, int len0, int len_step, int T) {
@@ -205,15 +204,16 @@ namespace wl {
 
 // ---- decode form: persistent, warp-specialised, fp8 tensor cores ---------------------------
 // One CTA per SM streams a contiguous range of 128-key tiles of one row's
-// cache. Roles (6 warps), connected by mbarriers only:
+// cache. Roles (10 warps), connected by mbarriers only:
 //   warp 0      TMA producer: the tile's fp8 keys as one 128 x 128-byte box with
 //               128B swizzle (a tensor-map load; rows past the cache end read as
-//               zero) plus its scales (bulk copy) into ring stage i % IDX_NS
+//               zero) into ring stage i % IDX_NS
 //   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4 straight on the fp8 keys
-//               (M = 128 keys, N = 32 heads, K = 32 per instruction), two chains
-//               per tile — the query's hi and lo e4m3 terms — into TMEM
-//   warps 2-5   epilogue:     tcgen05.ld both chains of one key, combine, scale,
-//               relu, head-weighted sum, store (+ fused top-k histogram)
+//               (M = 128 keys, K = 32 per instruction), one chain of 4
+//               per tile: N = 64 = the query's hi and lo e4m3 terms side by side
+//   warps 2-9   epilogue:     tcgen05.ld both halves for one key, combine, scale,
+//               relu, head-weighted sum, store (+ fused top-k histogram); two
+//               groups of 4 warps take alternate tiles
 //
 // The query in e4m3: per head, q * s_h (s_h a power of two putting the head's
 // largest element in [128, 256)) = hi + lo / 32 with hi = e4m3(q s_h) and
@@ -226,9 +226,10 @@ namespace wl {
 // TOPK_HIST_BITS bits of the order-preserving score keys (warp-aggregated
 // global atomics) — the first radix pass of the top-k, fused here so that no
 // kernel re-reads the scores for it.
-constexpr int IDX_NS = 8;    // TMA stages (keys + scales)
+constexpr int IDX_NS = 8;    // TMA stages of fp8 keys
 constexpr int IDX_NACC = 4;  // accumulator sets (hi, lo) in flight
-constexpr int IDX_STREAM_THREADS = 192;
+constexpr int IDX_STREAM_THREADS = 320;
+constexpr int IDX_EPI_GROUPS = 2;  // epilogue groups of 4 warps, alternating tiles
 constexpr int TOPK_HIST_BITS = 13;
 constexpr int TOPK_HIST_BINS = 1 << TOPK_HIST_BITS;
 
@@ -237,15 +238,14 @@ struct IdxStreamLayout {
     static constexpr uint32_t QT = IDX_H * IDX_D;          // one e4m3 query term, 4 KB
     static constexpr uint32_t OFF_K8 = 0;
     static constexpr uint32_t OFF_Q = OFF_K8 + IDX_NS * K8_TILE;  // hi, lo
-    static constexpr uint32_t OFF_SC = OFF_Q + 2 * QT;             // [IDX_NS][128] scales
-    static constexpr uint32_t OFF_W = OFF_SC + IDX_NS * IDX_TILE * 4;
+    static constexpr uint32_t OFF_W = OFF_Q + 2 * QT;
     static constexpr uint32_t OFF_BAR = OFF_W + IDX_H * 4;
     static constexpr int N_BARS = 2 * IDX_NS + 2 * IDX_NACC;  // full, empty, acc_full, acc_empty
     static constexpr uint32_t OFF_SLOT = OFF_BAR + N_BARS * 8;
     static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;
     static constexpr uint32_t TMEM_COLS = 64 * IDX_NACC;  // 256
-    // kind::f8f6f4: E4M3 A and B (format 0), fp32 D; M = 128, N = 32
-    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(IDX_H >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    // kind::f8f6f4: E4M3 A and B (format 0), fp32 D; M = 128, N = 64 (hi ‖ lo)
+    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(2 * IDX_H >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 };
 
 __device__ __forceinline__ uint32_t score_key(float f) {
@@ -299,7 +299,6 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
     uint8_t* k8 = smem + L::OFF_K8;
     uint8_t* sQ = smem + L::OFF_Q;
     float* sW = reinterpret_cast<float*>(smem + L::OFF_W);
-    float* sSc = reinterpret_cast<float*>(smem + L::OFF_SC);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* empty = full + IDX_NS;
     uint64_t* acc_full = empty + IDX_NS;
@@ -321,7 +320,7 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < IDX_NS; ++s) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, 1 + 128);  // the MMA's commit + the epilogue's scale reads
+            mbar_init(empty + s, 1);  // the MMA's commit
         }
         for (int b = 0; b < IDX_NACC; ++b) {
             mbar_init(acc_full + b, 1);
@@ -330,7 +329,7 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);  // warp 1 allocates and frees
-    // Query -> two e4m3 terms per head (6 warps over 32 heads).
+    // Query -> two e4m3 terms per head (all warps over 32 heads).
     for (int h = warp; h < IDX_H; h += IDX_STREAM_THREADS / 32) {
         const __nv_bfloat16* qh = p.q + ((long long)r * IDX_H + h) * IDX_D;
         float x[4];
@@ -368,7 +367,6 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const bool sc_bulk_all = p.scale_bulk != 0;
 
     if (warp == 0) {
         // ---------------- TMA producer (whole warp loops, lane 0 issues) ----------------
@@ -378,11 +376,8 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
             if (lane == 0) {
                 WL_TR(0, i);
                 const int t0 = (tb + i) * IDX_TILE;
-                const int nk = min(IDX_TILE, len - t0);
-                const bool sc_bulk = sc_bulk_all && (nk & 3) == 0;
-                mbar_expect_tx(full + s, L::K8_TILE + (sc_bulk ? (uint32_t)nk * 4u : 0u));
+                mbar_expect_tx(full + s, L::K8_TILE);
                 tma_load3d(k8 + s * L::K8_TILE, &sp.tm_keys, 0, t0, seq, full + s);
-                if (sc_bulk) bulk_g2s(sSc + s * IDX_TILE, scale + t0, (uint32_t)nk * 4u, full + s);
             }
             __syncwarp();
         }
@@ -400,9 +395,9 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
                 const uint32_t d = tmem + (uint32_t)(a * 64);
 #pragma unroll
                 for (int kk = 0; kk < IDX_D / 32; ++kk) {
-                    const uint64_t ad = desc_sw128(sA + kk * 32, 16, 1024);
-                    mma_f8(d, ad, desc_sw128(sQa + kk * 32, 16, 1024), L::IDESC, kk > 0 ? 1u : 0u);
-                    mma_f8(d + 32, ad, desc_sw128(sQa + L::QT + kk * 32, 16, 1024), L::IDESC, kk > 0 ? 1u : 0u);
+                    // B = the 64 rows hi[0..31] ‖ lo[0..31], one swizzled block
+                    mma_f8(d, desc_sw128(sA + kk * 32, 16, 1024), desc_sw128(sQa + kk * 32, 16, 1024), L::IDESC,
+                           kk > 0 ? 1u : 0u);
                 }
                 mma_commit(acc_full + a);
                 mma_commit(empty + s);  // keys consumed
@@ -411,32 +406,34 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
             __syncwarp();
         }
     } else {
-        // ---------------- epilogue (warps 2..5 -> TMEM lane quarters 2,3,0,1) ----------------
+        // ------- epilogue (warps 2..9 -> TMEM lane quarters 2,3,0,1; group g takes tiles i = g mod 2) -------
         const int quarter = warp & 3;
         const int key = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        for (int i = 0; i < n; ++i) {
-            const int s = i % IDX_NS, a = i % IDX_NACC;
+        auto load_scale = [&](int i) {
+            const int t = (tb + i) * IDX_TILE + key;
+            return (i < n && t < len) ? __ldg(scale + t) : 0.f;
+        };
+        // Scales by plain loads one tile of this group ahead (a TMA copy per
+        // tile this small would cost the copy engine as much time as the 16 KB
+        // key tile).
+        float sc_next = load_scale((warp - 2) >> 2);
+        for (int i = (warp - 2) >> 2; i < n; i += IDX_EPI_GROUPS) {
+            const int a = i % IDX_NACC;
             const int t0 = (tb + i) * IDX_TILE;
-            const int nk = min(IDX_TILE, len - t0);
+            const float sc_raw = sc_next;
+            sc_next = load_scale(i + IDX_EPI_GROUPS);
             if (!mbar_wait(acc_full + a, (uint32_t)(i / IDX_NACC) & 1u, 15)) break;
             if (key == 0) WL_TR(5, i);
             tc_fence_after();
-            float sc = 0.f;
-            // the scales arrived with the keys: observe that copy's barrier too
-            if (sc_bulk_all && (nk & 3) == 0 && !mbar_wait(full + s, (uint32_t)(i / IDX_NS) & 1u, 16)) break;
-            if (key < nk)
-                sc = (sc_bulk_all && (nk & 3) == 0) ? sSc[s * IDX_TILE + key] : __ldg(scale + t0 + key);
-            sc *= p.qk_scale;
-            float hi[32], lo[32];
-            tmem_ld32(tmem + lane_base + (uint32_t)(a * 64), hi);
-            tmem_ld32(tmem + lane_base + (uint32_t)(a * 64 + 32), lo);
+            const float sc = sc_raw * p.qk_scale;
+            float acc[64];  // [0, 32): hi terms, [32, 64): lo terms
+            tmem_ld64(tmem + lane_base + (uint32_t)(a * 64), acc);
             tc_fence_before();
             mbar_arrive(acc_empty + a);
-            mbar_arrive(empty + s);
             float v = 0.f;
 #pragma unroll
-            for (int h = 0; h < 32; ++h) v = fmaf(sW[h], fmaxf(fmaf(lo[h], 0.03125f, hi[h]) * sc, 0.f), v);
+            for (int h = 0; h < 32; ++h) v = fmaf(sW[h], fmaxf(fmaf(acc[32 + h], 0.03125f, acc[h]) * sc, 0.f), v);
             const int t = t0 + key;
             const bool valid = t < len;
             if (valid) out[t] = v;

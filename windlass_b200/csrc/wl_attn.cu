@@ -157,7 +157,6 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
     p.out = out;
     p.out_stride = out_stride;
     p.qk_scale = cfg->idx_qk_scale;
-    p.scale_bulk = aligned16(cache->scale) && ((cache->scale_seq_stride * 4) % 16 == 0);
     const int ntiles = (int)ceil_div(T, wl::IDX_TILE);
     if (rows->rows_per_seq >= rows->n_rows && rows->n_rows >= 8) {
         // Many rows over one shared cache (prefill): 8 rows (N = 256) per MMA.
