@@ -125,7 +125,11 @@ def _topk_case(x, k):
 
 
 @pytest.mark.parametrize("T,k", [(4096, 2048), (32768, 2048), (131072, 2048), (5000, 1), (70000, 4095),
-                                 (2048, 2048), (1000, 2048), (1, 2048)])
+                                 (2048, 2048), (1000, 2048), (1, 2048),
+                                 # cluster top-k: odd lengths (scalar loads), each per-thread width,
+                                 # its upper limit, and the partitioned path above it
+                                 (8193, 2048), (70001, 2048), (131071, 8192), (196608, 2048),
+                                 (196609, 2048), (250000, 2048)])
 def test_topk_random_exact(T, k):
     rng = np.random.default_rng(T + k)
     _topk_case(rng.standard_normal(T).astype(np.float32), k)
@@ -448,9 +452,25 @@ def test_decode_long_context_multi_cta_topk():
         assert_ulp(rc, cpu(out["ctx"])[s], what=f"seq {s}")
 
 
+def test_topk_cluster_ragged_rows():
+    """Rows of different lengths in one call (the prefill row pattern): every
+    row's set equals numpy's top-k over its own prefix."""
+    rng = np.random.default_rng(12)
+    T, n_rows = 40000, 6
+    x = rng.standard_normal((n_rows, T)).astype(np.float32)
+    rows = _lib.Rows(n_rows, n_rows, 9000, 6000)  # lengths 9000, 15000, ..., 39000
+    sel, n = A.indexer_topk(torch.from_numpy(x).cuda(), 2048, rows=rows, T=T)
+    sel, n = cpu(sel), cpu(n)
+    for r in range(n_rows):
+        L = 9000 + 6000 * r
+        assert n[r] == 2048
+        assert np.array_equal(sel[r][:2048], np.sort(o.indexer_topk(x[r, :L], 2048))), f"row {r}"
+
+
 def test_topk_multi_cta_with_heavy_ties():
     rng = np.random.default_rng(11)
     _topk_case(rng.integers(0, 3, 100000).astype(np.float32), 2048)
     x = np.zeros(60000, np.float32)
     x[rng.choice(60000, 100, replace=False)] = 1.0
     _topk_case(x, 2048)
+    _topk_case(rng.integers(0, 3, 220000).astype(np.float32), 2048)  # partitioned path

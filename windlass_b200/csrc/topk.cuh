@@ -458,6 +458,236 @@ __global__ void __launch_bounds__(TOPKM_THREADS) topk_emit_kernel(TopkMParams p)
                                 p.cnt_eq[(long long)r * p.n_chunks + c], 0xFFFFFFFFu, out, scan_sh);
 }
 
+// ---- cluster top-k for decode rows ----------------------------------------------------
+// One thread-block cluster of TOPKC_CL CTAs per row; CTA `rank` holds the
+// scores [rank * 1024 * PER, (rank + 1) * 1024 * PER) of the row in registers
+// (PER consecutive keys per thread), read once. With the first-level histogram
+// (top HBITS bits) from the indexer's epilogue:
+//   1. every CTA finds the bin b1 holding the k-th key from that histogram;
+//   2. two refinement passes (10 + 9 bits) over the keys in b1: each CTA builds
+//      its shared-memory histogram, the cluster barrier publishes them, every
+//      CTA sums the TOPKC_CL histograms over distributed shared memory and
+//      finds the next bin — giving the exact k-th key `thr` and how many keys
+//      equal to it are taken (`need`);
+//   3. each CTA counts its keys > thr and == thr (block scan), the CTAs
+//      exchange their totals over distributed shared memory, and every thread
+//      writes its selected keys at their final, ascending positions.
+// One launch, no global scratch beyond the histogram.
+constexpr int TOPKC_CL = 8;
+constexpr int TOPKC_THREADS = 1024;
+
+#ifdef WL_TRACE
+__device__ long long* g_trace_topk;
+#define WL_TRK(slot)                                                                                  \
+    do {                                                                                              \
+        if (g_trace_topk && blockIdx.y == 0 && threadIdx.x == 0) g_trace_topk[blockIdx.x * 16 + (slot)] = clock64(); \
+    } while (0)
+#else
+#define WL_TRK(slot) \
+    do {             \
+    } while (0)
+#endif
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t dsmem_ld_u32(const void* local, uint32_t rank) {
+    uint32_t ra, v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(ra) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    cluster_arrive();
+    cluster_wait();
+}
+
+// Block-wide search from the top over bins held by threads: thread t owns the
+// consecutive bins [t * PERB, (t + 1) * PERB) with counts c[0..PERB) (higher t
+// and higher j = higher bins). Every thread returns the bin b where the running
+// count from the top crosses `need` (count(bins > b) < need <= count(bins >= b))
+// and count(bins > b). `sh` holds >= 35 words. Requires need <= total.
+template <int PERB>
+__device__ __forceinline__ void block_find_from_top(const uint32_t (&c)[PERB], uint32_t need, uint32_t* sh,
+                                                    uint32_t* out_bin, uint32_t* out_above) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint32_t s = 0;
+#pragma unroll
+    for (int j = 0; j < PERB; ++j) s += c[j];
+    uint32_t suf = s;  // inclusive suffix sum within the warp (lanes >= this one)
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += y;
+    }
+    if (lane == 0) sh[warp] = suf;  // warp total
+    __syncthreads();
+    // every warp: the sum of the totals of the warps above it
+    const uint32_t wt = lane < nw && lane > warp ? sh[lane] : 0u;
+    uint32_t above_w = wt;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) above_w += __shfl_xor_sync(0xffffffffu, above_w, o);
+    uint32_t above = above_w + suf - s;  // count in the bins above this thread's segment
+    if (s > 0 && above < need && need <= above + s) {
+        uint32_t b = 0;
+#pragma unroll
+        for (int j = PERB - 1; j >= 0; --j) {
+            if (above < need && need <= above + c[j]) {
+                b = (uint32_t)(threadIdx.x * PERB + j);
+                break;
+            }
+            above += c[j];
+        }
+        sh[33] = b;
+        sh[34] = above;
+    }
+    __syncthreads();
+    *out_bin = sh[33];
+    *out_above = sh[34];
+    __syncthreads();
+}
+
+template <int PER>
+__global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS, 1)
+    topk_cluster_kernel(TopkMParams p, int vec4) {
+    static_assert(PER % 4 == 0 && PER <= 32, "PER: whole float4s, one bit each in a 32-bit mask");
+    __shared__ uint32_t hloc[2][1024];  // this CTA's refinement histograms (read by the cluster)
+    __shared__ uint32_t scan_sh[36];
+    __shared__ uint32_t tot[2];  // this CTA's count of keys > thr, == thr (read by the cluster)
+    const int tid = threadIdx.x, r = blockIdx.y;
+    const uint32_t rank = cluster_ctarank();
+    const int len = topk_row_len(p, r);
+    const int kk = min(p.k, len);
+    int* out = p.out + (long long)r * p.out_stride;
+    const int lo = (int)rank * TOPKC_THREADS * PER, hi = min(len, lo + TOPKC_THREADS * PER);
+    WL_TRK(0);
+    if (rank == 0 && tid == 0 && p.n_out) p.n_out[r] = kk > 0 ? kk : 0;
+    if (kk <= 0) return;  // uniform over the cluster
+    if (kk >= len) {
+        for (int i = lo + tid; i < hi; i += TOPKC_THREADS) out[i] = i;
+        return;
+    }
+    // ---- loads: the first-level histogram (8 consecutive bins per thread) and
+    // the row's scores (PER consecutive per thread), all in flight together ----
+    static_assert(HB == 8 * TOPKC_THREADS, "level-1 bins per thread");
+    const uint4* hg = reinterpret_cast<const uint4*>(p.hist + (long long)r * HB) + 2 * tid;
+    const uint4 hx = hg[0], hy = hg[1];
+    const float* in = p.in + (long long)r * p.in_stride;
+    const int i0 = lo + tid * PER;
+    const int nvalid = max(0, min(PER, hi - i0));
+    const uint32_t valid = nvalid >= 32 ? 0xffffffffu : (1u << nvalid) - 1u;
+    float f[PER];
+    if (vec4 && nvalid == PER) {
+#pragma unroll
+        for (int j = 0; j < PER; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(in + i0 + j);
+            f[j] = v.x;
+            f[j + 1] = v.y;
+            f[j + 2] = v.z;
+            f[j + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) f[j] = j < nvalid ? in[i0 + j] : 0.f;
+    }
+    for (int i = tid; i < 2 * 1024; i += TOPKC_THREADS) (&hloc[0][0])[i] = 0;
+    WL_TRK(1);
+    // ---- level 1: the bin b1 of the indexer's histogram holding the k-th key ----
+    uint32_t b1, above1;
+    {
+        const uint32_t c8[8] = {hx.x, hx.y, hx.z, hx.w, hy.x, hy.y, hy.z, hy.w};
+        block_find_from_top<8>(c8, (uint32_t)kk, scan_sh, &b1, &above1);
+    }
+    uint32_t u[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) u[j] = ordered_key(f[j]);
+    WL_TRK(2);
+    // One pass over the keys: those in bins above b1 are selected outright, those
+    // in b1 are the candidates; every later step walks the candidate bits only.
+    uint32_t mabove = 0, mcand = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const uint32_t bin = u[j] >> (32 - HBITS);
+        mabove |= (bin > b1 ? 1u : 0u) << j;
+        mcand |= (bin == b1 ? 1u : 0u) << j;
+    }
+    mabove &= valid;
+    mcand &= valid;
+    // ---- levels 2, 3 over the cluster: bin `tid` of each pass summed over the CTAs ----
+    uint32_t prefix = b1 << (32 - HBITS), mask_hi = ~0u << (32 - HBITS), remaining = (uint32_t)kk - above1;
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+        const int shift = pass == 0 ? 9 : 0;
+        const uint32_t nb = pass == 0 ? 1024u : 512u;
+        uint32_t* h = hloc[pass];
+        for (uint32_t m = mcand; m; m &= m - 1) {
+            const uint32_t x = u[__ffs(m) - 1];  // dynamic index: local memory only for this rare walk
+            if ((x & mask_hi) == prefix) atomicAdd(&h[(x >> shift) & (nb - 1)], 1u);
+        }
+        WL_TRK(3 + 3 * pass);
+        cluster_sync_all();  // every CTA's histogram complete and visible
+        WL_TRK(4 + 3 * pass);
+        uint32_t c1[1] = {0u};
+        if (tid < (int)nb) {
+#pragma unroll
+            for (int c = 0; c < TOPKC_CL; ++c) c1[0] += dsmem_ld_u32(&h[tid], (uint32_t)c);
+        }
+        uint32_t b, above;
+        block_find_from_top<1>(c1, remaining, scan_sh, &b, &above);
+        prefix |= b << shift;
+        mask_hi |= (nb - 1) << shift;
+        remaining -= above;
+        WL_TRK(5 + 3 * pass);
+    }
+    const uint32_t thr = prefix, need = remaining;
+    // ---- ordered emission ----
+    uint32_t mgt = mabove, meq = 0;
+    for (uint32_t m = mcand; m; m &= m - 1) {
+        const int j = __ffs(m) - 1;
+        const uint32_t x = u[j];
+        mgt |= (x > thr ? 1u : 0u) << j;
+        meq |= (x == thr ? 1u : 0u) << j;
+    }
+    uint32_t total;
+    const uint32_t ex = block_excl_scan(((uint32_t)__popc(meq) << 16) | (uint32_t)__popc(mgt), scan_sh, &total);
+    if (tid == 0) {
+        tot[0] = total & 0xffffu;
+        tot[1] = total >> 16;
+    }
+    WL_TRK(9);
+    cluster_sync_all();  // totals visible; also orders every remote histogram read before exit
+    WL_TRK(10);
+    uint32_t gt_b = 0, eq_b = 0;
+    for (uint32_t c = 0; c < rank; ++c) {
+        gt_b += dsmem_ld_u32(&tot[0], c);
+        eq_b += dsmem_ld_u32(&tot[1], c);
+    }
+    cluster_arrive();  // this CTA's remote reads are done
+    gt_b += ex & 0xffffu;
+    eq_b += ex >> 16;
+    for (uint32_t m = mgt | meq; m; m &= m - 1) {
+        const int j = __ffs(m) - 1;
+        if ((mgt >> j) & 1u) {
+            out[gt_b + min(eq_b, need)] = i0 + j;
+            ++gt_b;
+        } else {
+            if (eq_b < need) out[gt_b + eq_b] = i0 + j;
+            ++eq_b;
+        }
+    }
+    WL_TRK(11);
+    cluster_wait();  // no CTA leaves while another may still read its totals
+    WL_TRK(12);
+}
+
 // ---- normalisation of an arbitrary index list ---------------------------------
 // Keeps key t in [0, len) iff some entry equals t: the mask the reference builds
 // (index_mask_fill + index_mask_scatter, glm_kernels.cuh:526-537) read back as a

@@ -187,6 +187,13 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
 
 // Rows longer than this use the multi-CTA top-k (which needs a workspace).
 constexpr int kTopkMultiMin = wl::TOPK_SMEM_MAX + 1;
+// Rows in (kTopkClusterMin, kTopkClusterMax] use the one-launch cluster top-k
+// (with a workspace for its first-level histogram).
+constexpr int kTopkClusterMin = 8192;
+constexpr int kTopkClusterMax = wl::TOPKC_CL * wl::TOPKC_THREADS * 24;
+// Whether a decode row of length T selects through a first-level histogram
+// (which the indexer's epilogue can then accumulate for free).
+inline bool topk_wants_hist(int32_t T, int32_t k) { return T > kTopkClusterMin && k < T; }
 constexpr int kTopkMaxChunks = 1024;
 static_assert(wl::TOPK_HIST_BITS == wl::HBITS, "indexer-fused histogram and top-k agree on bits");
 
@@ -258,7 +265,8 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
     if (!index || !sel_out || k <= 0) return WL_ERR_ARG;
     if (sel_stride < (k < T ? k : T)) return WL_ERR_ARG;
     const int lmax = max_row_len(rows, T);
-    if (ws && !cand_idx && lmax >= kTopkMultiMin && rows->n_rows <= 65535) {
+    const bool cluster = lmax > kTopkClusterMin && lmax <= kTopkClusterMax;
+    if (ws && !cand_idx && (cluster || lmax >= kTopkMultiMin) && rows->n_rows <= 65535) {
         wl::TopkMParams p{};
         p.in = index;
         p.in_stride = index_stride;
@@ -290,6 +298,20 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
             topk_hist_kernel<<<dim3((unsigned)ceil_div(lmax, 8192), rows->n_rows), 256, 0, st>>>(
                 index, index_stride, rows->len0, rows->len_step, rows->rows_per_seq, T, ws->hist);
             WL_CUDA_TRY(cudaGetLastError());
+        }
+        if (cluster) {
+            const dim3 gc(wl::TOPKC_CL, rows->n_rows);
+            const int vec4 = aligned16(index) && (index_stride & 3) == 0;
+            if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 4)
+                wl::topk_cluster_kernel<4><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+            else if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 8)
+                wl::topk_cluster_kernel<8><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+            else if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 16)
+                wl::topk_cluster_kernel<16><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+            else
+                wl::topk_cluster_kernel<24><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+            WL_CUDA_TRY(cudaGetLastError());
+            return WL_OK;
         }
         const dim3 g(p.n_chunks, rows->n_rows);
         wl::topk_partition_kernel<<<g, wl::TOPKM_THREADS, wl::TOPKM_PART_SMEM, st>>>(p);
@@ -697,7 +719,7 @@ static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, co
     if (io->mode == WL_MODE_OWNER) {
         float* index = io->index_out ? io->index_out : w.index;
         const int64_t istride = io->index_out ? io->index_stride : T;
-        const bool fuse = T >= kTopkMultiMin && cfg->index_topk < T;
+        const bool fuse = topk_wants_hist(T, cfg->index_topk);
         if (fuse) WL_CUDA_TRY(cudaMemsetAsync(w.topk.hist, 0, (size_t)B * (wl::HB + 1) * 4, st));
         if (int e = launch_indexer(cfg, &io->index, T, &rows, io->q_idx, io->w_idx, index, istride, st,
                                    fuse ? w.topk.hist : nullptr))
@@ -935,7 +957,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         if (!io->sel_out || !io->sel_n_out || io->sel_stride < kg) return WL_ERR_ARG;
         const wl_rows lrows{B, 1, T, 0};
         float* index = w.index;
-        const bool fuse = T >= kTopkMultiMin && k < T;
+        const bool fuse = topk_wants_hist(T, k);
         if (fuse) WL_CUDA_TRY(cudaMemsetAsync(w.topk.hist, 0, (size_t)B * (wl::HB + 1) * 4, st));
         if (int e = launch_indexer(cfg, &io->index, T, &lrows, io->q_idx, io->w_idx, index, T, st,
                                    fuse ? w.topk.hist : nullptr))
@@ -1011,7 +1033,11 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
 
 #ifdef WL_TRACE
 int wl_trace_set(long long* buf) {
-    return cudaMemcpyToSymbol(wl::g_trace, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
+    long long* b2 = buf ? buf + 1024 : nullptr;
+    return cudaMemcpyToSymbol(wl::g_trace, &buf, sizeof(buf)) == cudaSuccess &&
+                   cudaMemcpyToSymbol(wl::g_trace_topk, &b2, sizeof(b2)) == cudaSuccess
+               ? WL_OK
+               : WL_ERR_CUDA;
 }
 #endif
 
