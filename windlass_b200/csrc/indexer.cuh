@@ -227,9 +227,10 @@ namespace wl {
 // global atomics) — the first radix pass of the top-k, fused here so that no
 // kernel re-reads the scores for it.
 constexpr int IDX_NS = 8;    // TMA stages of fp8 keys
+constexpr int IDX_CTAS_PER_SM = 1;
 constexpr int IDX_NACC = 4;  // accumulator sets (hi, lo) in flight
-constexpr int IDX_STREAM_THREADS = 320;
 constexpr int IDX_EPI_GROUPS = 2;  // epilogue groups of 4 warps, alternating tiles
+constexpr int IDX_STREAM_THREADS = 64 + 128 * IDX_EPI_GROUPS;
 constexpr int TOPK_HIST_BITS = 13;
 constexpr int TOPK_HIST_BINS = 1 << TOPK_HIST_BITS;
 
@@ -291,9 +292,10 @@ __device__ long long* g_trace;
     } while (0)
 #endif
 
-__global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
+__global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
     indexer_stream_kernel(IdxParams p, const __grid_constant__ IdxStreamParams sp, unsigned* hist, int tiles_per_cta) {
     using L = IdxStreamLayout;
+    WL_KT_BEGIN(0);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* k8 = smem + L::OFF_K8;
@@ -312,7 +314,10 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
     const int ntiles = (len + IDX_TILE - 1) / IDX_TILE;
     const int tb = blockIdx.x * tiles_per_cta;
     const int n = min(tb + tiles_per_cta, ntiles) - tb;
-    if (n <= 0) return;
+    if (n <= 0) {
+        pdl_wait();
+        return;
+    }
     const float* scale = p.scale + (long long)seq * p.scale_seq;
     float* out = p.out + (long long)r * p.out_stride;
     unsigned* hrow = hist ? hist + (long long)r * TOPK_HIST_BINS : nullptr;
@@ -329,8 +334,16 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);  // warp 1 allocates and frees
-    // Query -> two e4m3 terms per head (all warps over 32 heads).
-    for (int h = warp; h < IDX_H; h += IDX_STREAM_THREADS / 32) {
+    tc_fence_before();
+    __syncthreads();  // barriers initialised, TMEM address published
+    tc_fence_after();
+    pdl_wait();  // everything above overlaps the previous kernel; global data below
+    pdl_trigger();
+    const uint32_t tmem = *tmem_slot;
+    const bool producer = warp == 0;
+    // Query -> two e4m3 terms per head, by every warp but the producer, which
+    // starts streaming keys at once; a named barrier joins the other warps.
+    for (int h = warp - 1; !producer && h < IDX_H; h += IDX_STREAM_THREADS / 32 - 1) {
         const __nv_bfloat16* qh = p.q + ((long long)r * IDX_H + h) * IDX_D;
         float x[4];
         float mx = 0.f;
@@ -362,13 +375,12 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
         *reinterpret_cast<uint32_t*>(sQ + L::QT + off) = lo4;
         if (lane == 0) sW[h] = __ldg(p.w + (long long)r * IDX_H + h) / s_h;
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    if (!producer) {
+        fence_proxy_async_smem();  // the query tile is read by the tensor cores
+        asm volatile("bar.sync 1, %0;" ::"n"(IDX_STREAM_THREADS - 32) : "memory");
+    }
 
-    if (warp == 0) {
+    if (producer) {
         // ---------------- TMA producer (whole warp loops, lane 0 issues) ----------------
         for (int i = 0; i < n; ++i) {
             const int s = i % IDX_NS;
@@ -436,9 +448,15 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
             for (int h = 0; h < 32; ++h) v = fmaf(sW[h], fmaxf(fmaf(acc[32 + h], 0.03125f, acc[h]) * sc, 0.f), v);
             const int t = t0 + key;
             const bool valid = t < len;
+#ifndef WL_EXP_NOSTORE
             if (valid) out[t] = v;
+#endif
             if (key == 0) WL_TR(6, i);
+#ifdef WL_EXP_NOHIST
+            if (false) {
+#else
             if (hrow) {
+#endif
                 const uint32_t bb = valid ? score_key(v) >> (32 - TOPK_HIST_BITS) : 0xFFFFFFFFu;
                 const unsigned peers = __match_any_sync(0xffffffffu, bb);
                 if (valid && lane == __ffs(peers) - 1) atomicAdd(hrow + bb, (unsigned)__popc(peers));
@@ -451,6 +469,7 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, 1)
         tc_fence_after();
         tmem_dealloc(tmem, L::TMEM_COLS);
     }
+    WL_KT_END(0);
 }
 
 }  // namespace wl

@@ -96,6 +96,9 @@ __device__ __forceinline__ void warp_transpose_reduce64(float* v, float& out0, f
 }
 
 __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
+    WL_KT_BEGIN(2);
+    pdl_wait();
+    pdl_trigger();
     using L = AttnLayout;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -397,6 +400,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
         tc_fence_after();
         tmem_dealloc(tmem, L::TMEM_COLS);
     }
+    WL_KT_END(2);
 }
 
 // ---- (o, lse) merge ---------------------------------------------------------------
@@ -413,6 +417,9 @@ struct MergeParams {
 // grid (n_heads, dv / 128, n_rows), 32 threads: lane l owns 4 latent columns.
 // Up to 32 parts: lane s holds part s's lse; all parts' columns load at once.
 __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
+    WL_KT_BEGIN(3);
+    pdl_wait();
+    pdl_trigger();
     const int h = blockIdx.x, q = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
     const float* lp = p.lse_part + (long long)r * p.lse_row_stride + h;
     const float ls = lane < p.n_parts ? lp[(long long)lane * p.lse_part_stride] : -INFINITY;
@@ -449,6 +456,7 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
     *reinterpret_cast<float4*>(p.ctx + ((long long)r * p.n_heads + h) * p.dv + c) = acc;
     if (q == 0 && lane == 0 && p.lse)
         p.lse[(long long)r * p.n_heads + h] = (W > 0.f) ? M + logf(W) : -INFINITY;
+    WL_KT_END(3);
 }
 
 }  // namespace wl

@@ -167,6 +167,32 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while its predecessor still runs; it must call
+// pdl_wait() before its first global access (read or write) of data another
+// kernel may touch, and only then pdl_trigger() — so that, transitively, every
+// grid before its predecessor has completed once a dependent starts. Both are
+// no-ops for a kernel launched without the attribute.
+#ifdef WL_TRACE
+// Per-kernel first-start / last-end global timestamps (trace builds only).
+__device__ unsigned long long* g_ktrace;
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define WL_KT_BEGIN(k) \
+    do { if (g_ktrace && threadIdx.x == 0) atomicMin(g_ktrace + 2 * (k), gtimer()); } while (0)
+#define WL_KT_END(k) \
+    do { if (g_ktrace && threadIdx.x == 0) atomicMax(g_ktrace + 2 * (k) + 1, gtimer()); } while (0)
+#else
+#define WL_KT_BEGIN(k) do {} while (0)
+#define WL_KT_END(k) do {} while (0)
+#endif
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 32 lanes x 32 consecutive 32-bit columns: thread (lane i) gets row (lane base + i).
 // Loads and waits: the wait names the loaded registers as read-write operands,
 // so no use of them can be scheduled before the data has landed.

@@ -189,6 +189,8 @@ struct TopkParams {
 constexpr int TOPK_SMEM_MAX = 40960;
 
 __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(TopkParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ float srow[];
     __shared__ uint32_t hist[2048];
     __shared__ uint32_t scan_sh[33];
@@ -282,6 +284,8 @@ __device__ __forceinline__ int topk_row_len(const TopkMParams& p, int r) {
 }
 
 __global__ void __launch_bounds__(TOPKM_THREADS) topk_partition_kernel(TopkMParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ uint32_t dyn[];  // candidate buffer: keys, positions
     uint32_t* ckey = dyn;
     int* cpos = reinterpret_cast<int*>(ckey + TOPKM_CHUNK_MAX);
@@ -357,6 +361,8 @@ __global__ void __launch_bounds__(TOPKM_THREADS) topk_partition_kernel(TopkMPara
 }
 
 __global__ void __launch_bounds__(TOPK_THREADS) topk_threshold_kernel(TopkMParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ uint32_t dyn[];  // 1024-bin histogram, then staged candidates
     uint32_t* h = dyn;
     uint32_t* sk = dyn + 1024;
@@ -440,6 +446,8 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_threshold_kernel(TopkMParam
 }
 
 __global__ void __launch_bounds__(TOPKM_THREADS) topk_emit_kernel(TopkMParams p) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ uint32_t scan_sh[33];
     const int c = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
     const int len = topk_row_len(p, r);
@@ -558,6 +566,9 @@ __device__ __forceinline__ void block_find_from_top(const uint32_t (&c)[PERB], u
 template <int PER>
 __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS, 1)
     topk_cluster_kernel(TopkMParams p, int vec4) {
+    WL_KT_BEGIN(1);
+    pdl_wait();
+    pdl_trigger();
     static_assert(PER % 4 == 0 && PER <= 32, "PER: whole float4s, one bit each in a 32-bit mask");
     __shared__ uint32_t hloc[2][1024];  // this CTA's refinement histograms (read by the cluster)
     __shared__ uint32_t scan_sh[36];
@@ -686,6 +697,7 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     WL_TRK(11);
     cluster_wait();  // no CTA leaves while another may still read its totals
     WL_TRK(12);
+    WL_KT_END(1);
 }
 
 // ---- normalisation of an arbitrary index list ---------------------------------
@@ -704,6 +716,8 @@ struct NormParams {
 };
 
 __global__ void __launch_bounds__(TOPK_THREADS) sel_normalize_kernel(NormParams p) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ uint32_t bm[];
     __shared__ uint32_t scan_sh[33];
     const int r = blockIdx.x, tid = threadIdx.x;

@@ -10,7 +10,9 @@
 // followed by the split-K (o, lse) merge. All launches go on the caller's
 // stream; nothing allocates; every failure is a status code.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 #include <mutex>
 #include <nccl.h>
 
@@ -122,6 +124,33 @@ int encode_keys_map(CUtensorMap* tm, const void* keys, int32_t T, int n_seq, int
     return WL_OK;
 }
 
+// Launches a kernel of the decode chain with programmatic stream
+// serialisation, so that its launch and prologue overlap the previous kernel
+// (each such kernel calls pdl_wait() before touching global data). WL_NO_PDL=1
+// in the environment turns this off.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("WL_NO_PDL");
+        return !(e && e[0] == '1');
+    }();
+    return on;
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int rows_ok(const wl_rows* r, int32_t T) {
     if (!r || r->n_rows <= 0 || r->rows_per_seq <= 0 || r->len0 < 0 || r->len_step < 0 || T <= 0)
         return WL_ERR_ARG;
@@ -170,7 +199,7 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
         // Decode: each row streams its own cache; at most one CTA per SM in
         // total, each over a contiguous range of tiles.
         if (rows->n_rows > 65535) return WL_ERR_ARG;
-        int cpr = sm_count() / rows->n_rows;
+        int cpr = wl::IDX_CTAS_PER_SM * sm_count() / rows->n_rows;
         if (cpr < 1) cpr = 1;
         if (cpr > ntiles) cpr = ntiles;
         const int tpc = (int)ceil_div(ntiles, cpr);
@@ -179,7 +208,7 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
         const int n_seq = (int)ceil_div(rows->n_rows, rows->rows_per_seq);
         const int e = encode_keys_map(&sp.tm_keys, cache->keys, T, n_seq, cache->keys_seq_stride);
         if (e != WL_OK) return e;
-        wl::indexer_stream_kernel<<<grid, wl::IDX_STREAM_THREADS, wl::IdxStreamLayout::BYTES, st>>>(p, sp, hist, tpc);
+        WL_CUDA_TRY(launch_pdl(wl::indexer_stream_kernel, grid, dim3(wl::IDX_STREAM_THREADS), wl::IdxStreamLayout::BYTES, st, p, sp, hist, tpc));
     }
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
@@ -237,6 +266,8 @@ TopkWs topk_ws_carve(void* base, int32_t rows, int32_t T) {
 // did not fuse it.
 __global__ void topk_hist_kernel(const float* in, long long in_stride, int len0, int len_step, int rows_per_seq,
                                  int T, unsigned* hist) {
+    wl::pdl_wait();
+    wl::pdl_trigger();
     const int r = blockIdx.y;
     const long long l = (long long)len0 + (long long)(r % rows_per_seq) * len_step;
     const int len = (int)(l < T ? l : T);
@@ -303,20 +334,20 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
             const dim3 gc(wl::TOPKC_CL, rows->n_rows);
             const int vec4 = aligned16(index) && (index_stride & 3) == 0;
             if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 4)
-                wl::topk_cluster_kernel<4><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<4>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
             else if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 8)
-                wl::topk_cluster_kernel<8><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<8>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
             else if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 16)
-                wl::topk_cluster_kernel<16><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<16>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
             else
-                wl::topk_cluster_kernel<24><<<gc, wl::TOPKC_THREADS, 0, st>>>(p, vec4);
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<24>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
             WL_CUDA_TRY(cudaGetLastError());
             return WL_OK;
         }
         const dim3 g(p.n_chunks, rows->n_rows);
-        wl::topk_partition_kernel<<<g, wl::TOPKM_THREADS, wl::TOPKM_PART_SMEM, st>>>(p);
-        wl::topk_threshold_kernel<<<rows->n_rows, wl::TOPK_THREADS, wl::TOPKM_THR_SMEM, st>>>(p);
-        wl::topk_emit_kernel<<<g, wl::TOPKM_THREADS, 0, st>>>(p);
+        WL_CUDA_TRY(launch_pdl(wl::topk_partition_kernel, g, dim3(wl::TOPKM_THREADS), wl::TOPKM_PART_SMEM, st, p));
+        WL_CUDA_TRY(launch_pdl(wl::topk_threshold_kernel, dim3(rows->n_rows), dim3(wl::TOPK_THREADS), wl::TOPKM_THR_SMEM, st, p));
+        WL_CUDA_TRY(launch_pdl(wl::topk_emit_kernel, g, dim3(wl::TOPKM_THREADS), 0, st, p));
         WL_CUDA_TRY(cudaGetLastError());
         return WL_OK;
     }
@@ -334,7 +365,7 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
     p.out_stride = sel_stride;
     p.n_out = sel_n_out;
     const size_t smem = lmax <= wl::TOPK_SMEM_MAX ? (size_t)lmax * 4 : 0;
-    wl::topk_kernel<<<rows->n_rows, wl::TOPK_THREADS, smem, st>>>(p);
+    WL_CUDA_TRY(launch_pdl(wl::topk_kernel, dim3(rows->n_rows), dim3(wl::TOPK_THREADS), smem, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
@@ -358,7 +389,7 @@ int launch_normalize(const int32_t* in, int64_t in_stride, const int32_t* n_in_d
     p.out = out;
     p.out_stride = out_stride;
     p.n_out = n_out;
-    wl::sel_normalize_kernel<<<rows->n_rows, wl::TOPK_THREADS, smem, st>>>(p);
+    WL_CUDA_TRY(launch_pdl(wl::sel_normalize_kernel, dim3(rows->n_rows), dim3(wl::TOPK_THREADS), smem, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
@@ -401,7 +432,7 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     p.lse_part = lse_part;
     p.scale_log2 = cfg->softmax_scale * 1.4426950408889634f;
     dim3 grid(max_splits, rows->n_rows);
-    wl::mla_sparse_attn_kernel<<<grid, 128, AttnLayout::BYTES, st>>>(p);
+    WL_CUDA_TRY(launch_pdl(wl::mla_sparse_attn_kernel, grid, dim3(128), AttnLayout::BYTES, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
@@ -414,7 +445,7 @@ int launch_merge(const float* o_part, const float* lse_part, int32_t n_rows, int
         return WL_ERR_ARG;
     wl::MergeParams p{o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
                       lse_part_stride, n_heads, dv, ctx, lse};
-    wl::lse_merge_kernel<<<dim3(n_heads, dv / 128, n_rows), 32, 0, st>>>(p);
+    WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
@@ -1032,6 +1063,9 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
 }
 
 #ifdef WL_TRACE
+int wl_ktrace_set(unsigned long long* buf) {
+    return cudaMemcpyToSymbol(wl::g_ktrace, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
+}
 int wl_trace_set(long long* buf) {
     long long* b2 = buf ? buf + 1024 : nullptr;
     return cudaMemcpyToSymbol(wl::g_trace, &buf, sizeof(buf)) == cudaSuccess &&
