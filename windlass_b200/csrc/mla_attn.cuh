@@ -8,7 +8,7 @@
 // with its index mask (src/glm_kernels.cuh:526-545 -> masked keys contribute
 // exactly zero), computed only over the selected keys instead of over all T.
 //
-// One CTA (4 warps) walks a contiguous range of the selection list in tiles of
+// One CTA (8 warps) walks a contiguous range of the selection list in tiles of
 // 128 keys:
 //   gather  — each key's 1152-byte [c_kv | k_rot] bf16 row is copied with
 //             16-byte cp.async straight into a 128B-swizzled tile, one commit
@@ -16,7 +16,7 @@
 //             loads of chunks c+1..8;
 //   QK^T    — tcgen05.mma M = 128 keys x N = 64 heads x K = 576, A = the row
 //             tile (K-major), B = the absorbed query (K-major), fp32 in TMEM;
-//   softmax — thread j owns key j's 64 scores (tcgen05.ld), per-head max and
+//   softmax — two threads own key j's 64 scores (32 heads each, tcgen05.ld), per-head max and
 //             sum are warp transpose-reductions, online rescaling across tiles;
 //             P (bf16) is written over the consumed k_rot chunk;
 //   P.V     — O^T[c,h] += V^T[c,j] P^T[j,h]: M = 128 latent columns (x4),
@@ -34,6 +34,7 @@ constexpr int AT_H = 64;
 constexpr int AT_D = 576;
 constexpr int AT_DV = 512;
 constexpr int AT_CHUNKS = 9;
+constexpr int AT_THREADS = 256;  // 8 warps: two per TMEM lane quarter, splitting the heads
 
 struct AttnLayout {
     static constexpr uint32_t ROW_CHUNK = AT_TILE * 128;  // 16 KB
@@ -95,8 +96,30 @@ __device__ __forceinline__ void warp_transpose_reduce64(float* v, float& out0, f
     out1 = v[1];
 }
 
-__global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
+// Reduce 32 per-lane values across the warp; lane l ends with value l.
+template <bool IS_MAX>
+__device__ __forceinline__ float warp_transpose_reduce32(float* v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int step = 0; step < 5; ++step) {
+        const int half = 16 >> step;
+        const int off = 16 >> step;
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float a = v[i], b = v[i + half];
+            const float send = upper ? a : b;
+            const float keep = upper ? b : a;
+            const float recv = __shfl_xor_sync(0xffffffffu, send, off);
+            v[i] = IS_MAX ? fmaxf(keep, recv) : keep + recv;
+        }
+    }
+    return v[0];
+}
+
+__global__ void __launch_bounds__(AT_THREADS, 1) mla_sparse_attn_kernel(AttnParams p) {
     WL_KT_BEGIN(2);
+    WL_TA(0);
     pdl_wait();
     pdl_trigger();
     using L = AttnLayout;
@@ -114,6 +137,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     int* misc = reinterpret_cast<int*>(smem + L::OFF_MISC);  // [0]=cb [1]=ce [2]=tmem [3]=rescale [4,5]=e0,e1
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3, hh = warp >> 2;  // TMEM lane quarter; which 32 heads
     const int r = blockIdx.y, s = blockIdx.x;
     const int seq = r / p.rows_per_seq;
     const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
@@ -174,10 +198,11 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     }
     __syncthreads();
     const int cb = misc[0], ce = misc[1];
+    WL_TA(1);
     float* o_out = p.o_part + ((long long)r * p.max_splits + s) * (AT_H * AT_DV);
     float* lse_out = p.lse_part + ((long long)r * p.max_splits + s) * AT_H;
     if (cb >= ce) {  // empty range: a zero partial with weight e^-inf
-        for (int i = tid; i < AT_H * AT_DV / 4; i += 128)
+        for (int i = tid; i < AT_H * AT_DV / 4; i += AT_THREADS)
             reinterpret_cast<float4*>(o_out)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (tid < AT_H) lse_out[tid] = -INFINITY;
         return;
@@ -195,7 +220,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     // Absorbed query [64][576] -> 9 swizzled K-major chunks (commit group 0).
     {
         const __nv_bfloat16* q = p.q_abs + (long long)r * AT_H * AT_D;
-        for (int pid = tid; pid < AT_H * 72; pid += 128) {
+        for (int pid = tid; pid < AT_H * 72; pid += AT_THREADS) {
             const int h = pid / 72, pp = pid % 72;
             cp_async16(sQ + (uint32_t)(pp >> 3) * L::Q_CHUNK + sw128_off(h, pp & 7),
                        q + (long long)h * AT_D + pp * 8, 16);
@@ -205,8 +230,9 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    WL_TA(2);
     const uint32_t tmem = (uint32_t)misc[2];
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem, tO = tmem + 64;
 
     const __nv_bfloat16* ckv = p.c_kv + (long long)seq * p.ckv_seq;
@@ -219,7 +245,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
     for (int it = 0; it < n_tiles; ++it) {
         const int tb = cb + it * AT_TILE;
         const int nv = min(AT_TILE, ce - tb);
-        {
+        if (tid < AT_TILE) {
             int row = -1;
             if (tid < nv) {
                 const long long key = list ? (long long)list[tb + tid] : (long long)(tb + tid);
@@ -234,8 +260,8 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
 #pragma unroll 1
         for (int c = 0; c < AT_CHUNKS; ++c) {
 #pragma unroll
-            for (int k2 = 0; k2 < 8; ++k2) {
-                const int pid = k2 * 128 + tid;
+            for (int k2 = 0; k2 < AT_TILE * 8 / AT_THREADS; ++k2) {
+                const int pid = k2 * AT_THREADS + tid;
                 const int j = pid >> 3, seg = pid & 7;
                 const int row = row_idx[j];
                 const __nv_bfloat16* src =
@@ -245,6 +271,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
             }
             cp_async_commit();
         }
+        WL_TA(3);
         // QK^T chunk by chunk as the loads land.
 #pragma unroll 1
         for (int c = 0; c < AT_CHUNKS; ++c) {
@@ -277,23 +304,21 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
         phase ^= 1;
         if (!__syncthreads_and(ok)) break;
         tc_fence_after();
+        WL_TA(4);
 
         // ---- softmax over this tile (log2 domain) ----
-        float sv[64];
-        tmem_ld32(tS + lane_base, sv);
-        tmem_ld32(tS + lane_base + 32, sv + 32);
-        tmem_wait_ld();
-        const bool valid = tid < nv;
+        // Thread: key j = quarter * 32 + lane, heads [32 hh, 32 hh + 32).
+        const int j = quarter * 32 + lane;
+        float sv[32];
+        tmem_ld32(tS + lane_base + (uint32_t)(hh * 32), sv);
+        const bool valid = j < nv;
 #pragma unroll
-        for (int h = 0; h < 64; ++h) sv[h] = valid ? sv[h] * p.scale_log2 : -INFINITY;
+        for (int h = 0; h < 32; ++h) sv[h] = valid ? sv[h] * p.scale_log2 : -INFINITY;
         {
-            float tmp[64];
+            float tmp[32];
 #pragma unroll
-            for (int h = 0; h < 64; ++h) tmp[h] = sv[h];
-            float a0, a1;
-            warp_transpose_reduce64<true>(tmp, a0, a1);
-            red[warp * 64 + 2 * lane] = a0;
-            red[warp * 64 + 2 * lane + 1] = a1;
+            for (int h = 0; h < 32; ++h) tmp[h] = sv[h];
+            red[quarter * 64 + hh * 32 + lane] = warp_transpose_reduce32<true>(tmp);
         }
         __syncthreads();
         if (tid < AT_H) {
@@ -308,25 +333,23 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
         if (tid < AT_H && it > 0 && alpha[tid] != 1.f) misc[3] = 1;
         // P = exp2(s - m), rounded to bf16; row j = this thread's key.
         {
-            float ps[64];
+            float ps[32];
 #pragma unroll
-            for (int pc = 0; pc < 8; ++pc) {
+            for (int pc = 0; pc < 4; ++pc) {
                 uint32_t w4[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int h = pc * 8 + e * 2;
+                    const int hl = pc * 8 + e * 2, h = hh * 32 + hl;
                     const __nv_bfloat162 b2 =
-                        __floats2bfloat162_rn(exp2f(sv[h] - m_run[h]), exp2f(sv[h + 1] - m_run[h + 1]));
+                        __floats2bfloat162_rn(exp2f(sv[hl] - m_run[h]), exp2f(sv[hl + 1] - m_run[h + 1]));
                     w4[e] = *reinterpret_cast<const uint32_t*>(&b2);
-                    ps[h] = __low2float(b2);
-                    ps[h + 1] = __high2float(b2);
+                    ps[hl] = __low2float(b2);
+                    ps[hl + 1] = __high2float(b2);
                 }
-                sts_v4(sP + sw128_off(tid, pc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
+                sts_v4(sP + sw128_off(j, hh * 4 + pc), make_uint4(w4[0], w4[1], w4[2], w4[3]));
             }
-            float a0, a1;
-            warp_transpose_reduce64<false>(ps, a0, a1);
-            red[warp * 64 + 2 * lane] = a0;
-            red[warp * 64 + 2 * lane + 1] = a1;
+            // red[] was last read (the max) before the barrier above
+            red[quarter * 64 + hh * 32 + lane] = warp_transpose_reduce32<false>(ps);
         }
         __syncthreads();
         if (tid < AT_H)
@@ -334,7 +357,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
         // Rescale the running O^T (lane = latent column, column = head).
         if (misc[3]) {
 #pragma unroll 1
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 2 * hh; q < 2 * hh + 2; ++q) {
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     float ov[32];
@@ -352,6 +375,7 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
+        WL_TA(5);
         if (tid == 0) {
 #pragma unroll 1
             for (int q = 0; q < 4; ++q) {
@@ -369,28 +393,37 @@ __global__ void __launch_bounds__(128, 1) mla_sparse_attn_kernel(AttnParams p) {
         phase ^= 1;
         if (!__syncthreads_and(ok)) break;
         tc_fence_after();
+        WL_TA(6);
     }
 
     if (ok) {
         if (tid < AT_H) alpha[tid] = 1.f / l_run[tid];  // reuse: 1/l per head
         __syncthreads();
-        // o[h][c] = O^T[c][h] / l[h]; lane = c within chunk q.
+        // o[h][c] = O^T[c][h] / l[h], staged in shared memory over the (consumed)
+        // row tile in the partial's own [h][c] layout, then copied out with
+        // coalesced 16-byte stores. Lane = latent column c within chunk q.
+        float* stage = reinterpret_cast<float*>(smem + L::OFF_ROWS);
 #pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 2 * hh; q < 2 * hh + 2; ++q) {
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 float ov[32];
                 tmem_ld32(tO + lane_base + (uint32_t)(q * 64 + hf * 32), ov);
-                tmem_wait_ld();
-                const int c = q * 128 + warp * 32 + lane;
+                const int c = q * 128 + quarter * 32 + lane;
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int h = hf * 32 + i;
-                    o_out[h * AT_DV + c] = ov[i] * alpha[h];
+                    stage[h * AT_DV + c] = ov[i] * alpha[h];
                 }
             }
         }
+        __syncthreads();
+        const float4* st4 = reinterpret_cast<const float4*>(stage);
+        float4* o4 = reinterpret_cast<float4*>(o_out);
+#pragma unroll 4
+        for (int i = tid; i < AT_H * AT_DV / 4; i += AT_THREADS) o4[i] = st4[i];
         if (tid < AT_H) lse_out[tid] = (m_run[tid] + log2f(l_run[tid])) * 0.69314718055994531f;
+        WL_TA(7);
     } else {
         cp_async_wait_all();
     }

@@ -167,6 +167,29 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
 }
 
+// ---- thread-block clusters: rank, distributed shared memory, barrier ----
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t dsmem_ld_u32(const void* local, uint32_t rank) {
+    uint32_t ra, v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(ra) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    cluster_arrive();
+    cluster_wait();
+}
+
 // Programmatic dependent launch. A kernel launched with programmatic stream
 // serialisation may start while its predecessor still runs; it must call
 // pdl_wait() before its first global access (read or write) of data another
@@ -181,11 +204,18 @@ __device__ __forceinline__ unsigned long long gtimer() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+__device__ long long* g_trace_attn;
+#define WL_TA(slot)                                                                                        \
+    do {                                                                                                   \
+        if (g_trace_attn && threadIdx.x == 0 && blockIdx.y == 0 && blockIdx.x < 16)                        \
+            g_trace_attn[blockIdx.x * 16 + (slot)] = clock64();                                           \
+    } while (0)
 #define WL_KT_BEGIN(k) \
     do { if (g_ktrace && threadIdx.x == 0) atomicMin(g_ktrace + 2 * (k), gtimer()); } while (0)
 #define WL_KT_END(k) \
     do { if (g_ktrace && threadIdx.x == 0) atomicMax(g_ktrace + 2 * (k) + 1, gtimer()); } while (0)
 #else
+#define WL_TA(slot) do {} while (0)
 #define WL_KT_BEGIN(k) do {} while (0)
 #define WL_KT_END(k) do {} while (0)
 #endif

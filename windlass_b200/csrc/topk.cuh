@@ -496,28 +496,6 @@ __device__ long long* g_trace_topk;
     } while (0)
 #endif
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t dsmem_ld_u32(const void* local, uint32_t rank) {
-    uint32_t ra, v;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(ra) : "memory");
-    return v;
-}
-__device__ __forceinline__ void cluster_arrive() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    cluster_arrive();
-    cluster_wait();
-}
-
 // Block-wide search from the top over bins held by threads: thread t owns the
 // consecutive bins [t * PERB, (t + 1) * PERB) with counts c[0..PERB) (higher t
 // and higher j = higher bins). Every thread returns the bin b where the running

@@ -432,7 +432,7 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     p.lse_part = lse_part;
     p.scale_log2 = cfg->softmax_scale * 1.4426950408889634f;
     dim3 grid(max_splits, rows->n_rows);
-    WL_CUDA_TRY(launch_pdl(wl::mla_sparse_attn_kernel, grid, dim3(128), AttnLayout::BYTES, st, p));
+    WL_CUDA_TRY(launch_pdl(wl::mla_sparse_attn_kernel, grid, dim3(wl::AT_THREADS), AttnLayout::BYTES, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
@@ -1063,6 +1063,9 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
 }
 
 #ifdef WL_TRACE
+int wl_atrace_set(long long* buf) {
+    return cudaMemcpyToSymbol(wl::g_trace_attn, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
+}
 int wl_ktrace_set(unsigned long long* buf) {
     return cudaMemcpyToSymbol(wl::g_ktrace, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
 }
