@@ -445,6 +445,8 @@ struct MergeParams {
     int n_heads, dv;
     float* ctx;
     float* lse;
+    long long ctx_row_stride;  // floats between rows of ctx (n_heads * dv when dense)
+    long long lse_out_row_stride;  // floats between rows of lse (n_heads when dense)
 };
 
 // grid (n_heads, dv / 128, n_rows), 32 threads: lane l owns 4 latent columns.
@@ -486,9 +488,9 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
             acc.w = fmaf(wv[j], v[j].w, acc.w);
         }
     }
-    *reinterpret_cast<float4*>(p.ctx + ((long long)r * p.n_heads + h) * p.dv + c) = acc;
+    *reinterpret_cast<float4*>(p.ctx + (long long)r * p.ctx_row_stride + (long long)h * p.dv + c) = acc;
     if (q == 0 && lane == 0 && p.lse)
-        p.lse[(long long)r * p.n_heads + h] = (W > 0.f) ? M + logf(W) : -INFINITY;
+        p.lse[(long long)r * p.lse_out_row_stride + h] = (W > 0.f) ? M + logf(W) : -INFINITY;
     WL_KT_END(3);
 }
 

@@ -182,7 +182,37 @@ struct TopkParams {
     int* out;
     long long out_stride;
     int* n_out;  // optional [n_rows]
+    // Segmented rows (topk_reg_kernel only): seg_len > 0 places element i of a
+    // row at row_base + (i / seg_len) * seg_stride + i % seg_len — e.g. the
+    // [rank][row][k] result of an all-gather read as rows of rank * k entries.
+    int seg_len;
+    long long seg_stride;
 };
+
+// Optional candidate outputs of a selection (the sharded decode's exchange
+// format): output position pos of row r also gets score[r * stride + pos] (the
+// selected score) and gidx[r * stride + pos] = base + key index; positions
+// [k', k) are padded with (-inf, INT_MAX).
+struct CandOut {
+    float* score;
+    int* gidx;
+    long long stride;
+    int k;
+    long long base;
+};
+
+// Inverse of ordered_key (-0 comes back as +0).
+__device__ __forceinline__ float key_to_float(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
+}
+
+__device__ __forceinline__ void cand_pad(const CandOut& co, int r, int from, int tid, int nt) {
+    if (!co.score) return;
+    for (int pos = from + tid; pos < co.k; pos += nt) {
+        co.score[(long long)r * co.stride + pos] = -INFINITY;
+        co.gidx[(long long)r * co.stride + pos] = 0x7fffffff;
+    }
+}
 
 // One CTA per row. Rows of up to TOPK_SMEM_MAX elements are staged once in
 // shared memory and every pass reads them from there.
@@ -543,7 +573,7 @@ __device__ __forceinline__ void block_find_from_top(const uint32_t (&c)[PERB], u
 
 template <int PER>
 __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS, 1)
-    topk_cluster_kernel(TopkMParams p, int vec4) {
+    topk_cluster_kernel(TopkMParams p, int vec4, CandOut co) {
     WL_KT_BEGIN(1);
     pdl_wait();
     pdl_trigger();
@@ -559,9 +589,16 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     const int lo = (int)rank * TOPKC_THREADS * PER, hi = min(len, lo + TOPKC_THREADS * PER);
     WL_TRK(0);
     if (rank == 0 && tid == 0 && p.n_out) p.n_out[r] = kk > 0 ? kk : 0;
+    if (rank == 0) cand_pad(co, r, max(kk, 0), tid, TOPKC_THREADS);
     if (kk <= 0) return;  // uniform over the cluster
     if (kk >= len) {
-        for (int i = lo + tid; i < hi; i += TOPKC_THREADS) out[i] = i;
+        for (int i = lo + tid; i < hi; i += TOPKC_THREADS) {
+            out[i] = i;
+            if (co.score) {
+                co.score[(long long)r * co.stride + i] = p.in[(long long)r * p.in_stride + i];
+                co.gidx[(long long)r * co.stride + i] = (int)(co.base + i);
+            }
+        }
         return;
     }
     // ---- loads: the first-level histogram (8 consecutive bins per thread) and
@@ -664,18 +701,165 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     eq_b += ex >> 16;
     for (uint32_t m = mgt | meq; m; m &= m - 1) {
         const int j = __ffs(m) - 1;
+        int pos = -1;
         if ((mgt >> j) & 1u) {
-            out[gt_b + min(eq_b, need)] = i0 + j;
+            pos = (int)(gt_b + min(eq_b, need));
             ++gt_b;
         } else {
-            if (eq_b < need) out[gt_b + eq_b] = i0 + j;
+            if (eq_b < need) pos = (int)(gt_b + eq_b);
             ++eq_b;
+        }
+        if (pos >= 0) {
+            out[pos] = i0 + j;
+            if (co.score) {
+                co.score[(long long)r * co.stride + pos] = key_to_float(u[j]);
+                co.gidx[(long long)r * co.stride + pos] = (int)(co.base + i0 + j);
+            }
         }
     }
     WL_TRK(11);
     cluster_wait();  // no CTA leaves while another may still read its totals
     WL_TRK(12);
     WL_KT_END(1);
+}
+
+// ---- single-CTA top-k with the row in registers --------------------------------------
+// Rows of up to TOPK_THREADS * PER keys (PER consecutive per thread, read once):
+// an 11-bit first-level histogram (warp-aggregated shared-memory atomics: the
+// top bins of real score distributions are crowded), then two refinement
+// passes (11 + 10 bits) that walk only the keys of the crossing bin, then the
+// ordered emission. Supports candidate-index mapping (`cand_idx`), segmented
+// rows and candidate outputs.
+template <int PER>
+__global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p, int vec4, CandOut co) {
+    static_assert(PER % 4 == 0 && PER <= 32, "PER: whole float4s, one bit each in a 32-bit mask");
+    pdl_wait();
+    pdl_trigger();
+    __shared__ uint32_t hist[2048];
+    __shared__ uint32_t scan_sh[36];
+    const int tid = threadIdx.x, lane = tid & 31, r = blockIdx.x;
+    const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
+    const int len = (int)(lraw < p.T ? lraw : p.T);
+    const int kk = min(p.k, len);
+    int* out = p.out + (long long)r * p.out_stride;
+    if (tid == 0 && p.n_out) p.n_out[r] = kk > 0 ? kk : 0;
+    cand_pad(co, r, max(kk, 0), tid, TOPK_THREADS);
+    if (kk <= 0) return;
+    const float* row = p.in + (long long)r * p.in_stride;
+    const int* crow = p.cand_idx ? p.cand_idx + (long long)r * p.in_stride : nullptr;
+    auto off = [&](int i) -> long long {
+        return p.seg_len > 0 ? (long long)(i / p.seg_len) * p.seg_stride + i % p.seg_len : (long long)i;
+    };
+    if (kk >= len) {
+        for (int i = tid; i < len; i += TOPK_THREADS) {
+            const int key = crow ? crow[off(i)] : i;
+            out[i] = key;
+            if (co.score) {
+                co.score[(long long)r * co.stride + i] = row[off(i)];
+                co.gidx[(long long)r * co.stride + i] = (int)(co.base + key);
+            }
+        }
+        return;
+    }
+    const int i0 = tid * PER;
+    const int nvalid = max(0, min(PER, len - i0));
+    const uint32_t valid = nvalid >= 32 ? 0xffffffffu : (1u << nvalid) - 1u;
+    uint32_t u[PER];
+    {
+        float f[PER];
+        const long long o0 = nvalid > 0 ? off(i0) : 0;  // PER divides seg_len: one segment per thread
+        if (vec4 && nvalid == PER) {
+#pragma unroll
+            for (int j = 0; j < PER; j += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(row + o0 + j);
+                f[j] = v.x;
+                f[j + 1] = v.y;
+                f[j + 2] = v.z;
+                f[j + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < PER; ++j) f[j] = j < nvalid ? row[o0 + j] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < PER; ++j) u[j] = ordered_key(f[j]);
+    }
+    for (int i = tid; i < 2048; i += TOPK_THREADS) hist[i] = 0;
+    __syncthreads();
+    // ---- level 1: bits 31..21 ----
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const bool v = (valid >> j) & 1u;
+        const uint32_t bin = v ? u[j] >> 21 : 0xffffffffu;
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        if (v && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+    }
+    __syncthreads();
+    uint32_t b1, above1;
+    {
+        const uint32_t c2[2] = {hist[2 * tid], hist[2 * tid + 1]};
+        block_find_from_top<2>(c2, (uint32_t)kk, scan_sh, &b1, &above1);
+    }
+    uint32_t mabove = 0, mcand = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const uint32_t bin = u[j] >> 21;
+        mabove |= (bin > b1 ? 1u : 0u) << j;
+        mcand |= (bin == b1 ? 1u : 0u) << j;
+    }
+    mabove &= valid;
+    mcand &= valid;
+    // ---- levels 2 (bits 20..10) and 3 (bits 9..0), over the crossing bin's keys ----
+    uint32_t prefix = b1 << 21, mask_hi = 0xffe00000u, remaining = (uint32_t)kk - above1;
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+        const int shift = pass == 0 ? 10 : 0;
+        const uint32_t nb = pass == 0 ? 2048u : 1024u;
+        for (int i = tid; i < 2048; i += TOPK_THREADS) hist[i] = 0;
+        __syncthreads();
+        for (uint32_t m = mcand; m; m &= m - 1) {
+            const uint32_t x = u[__ffs(m) - 1];
+            if ((x & mask_hi) == prefix) atomicAdd(&hist[(x >> shift) & (nb - 1)], 1u);
+        }
+        __syncthreads();
+        uint32_t b, above;
+        const uint32_t c2[2] = {2 * tid < (int)nb ? hist[2 * tid] : 0u, 2 * tid + 1 < (int)nb ? hist[2 * tid + 1] : 0u};
+        block_find_from_top<2>(c2, remaining, scan_sh, &b, &above);
+        prefix |= b << shift;
+        mask_hi |= (nb - 1) << shift;
+        remaining -= above;
+    }
+    const uint32_t thr = prefix, need = remaining;
+    // ---- ordered emission ----
+    uint32_t mgt = mabove, meq = 0;
+    for (uint32_t m = mcand; m; m &= m - 1) {
+        const int j = __ffs(m) - 1;
+        const uint32_t x = u[j];
+        mgt |= (x > thr ? 1u : 0u) << j;
+        meq |= (x == thr ? 1u : 0u) << j;
+    }
+    uint32_t total;
+    const uint32_t ex = block_excl_scan(((uint32_t)__popc(meq) << 16) | (uint32_t)__popc(mgt), scan_sh, &total);
+    uint32_t gt_b = ex & 0xffffu, eq_b = ex >> 16;
+    for (uint32_t m = mgt | meq; m; m &= m - 1) {
+        const int j = __ffs(m) - 1;
+        int pos = -1;
+        if ((mgt >> j) & 1u) {
+            pos = (int)(gt_b + min(eq_b, need));
+            ++gt_b;
+        } else {
+            if (eq_b < need) pos = (int)(gt_b + eq_b);
+            ++eq_b;
+        }
+        if (pos >= 0) {
+            const int key = crow ? crow[off(i0 + j)] : i0 + j;
+            out[pos] = key;
+            if (co.score) {
+                co.score[(long long)r * co.stride + pos] = key_to_float(u[j]);
+                co.gidx[(long long)r * co.stride + pos] = (int)(co.base + key);
+            }
+        }
+    }
 }
 
 // ---- normalisation of an arbitrary index list ---------------------------------

@@ -23,6 +23,24 @@
 
 namespace {
 
+#ifdef WL_TRACE
+// Phase timeline of one host call (trace builds only): events recorded at
+// phase boundaries on the call's stream.
+cudaEvent_t g_ph_ev[32];
+int g_ph_n = -1;  // -1: off
+#define WL_PHASE(st)                                                                       \
+    do {                                                                                   \
+        if (g_ph_n >= 0 && g_ph_n < 32) {                                                  \
+            if (!g_ph_ev[g_ph_n]) cudaEventCreate(&g_ph_ev[g_ph_n]);                       \
+            cudaEventRecord(g_ph_ev[g_ph_n++], st);                                        \
+        }                                                                                  \
+    } while (0)
+#else
+#define WL_PHASE(st) \
+    do {             \
+    } while (0)
+#endif
+
 using wl::AttnLayout;
 constexpr int kMaxSplits = 16;   // split-K CTAs per decode row
 constexpr int kMaxDevices = 64;
@@ -224,6 +242,9 @@ constexpr int kTopkClusterMax = wl::TOPKC_CL * wl::TOPKC_THREADS * 24;
 // (which the indexer's epilogue can then accumulate for free).
 inline bool topk_wants_hist(int32_t T, int32_t k) { return T > kTopkClusterMin && k < T; }
 constexpr int kTopkMaxChunks = 1024;
+// Rows up to this length (without the cluster path) select in one CTA with the
+// row in registers.
+constexpr int kTopkRegMax = wl::TOPK_THREADS * 32;
 static_assert(wl::TOPK_HIST_BITS == wl::HBITS, "indexer-fused histogram and top-k agree on bits");
 
 struct TopkWs {
@@ -290,14 +311,20 @@ int max_row_len(const wl_rows* rows, int32_t T) {
 
 // hist_ready: the histogram block of `ws` already holds this call's
 // first-level histogram (fused into the indexer) and cand_n is zero.
+// `co` (optional) also writes each selection as (score, base + key) candidates;
+// seg_len > 0 reads segmented rows (single-CTA register path only).
 int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, int32_t T, int32_t k,
                 const int32_t* cand_idx, int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
-                cudaStream_t st, const TopkWs* ws = nullptr, bool hist_ready = false) {
+                cudaStream_t st, const TopkWs* ws = nullptr, bool hist_ready = false,
+                const wl::CandOut* co = nullptr, int32_t seg_len = 0, int64_t seg_stride = 0) {
+    const wl::CandOut cout = co ? *co : wl::CandOut{};
     if (!index || !sel_out || k <= 0) return WL_ERR_ARG;
     if (sel_stride < (k < T ? k : T)) return WL_ERR_ARG;
     const int lmax = max_row_len(rows, T);
     const bool cluster = lmax > kTopkClusterMin && lmax <= kTopkClusterMax;
-    if (ws && !cand_idx && (cluster || lmax >= kTopkMultiMin) && rows->n_rows <= 65535) {
+    if (seg_len > 0 && (lmax > kTopkRegMax || (seg_len % 32))) return WL_ERR_ARG;
+    if (co && !(seg_len > 0 || (ws && !cand_idx && cluster) || lmax <= kTopkRegMax)) return WL_ERR_ARG;
+    if (seg_len == 0 && ws && !cand_idx && (cluster || lmax >= kTopkMultiMin) && rows->n_rows <= 65535) {
         wl::TopkMParams p{};
         p.in = index;
         p.in_stride = index_stride;
@@ -334,13 +361,13 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
             const dim3 gc(wl::TOPKC_CL, rows->n_rows);
             const int vec4 = aligned16(index) && (index_stride & 3) == 0;
             if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 4)
-                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<4>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<4>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4, cout));
             else if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 8)
-                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<8>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<8>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4, cout));
             else if (lmax <= wl::TOPKC_CL * wl::TOPKC_THREADS * 16)
-                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<16>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<16>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4, cout));
             else
-                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<24>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4));
+                WL_CUDA_TRY(launch_pdl(wl::topk_cluster_kernel<24>, gc, dim3(wl::TOPKC_THREADS), 0, st, p, vec4, cout));
             WL_CUDA_TRY(cudaGetLastError());
             return WL_OK;
         }
@@ -364,6 +391,21 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
     p.out = sel_out;
     p.out_stride = sel_stride;
     p.n_out = sel_n_out;
+    p.seg_len = seg_len;
+    p.seg_stride = seg_stride;
+    if (lmax <= kTopkRegMax) {
+        const int vec4 = aligned16(index) && (index_stride & 3) == 0 && (seg_stride & 3) == 0;
+        const dim3 g(rows->n_rows), b(wl::TOPK_THREADS);
+        if (lmax <= wl::TOPK_THREADS * 4)
+            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<4>, g, b, 0, st, p, vec4, cout));
+        else if (lmax <= wl::TOPK_THREADS * 8)
+            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<8>, g, b, 0, st, p, vec4, cout));
+        else if (lmax <= wl::TOPK_THREADS * 16)
+            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<16>, g, b, 0, st, p, vec4, cout));
+        else
+            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<32>, g, b, 0, st, p, vec4, cout));
+        return WL_OK;
+    }
     const size_t smem = lmax <= wl::TOPK_SMEM_MAX ? (size_t)lmax * 4 : 0;
     WL_CUDA_TRY(launch_pdl(wl::topk_kernel, dim3(rows->n_rows), dim3(wl::TOPK_THREADS), smem, st, p));
     WL_CUDA_TRY(cudaGetLastError());
@@ -439,12 +481,15 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
 
 int launch_merge(const float* o_part, const float* lse_part, int32_t n_rows, int32_t n_parts, int64_t row_stride,
                  int64_t part_stride, int64_t lse_row_stride, int64_t lse_part_stride, int32_t n_heads,
-                 int32_t dv, float* ctx, float* lse, cudaStream_t st) {
+                 int32_t dv, float* ctx, float* lse, cudaStream_t st, int64_t ctx_row_stride = 0,
+                 int64_t lse_out_row_stride = 0) {
     if (!o_part || !lse_part || !ctx || n_rows <= 0 || n_parts <= 0 || n_parts > 32 || (dv % 128) ||
         n_heads <= 0 || n_rows > 65535)
         return WL_ERR_ARG;
     wl::MergeParams p{o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
-                      lse_part_stride, n_heads, dv, ctx, lse};
+                      lse_part_stride, n_heads, dv, ctx, lse,
+                      ctx_row_stride > 0 ? ctx_row_stride : (int64_t)n_heads * dv,
+                      lse_out_row_stride > 0 ? lse_out_row_stride : (int64_t)n_heads};
     WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
@@ -564,17 +609,6 @@ __global__ void candidates_to_rows_kernel(const float* s_all, const int* i_all, 
         const long long dst = (long long)b * nranks * k + (long long)rk * k + j;
         s_rows[dst] = s_all[x];
         i_rows[dst] = i_all[x];
-    }
-}
-
-// Pack this rank's merged (o, lse) per row: [row][64*512 + 64].
-__global__ void pack_partial_kernel(const float* ctx, const float* lse, int batch, float* out) {
-    const int per = wl::AT_H * wl::AT_DV + wl::AT_H;
-    const long long n = (long long)batch * per;
-    for (long long x = blockIdx.x * (long long)blockDim.x + threadIdx.x; x < n; x += (long long)gridDim.x * blockDim.x) {
-        const int b = (int)(x / per), e = (int)(x % per);
-        out[x] = e < wl::AT_H * wl::AT_DV ? ctx[(long long)b * wl::AT_H * wl::AT_DV + e]
-                                          : lse[(long long)b * wl::AT_H + (e - wl::AT_H * wl::AT_DV)];
     }
 }
 
@@ -726,7 +760,8 @@ size_t wl_attn_workspace_bytes(const wl_attn_cfg* cfg, int32_t T_max, int32_t ba
 
 static int decode_local(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, const DecodeWs& w,
                         int64_t t0, int64_t T_global, float* ctx, float* lse, const int32_t* sel,
-                        const int32_t* cnt, int32_t sel_n, int64_t stride, long long n_max, cudaStream_t st) {
+                        const int32_t* cnt, int32_t sel_n, int64_t stride, long long n_max, cudaStream_t st,
+                        int64_t ctx_row_stride = 0, int64_t lse_row_stride = 0) {
     // Attention over the selection restricted to this cache's window [t0, t0+T),
     // then the merge of its split-K partials.
     const int32_t B = io->batch;
@@ -739,7 +774,7 @@ static int decode_local(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, con
         return e;
     return launch_merge(w.o_part, w.lse_part, B, nsplit, (int64_t)nsplit * wl::AT_H * wl::AT_DV,
                         (int64_t)wl::AT_H * wl::AT_DV, (int64_t)nsplit * wl::AT_H, wl::AT_H, wl::AT_H,
-                        wl::AT_DV, ctx, lse, st);
+                        wl::AT_DV, ctx, lse, st, ctx_row_stride, lse_row_stride);
 }
 
 // Selection for decode: returns the list/count/stride the attention consumes.
@@ -980,6 +1015,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     const int32_t B = io->batch, T = io->T, k = cfg->index_topk;
     const int64_t Tg = shard->T_global, t0 = shard->t0;
     const int32_t kg = (int32_t)(k < Tg ? k : Tg);
+    WL_PHASE(st);
 
     const int32_t* gsel = nullptr;
     const int32_t* gcnt = nullptr;
@@ -994,10 +1030,21 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
                                    fuse ? w.topk.hist : nullptr))
             return e;
         const int32_t kl = k < T ? k : T;
-        if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st, &w.topk, fuse)) return e;
-        gather_candidates_kernel<<<dim3((unsigned)ceil_div(k, 256), B), 256, 0, st>>>(index, T, w.sel, kl, w.cnt, k, t0,
-                                                                                     w.cand_score, w.cand_idx);
-        WL_CUDA_TRY(cudaGetLastError());
+        WL_PHASE(st);
+        // Local top-k; its selection leaves as (score, global index) candidates,
+        // k per row (padded), straight from the top-k's emission where it can.
+        const bool cand_direct = T <= kTopkClusterMax;
+        const wl::CandOut co{w.cand_score, w.cand_idx, k, k, t0};
+        if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st, &w.topk, fuse,
+                                cand_direct ? &co : nullptr))
+            return e;
+        WL_PHASE(st);
+        if (!cand_direct) {
+            gather_candidates_kernel<<<dim3((unsigned)ceil_div(k, 256), B), 256, 0, st>>>(
+                index, T, w.sel, kl, w.cnt, k, t0, w.cand_score, w.cand_idx);
+            WL_CUDA_TRY(cudaGetLastError());
+        }
+        WL_PHASE(st);
         if (ncclGroupStart() != ncclSuccess) return WL_ERR_NCCL;
         if (ncclAllGather(w.cand_score, w.cand_score_all, (size_t)B * k, ncclFloat32, comm->comm, st) != ncclSuccess ||
             ncclAllGather(w.cand_idx, w.cand_idx_all, (size_t)B * k, ncclInt32, comm->comm, st) != ncclSuccess) {
@@ -1005,15 +1052,25 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
             return WL_ERR_NCCL;
         }
         if (ncclGroupEnd() != ncclSuccess) return WL_ERR_NCCL;
-        candidates_to_rows_kernel<<<256, 256, 0, st>>>(w.cand_score_all, w.cand_idx_all, N, B, k, w.cand_score_rows,
-                                                      w.cand_idx_rows);
-        WL_CUDA_TRY(cudaGetLastError());
-        // Exact global top-k over the candidates; candidate order is global
-        // key order, so position ties resolve to the lowest global index.
+        WL_PHASE(st);
+        // Exact global top-k over the candidates; candidate order (rank-major,
+        // ascending within a rank) is global key order, so position ties resolve
+        // to the lowest global index. The all-gathered [rank][row][k] buffers are
+        // read in place as rows of N segments of k.
         const wl_rows crows{B, 1, N * k, 0};
-        if (int e = launch_topk(w.cand_score_rows, (int64_t)N * k, &crows, N * k, kg, w.cand_idx_rows, io->sel_out,
-                                io->sel_stride, io->sel_n_out, st))
-            return e;
+        if ((k % 32) == 0 && (int64_t)N * k <= kTopkRegMax) {
+            if (int e = launch_topk(w.cand_score_all, k, &crows, N * k, kg, w.cand_idx_all, io->sel_out,
+                                    io->sel_stride, io->sel_n_out, st, nullptr, false, nullptr, k, (int64_t)B * k))
+                return e;
+        } else {
+            candidates_to_rows_kernel<<<256, 256, 0, st>>>(w.cand_score_all, w.cand_idx_all, N, B, k,
+                                                          w.cand_score_rows, w.cand_idx_rows);
+            WL_CUDA_TRY(cudaGetLastError());
+            if (int e = launch_topk(w.cand_score_rows, (int64_t)N * k, &crows, N * k, kg, w.cand_idx_rows,
+                                    io->sel_out, io->sel_stride, io->sel_n_out, st))
+                return e;
+        }
+        WL_PHASE(st);
         if (io->index_out) {
             // Local scores into the caller's buffer (this rank's window).
             for (int32_t b = 0; b < B; ++b)
@@ -1021,6 +1078,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
                                               index + (int64_t)b * T, (size_t)T * 4, (size_t)T * 4, 1,
                                               cudaMemcpyDeviceToDevice, st));
         }
+        WL_PHASE(st);
         gsel = io->sel_out;
         gcnt = io->sel_n_out;
         gstride = io->sel_stride;
@@ -1040,9 +1098,9 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
             gstride = Tg;
         }
     }
-    // Local partial over this rank's window, merged over its splits.
-    float* lctx = w.part_recv;  // scratch: [B][64][512] then lse [B][64]
-    float* llse = w.part_recv + (size_t)B * wl::AT_H * wl::AT_DV;
+    // Local partial over this rank's window, merged over its splits straight
+    // into the exchange layout [row][64 * 512 + 64].
+    const int64_t rowsz = wl::AT_H * wl::AT_DV + wl::AT_H;
     long long n_max = Tg;
     int32_t sel_n = 0;
     if (io->mode == WL_MODE_OWNER) n_max = kg;
@@ -1050,19 +1108,33 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         n_max = (gcnt || !(io->sel_flags & WL_SEL_CANONICAL)) ? gstride : io->sel_n;
         sel_n = io->sel_n;
     }
-    if (int e = decode_local(cfg, io, w, t0, Tg, lctx, llse, gsel, gcnt, sel_n, gstride, n_max, st)) return e;
-    pack_partial_kernel<<<256, 256, 0, st>>>(lctx, llse, B, w.part_send);
-    WL_CUDA_TRY(cudaGetLastError());
-    const size_t per = (size_t)B * (wl::AT_H * wl::AT_DV + wl::AT_H);
+    if (int e = decode_local(cfg, io, w, t0, Tg, w.part_send, w.part_send + wl::AT_H * wl::AT_DV, gsel, gcnt, sel_n,
+                             gstride, n_max, st, rowsz, rowsz))
+        return e;
+    const size_t per = (size_t)B * rowsz;
+    WL_PHASE(st);
     if (ncclAllGather(w.part_send, w.part_recv, per, ncclFloat32, comm->comm, st) != ncclSuccess) return WL_ERR_NCCL;
+    WL_PHASE(st);
     // part_recv: [rank][row][64*512 + 64]
-    const int64_t rowsz = wl::AT_H * wl::AT_DV + wl::AT_H;
     float* lse = io->lse ? io->lse : w.lse_tmp;
-    return launch_merge(w.part_recv, w.part_recv + wl::AT_H * wl::AT_DV, B, N, rowsz, (int64_t)B * rowsz, rowsz,
-                        (int64_t)B * rowsz, wl::AT_H, wl::AT_DV, io->ctx, lse, st);
+    const int em = launch_merge(w.part_recv, w.part_recv + wl::AT_H * wl::AT_DV, B, N, rowsz, (int64_t)B * rowsz,
+                                rowsz, (int64_t)B * rowsz, wl::AT_H, wl::AT_DV, io->ctx, lse, st);
+    WL_PHASE(st);
+    return em;
 }
 
 #ifdef WL_TRACE
+void wl_phase_begin() { g_ph_n = 0; }
+// Milliseconds between consecutive phase events; returns their count.
+int wl_phase_read(float* ms, int max_n) {
+    const int n = g_ph_n;
+    g_ph_n = -1;
+    if (n <= 0) return 0;
+    cudaEventSynchronize(g_ph_ev[n - 1]);
+    int m = 0;
+    for (int i = 1; i < n && m < max_n; ++i) cudaEventElapsedTime(&ms[m++], g_ph_ev[i - 1], g_ph_ev[i]);
+    return m;
+}
 int wl_atrace_set(long long* buf) {
     return cudaMemcpyToSymbol(wl::g_trace_attn, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
 }
