@@ -520,7 +520,14 @@ __device__ long long* g_trace_topk;
     do {                                                                                              \
         if (g_trace_topk && blockIdx.y == 0 && threadIdx.x == 0) g_trace_topk[blockIdx.x * 16 + (slot)] = clock64(); \
     } while (0)
+#define WL_TRR(slot)                                                                   \
+    do {                                                                               \
+        if (g_trace_topk && blockIdx.x == 0 && threadIdx.x == 0) g_trace_topk[128 + (slot)] = clock64(); \
+    } while (0)
 #else
+#define WL_TRR(slot) \
+    do {             \
+    } while (0)
 #define WL_TRK(slot) \
     do {             \
     } while (0)
@@ -725,19 +732,22 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
 
 // ---- single-CTA top-k with the row in registers --------------------------------------
 // Rows of up to TOPK_THREADS * PER keys (PER consecutive per thread, read once):
-// an 11-bit first-level histogram (warp-aggregated shared-memory atomics: the
-// top bins of real score distributions are crowded), then two refinement
-// passes (11 + 10 bits) that walk only the keys of the crossing bin, then the
-// ordered emission. Supports candidate-index mapping (`cand_idx`), segmented
-// rows and candidate outputs.
+// an 8-bit first level on warp-private counters (score distributions crowd a
+// few top bins), two 12-bit refinement levels on one shared histogram, then the
+// ordered emission. (Aggregating a warp's lanes by bin with __match_any_sync
+// measured several times slower than letting shared-memory atomics serialise.)
+// Supports candidate-index mapping (`cand_idx`), segmented rows and candidate
+// outputs.
 template <int PER>
 __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p, int vec4, CandOut co) {
     static_assert(PER % 4 == 0 && PER <= 32, "PER: whole float4s, one bit each in a 32-bit mask");
+    WL_TRR(0);
     pdl_wait();
     pdl_trigger();
-    __shared__ uint32_t hist[2048];
+    __shared__ uint32_t whist[TOPK_THREADS / 32][128];  // per warp: 256 16-bit counters (level 1)
+    __shared__ uint32_t hist[4096];                     // levels 2 and 3
     __shared__ uint32_t scan_sh[36];
-    const int tid = threadIdx.x, lane = tid & 31, r = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
     const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
     const int len = (int)(lraw < p.T ? lraw : p.T);
     const int kk = min(p.k, len);
@@ -784,62 +794,67 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
 #pragma unroll
         for (int j = 0; j < PER; ++j) u[j] = ordered_key(f[j]);
     }
-    for (int i = tid; i < 2048; i += TOPK_THREADS) hist[i] = 0;
-    __syncthreads();
-    // ---- level 1: bits 31..21 ----
+    WL_TRR(1);
+    // ---- level 1: bits 31..24, warp-private 16-bit counters (at most 32 * PER
+    // each), so that warps never contend on a crowded bin ----
+    for (int i = lane; i < 128; i += 32) whist[warp][i] = 0;
+    for (int i = tid; i < 4096; i += TOPK_THREADS) hist[i] = 0;
+    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-        const bool v = (valid >> j) & 1u;
-        const uint32_t bin = v ? u[j] >> 21 : 0xffffffffu;
-        const unsigned peers = __match_any_sync(0xffffffffu, bin);
-        if (v && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (unsigned)__popc(peers));
-    }
+    for (int j = 0; j < PER; ++j)
+        if ((valid >> j) & 1u) atomicAdd(&whist[warp][u[j] >> 25], 1u << (16 * ((u[j] >> 24) & 1u)));
     __syncthreads();
     uint32_t b1, above1;
     {
-        const uint32_t c2[2] = {hist[2 * tid], hist[2 * tid + 1]};
+        uint32_t c2[2] = {0u, 0u};  // thread t < 128 owns bins 2t, 2t + 1
+        if (tid < 128) {
+#pragma unroll 8
+            for (int w = 0; w < TOPK_THREADS / 32; ++w) {
+                const uint32_t x = whist[w][tid];
+                c2[0] += x & 0xffffu;
+                c2[1] += x >> 16;
+            }
+        }
+        WL_TRR(2);
         block_find_from_top<2>(c2, (uint32_t)kk, scan_sh, &b1, &above1);
+        WL_TRR(3);
     }
-    uint32_t mabove = 0, mcand = 0;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-        const uint32_t bin = u[j] >> 21;
-        mabove |= (bin > b1 ? 1u : 0u) << j;
-        mcand |= (bin == b1 ? 1u : 0u) << j;
-    }
-    mabove &= valid;
-    mcand &= valid;
-    // ---- levels 2 (bits 20..10) and 3 (bits 9..0), over the crossing bin's keys ----
-    uint32_t prefix = b1 << 21, mask_hi = 0xffe00000u, remaining = (uint32_t)kk - above1;
+    // ---- levels 2 (bits 23..12) and 3 (bits 11..0) over the crossing bin's
+    // keys, one shared histogram each: once the top byte is fixed the keys
+    // spread over the low bits ----
+    uint32_t prefix = b1 << 24, mask_hi = 0xff000000u, remaining = (uint32_t)kk - above1;
 #pragma unroll 1
     for (int pass = 0; pass < 2; ++pass) {
-        const int shift = pass == 0 ? 10 : 0;
-        const uint32_t nb = pass == 0 ? 2048u : 1024u;
-        for (int i = tid; i < 2048; i += TOPK_THREADS) hist[i] = 0;
-        __syncthreads();
-        for (uint32_t m = mcand; m; m &= m - 1) {
-            const uint32_t x = u[__ffs(m) - 1];
-            if ((x & mask_hi) == prefix) atomicAdd(&hist[(x >> shift) & (nb - 1)], 1u);
+        const int shift = pass == 0 ? 12 : 0;
+        if (pass == 1) {
+            for (int i = tid; i < 4096; i += TOPK_THREADS) hist[i] = 0;
+            __syncthreads();
         }
+#pragma unroll
+        for (int j = 0; j < PER; ++j)
+            if (((valid >> j) & 1u) && (u[j] & mask_hi) == prefix) atomicAdd(&hist[(u[j] >> shift) & 4095u], 1u);
         __syncthreads();
-        uint32_t b, above;
-        const uint32_t c2[2] = {2 * tid < (int)nb ? hist[2 * tid] : 0u, 2 * tid + 1 < (int)nb ? hist[2 * tid + 1] : 0u};
-        block_find_from_top<2>(c2, remaining, scan_sh, &b, &above);
+        uint32_t c4[4], b, above;  // thread t owns bins 4t .. 4t + 3
+#pragma unroll
+        for (int q = 0; q < 4; ++q) c4[q] = hist[4 * tid + q];
+        block_find_from_top<4>(c4, remaining, scan_sh, &b, &above);
         prefix |= b << shift;
-        mask_hi |= (nb - 1) << shift;
+        mask_hi |= 4095u << shift;
         remaining -= above;
+        WL_TRR(4 + 3 * pass);
     }
     const uint32_t thr = prefix, need = remaining;
     // ---- ordered emission ----
-    uint32_t mgt = mabove, meq = 0;
-    for (uint32_t m = mcand; m; m &= m - 1) {
-        const int j = __ffs(m) - 1;
-        const uint32_t x = u[j];
-        mgt |= (x > thr ? 1u : 0u) << j;
-        meq |= (x == thr ? 1u : 0u) << j;
+    uint32_t mgt = 0, meq = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const bool v = (valid >> j) & 1u;
+        mgt |= (v && u[j] > thr ? 1u : 0u) << j;
+        meq |= (v && u[j] == thr ? 1u : 0u) << j;
     }
     uint32_t total;
     const uint32_t ex = block_excl_scan(((uint32_t)__popc(meq) << 16) | (uint32_t)__popc(mgt), scan_sh, &total);
+    WL_TRR(5);
     uint32_t gt_b = ex & 0xffffu, eq_b = ex >> 16;
     for (uint32_t m = mgt | meq; m; m &= m - 1) {
         const int j = __ffs(m) - 1;
@@ -860,6 +875,7 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
             }
         }
     }
+    WL_TRR(6);
 }
 
 // ---- normalisation of an arbitrary index list ---------------------------------
