@@ -25,7 +25,7 @@
 // The range's normalised output o[h][c] and lse[h] (natural log) are written
 // as one partial; a split-K launch merges partials with lse_merge_kernel.
 #pragma once
-#include "ptx.cuh"
+#include "p2p.cuh"
 
 namespace wl {
 
@@ -447,6 +447,10 @@ struct MergeParams {
     float* lse;
     long long ctx_row_stride;  // floats between rows of ctx (n_heads * dv when dense)
     long long lse_out_row_stride;  // floats between rows of lse (n_heads when dense)
+    // Parts arriving through the peer exchange (ll.base set): o_part / lse_part
+    // are unused; part s's o words start at slot s, its lse words ll_lse_off on.
+    P2PRecv ll;
+    long long ll_lse_off;
 };
 
 // grid (n_heads, dv / 128, n_rows), 32 threads: lane l owns 4 latent columns.
@@ -456,29 +460,61 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
     pdl_wait();
     pdl_trigger();
     const int h = blockIdx.x, q = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
-    const float* lp = p.lse_part + (long long)r * p.lse_row_stride + h;
-    const float ls = lane < p.n_parts ? lp[(long long)lane * p.lse_part_stride] : -INFINITY;
+    const int c = q * 128 + lane * 4;
+    const bool ll = p.ll.base != nullptr;
+    const uint32_t epoch = ll ? p2p_epoch(p.ll) : 0u;
+    const uint64_t* lb = ll ? p2p_slot(p.ll, epoch, 0) : nullptr;
+    float ls = -INFINITY;
+    if (lane < p.n_parts) {
+        const long long li = (long long)r * p.lse_row_stride + h + (long long)lane * p.lse_part_stride;
+        ls = ll ? __uint_as_float(ll_wait1(lb + p.ll_lse_off + li, epoch, ll_load1_raw(lb + p.ll_lse_off + li), 21))
+                : p.lse_part[li];
+    }
     float M = ls;
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float wl = (M == -INFINITY || ls == -INFINITY) ? 0.f : exp2f((ls - M) * 1.4426950408889634f);
     float W = wl;
     for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
     const float inv = W > 0.f ? 1.f / W : 0.f;
-    const int c = q * 128 + lane * 4;
-    const float* base = p.o_part + (long long)r * p.row_stride + (long long)h * p.dv + c;
+    const long long oi = (long long)r * p.row_stride + (long long)h * p.dv + c;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     // Parts in groups of 8: all loads of a group are issued before any use.
     for (int s0 = 0; s0 < p.n_parts; s0 += 8) {
         float4 v[8];
         float wv[8];
+        uint64_t raw[8][4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int s = s0 + j;
             wv[j] = __shfl_sync(0xffffffffu, wl, s & 31) * inv;
             const bool use = s < p.n_parts && wv[j] != 0.f;  // empty parts are never read
-            v[j] = use ? *reinterpret_cast<const float4*>(base + (long long)s * p.part_stride)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
             if (!use) wv[j] = 0.f;
+            v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (use) {
+                const long long si = oi + (long long)s * p.part_stride;
+                if (ll) {  // raw words now (all loads in flight), tags checked below
+                    uint64_t w0, w1, w2, w3;
+                    ll_load2_raw(lb + si, w0, w1);
+                    ll_load2_raw(lb + si + 2, w2, w3);
+                    raw[j][0] = w0;
+                    raw[j][1] = w1;
+                    raw[j][2] = w2;
+                    raw[j][3] = w3;
+                } else {
+                    v[j] = *reinterpret_cast<const float4*>(p.o_part + si);
+                }
+            }
+        }
+        if (ll) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (wv[j] == 0.f) continue;
+                const uint64_t* w = lb + oi + (long long)(s0 + j) * p.part_stride;
+                v[j] = make_float4(__uint_as_float(ll_wait1(w, epoch, raw[j][0], 21)),
+                                   __uint_as_float(ll_wait1(w + 1, epoch, raw[j][1], 21)),
+                                   __uint_as_float(ll_wait1(w + 2, epoch, raw[j][2], 21)),
+                                   __uint_as_float(ll_wait1(w + 3, epoch, raw[j][3], 21)));
+            }
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {

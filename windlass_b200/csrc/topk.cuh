@@ -17,7 +17,7 @@
 // emits, in index order, every element above thr and the first `need` equal
 // to it, positions from a block-wide exclusive scan. No sort.
 #pragma once
-#include "ptx.cuh"
+#include "p2p.cuh"
 
 namespace wl {
 
@@ -187,6 +187,11 @@ struct TopkParams {
     // [rank][row][k] result of an all-gather read as rows of rank * k entries.
     int seg_len;
     long long seg_stride;
+    // Rows arriving through the peer exchange (topk_reg_kernel only; ll.base
+    // set): `in` / `cand_idx` are unused, row r's score words start at slot 0
+    // + r * in_stride (segments = slots), its index words ll_idx_off further on.
+    P2PRecv ll;
+    long long ll_idx_off;
 };
 
 // Optional candidate outputs of a selection (the sharded decode's exchange
@@ -732,10 +737,13 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
 
 // ---- single-CTA top-k with the row in registers --------------------------------------
 // Rows of up to TOPK_THREADS * PER keys (PER consecutive per thread, read once):
-// an 8-bit first level on warp-private counters (score distributions crowd a
-// few top bins), two 12-bit refinement levels on one shared histogram, then the
-// ordered emission. (Aggregating a warp's lanes by bin with __match_any_sync
-// measured several times slower than letting shared-memory atomics serialise.)
+// the block's key range, then three radix levels over the offset from its
+// minimum (up to 11 + 11 + 10 bits, shared-memory histograms) — a range-adaptive
+// first level keeps crowded score distributions from piling onto a few bins
+// (fixed bit fields put most of a row into one or two exponent bins, and the
+// contended shared-memory atomics dominated) — then the ordered emission.
+// (Aggregating a warp's lanes by bin with __match_any_sync measured several
+// times slower than letting the shared-memory unit serialise.)
 // Supports candidate-index mapping (`cand_idx`), segmented rows and candidate
 // outputs.
 template <int PER>
@@ -744,8 +752,7 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
     WL_TRR(0);
     pdl_wait();
     pdl_trigger();
-    __shared__ uint32_t whist[TOPK_THREADS / 32][128];  // per warp: 256 16-bit counters (level 1)
-    __shared__ uint32_t hist[4096];                     // levels 2 and 3
+    __shared__ uint32_t hist[2048];
     __shared__ uint32_t scan_sh[36];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.x;
     const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
@@ -760,12 +767,27 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
     auto off = [&](int i) -> long long {
         return p.seg_len > 0 ? (long long)(i / p.seg_len) * p.seg_stride + i % p.seg_len : (long long)i;
     };
+    const bool ll = p.ll.base != nullptr;
+    const uint32_t epoch = ll ? p2p_epoch(p.ll) : 0u;
+    const uint64_t* lrow = ll ? p2p_slot(p.ll, epoch, 0) + (long long)r * p.in_stride : nullptr;
+    auto score_at = [&](int i) -> float {
+        if (!ll) return row[off(i)];
+        const uint64_t* w = lrow + off(i);
+        return __uint_as_float(ll_wait1(w, epoch, ll_load1_raw(w), 22));
+    };
+    auto key_at = [&](int i) -> int {
+        if (ll) {
+            const uint64_t* w = lrow + p.ll_idx_off + off(i);
+            return (int)ll_wait1(w, epoch, ll_load1_raw(w), 22);
+        }
+        return crow ? crow[off(i)] : i;
+    };
     if (kk >= len) {
         for (int i = tid; i < len; i += TOPK_THREADS) {
-            const int key = crow ? crow[off(i)] : i;
+            const int key = key_at(i);
             out[i] = key;
             if (co.score) {
-                co.score[(long long)r * co.stride + i] = row[off(i)];
+                co.score[(long long)r * co.stride + i] = score_at(i);
                 co.gidx[(long long)r * co.stride + i] = (int)(co.base + key);
             }
         }
@@ -778,7 +800,19 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
     {
         float f[PER];
         const long long o0 = nvalid > 0 ? off(i0) : 0;  // PER divides seg_len: one segment per thread
-        if (vec4 && nvalid == PER) {
+        if (ll) {
+            uint64_t w[PER];
+            if (nvalid == PER) {
+#pragma unroll
+                for (int j = 0; j < PER; j += 2) ll_load2_raw(lrow + o0 + j, w[j], w[j + 1]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < PER; ++j) w[j] = j < nvalid ? ll_load1_raw(lrow + o0 + j) : 0ull;
+            }
+#pragma unroll
+            for (int j = 0; j < PER; ++j)
+                f[j] = j < nvalid ? __uint_as_float(ll_wait1(lrow + o0 + j, epoch, w[j], 22)) : 0.f;
+        } else if (vec4 && nvalid == PER) {
 #pragma unroll
             for (int j = 0; j < PER; j += 4) {
                 const float4 v = *reinterpret_cast<const float4*>(row + o0 + j);
@@ -795,54 +829,78 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
         for (int j = 0; j < PER; ++j) u[j] = ordered_key(f[j]);
     }
     WL_TRR(1);
-    // ---- level 1: bits 31..24, warp-private 16-bit counters (at most 32 * PER
-    // each), so that warps never contend on a crowded bin ----
-    for (int i = lane; i < 128; i += 32) whist[warp][i] = 0;
-    for (int i = tid; i < 4096; i += TOPK_THREADS) hist[i] = 0;
-    __syncwarp();
+    // ---- the row's key range: levels bin the offset d = key - lo ----
+    uint32_t lo = 0xffffffffu, hi = 0u;
 #pragma unroll
     for (int j = 0; j < PER; ++j)
-        if ((valid >> j) & 1u) atomicAdd(&whist[warp][u[j] >> 25], 1u << (16 * ((u[j] >> 24) & 1u)));
+        if ((valid >> j) & 1u) {
+            lo = min(lo, u[j]);
+            hi = max(hi, u[j]);
+        }
+    lo = __reduce_min_sync(0xffffffffu, lo);
+    hi = __reduce_max_sync(0xffffffffu, hi);
+    if (lane == 0) {
+        scan_sh[warp] = lo;
+        hist[warp] = hi;  // hist is zeroed below, after this is read
+    }
+    __syncthreads();
+    if (warp == 0) {
+        uint32_t l = scan_sh[lane], h = hist[lane];
+        l = __reduce_min_sync(0xffffffffu, l);
+        h = __reduce_max_sync(0xffffffffu, h);
+        if (lane == 0) {
+            scan_sh[34] = l;
+            scan_sh[35] = h;
+        }
+    }
+    __syncthreads();
+    lo = scan_sh[34];
+    const uint32_t span = scan_sh[35] - lo;
+    // Level 1 takes the span's top (up to) 11 significant bits, level 2 the next
+    // 11, level 3 the rest (at most 10): the bins follow the data, so a row whose
+    // scores sit in a few binades still spreads over every bin of a level.
+    const int nbits = span ? 32 - __clz(span) : 0;
+    const int s1 = max(0, nbits - 11), s2 = max(0, s1 - 11);
+    for (int i = tid; i < 2048; i += TOPK_THREADS) hist[i] = 0;
+    __syncthreads();
+    // ---- level 1 ----
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+        if ((valid >> j) & 1u) atomicAdd(&hist[(u[j] - lo) >> s1], 1u);
     __syncthreads();
     uint32_t b1, above1;
     {
-        uint32_t c2[2] = {0u, 0u};  // thread t < 128 owns bins 2t, 2t + 1
-        if (tid < 128) {
-#pragma unroll 8
-            for (int w = 0; w < TOPK_THREADS / 32; ++w) {
-                const uint32_t x = whist[w][tid];
-                c2[0] += x & 0xffffu;
-                c2[1] += x >> 16;
-            }
-        }
+        uint32_t c2[2] = {hist[2 * tid], hist[2 * tid + 1]};
         WL_TRR(2);
         block_find_from_top<2>(c2, (uint32_t)kk, scan_sh, &b1, &above1);
         WL_TRR(3);
     }
-    // ---- levels 2 (bits 23..12) and 3 (bits 11..0) over the crossing bin's
-    // keys, one shared histogram each: once the top byte is fixed the keys
-    // spread over the low bits ----
-    uint32_t prefix = b1 << 24, mask_hi = 0xff000000u, remaining = (uint32_t)kk - above1;
+    // ---- levels 2 and 3 over the crossing bin's keys ----
+    uint32_t prefix = b1 << s1, mask_hi = s1 >= 32 ? 0u : (0xffffffffu << s1), remaining = (uint32_t)kk - above1;
+    int shift_hi = s1;
 #pragma unroll 1
     for (int pass = 0; pass < 2; ++pass) {
-        const int shift = pass == 0 ? 12 : 0;
-        if (pass == 1) {
-            for (int i = tid; i < 4096; i += TOPK_THREADS) hist[i] = 0;
-            __syncthreads();
-        }
-#pragma unroll
-        for (int j = 0; j < PER; ++j)
-            if (((valid >> j) & 1u) && (u[j] & mask_hi) == prefix) atomicAdd(&hist[(u[j] >> shift) & 4095u], 1u);
+        const int shift = pass == 0 ? s2 : 0;
+        const int nb_bits = shift_hi - shift;
+        if (nb_bits <= 0) continue;  // uniform: this level has no bits left
+        const uint32_t nb = 1u << nb_bits;
+        for (int i = tid; i < 2048; i += TOPK_THREADS) hist[i] = 0;
         __syncthreads();
-        uint32_t c4[4], b, above;  // thread t owns bins 4t .. 4t + 3
 #pragma unroll
-        for (int q = 0; q < 4; ++q) c4[q] = hist[4 * tid + q];
-        block_find_from_top<4>(c4, remaining, scan_sh, &b, &above);
+        for (int j = 0; j < PER; ++j) {
+            const uint32_t d = u[j] - lo;
+            if (((valid >> j) & 1u) && (d & mask_hi) == prefix) atomicAdd(&hist[(d >> shift) & (nb - 1u)], 1u);
+        }
+        __syncthreads();
+        uint32_t c2[2] = {2u * tid < nb ? hist[2 * tid] : 0u, 2u * tid + 1 < nb ? hist[2 * tid + 1] : 0u}, b, above;
+        block_find_from_top<2>(c2, remaining, scan_sh, &b, &above);
         prefix |= b << shift;
-        mask_hi |= 4095u << shift;
+        mask_hi |= (nb - 1u) << shift;
         remaining -= above;
+        shift_hi = shift;
         WL_TRR(4 + 3 * pass);
     }
+    prefix += lo;  // back from the offset to the key
     const uint32_t thr = prefix, need = remaining;
     // ---- ordered emission ----
     uint32_t mgt = 0, meq = 0;
@@ -867,7 +925,7 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
             ++eq_b;
         }
         if (pos >= 0) {
-            const int key = crow ? crow[off(i0 + j)] : i0 + j;
+            const int key = key_at(i0 + j);
             out[pos] = key;
             if (co.score) {
                 co.score[(long long)r * co.stride + pos] = key_to_float(u[j]);

@@ -13,27 +13,33 @@
 #include <cstdlib>
 #include <cstring>
 #include <utility>
+#include <vector>
 #include <mutex>
 #include <nccl.h>
 
 #include "../../include/wl_attn.h"
 #include "indexer.cuh"
 #include "mla_attn.cuh"
+#include "p2p.cuh"
 #include "topk.cuh"
 
 namespace {
 
 #ifdef WL_TRACE
-// Phase timeline of one host call (trace builds only): events recorded at
-// phase boundaries on the call's stream.
-cudaEvent_t g_ph_ev[32];
+// Phase timeline of one host call (trace builds only): a one-thread kernel
+// stamps the global timer at each phase boundary (works inside CUDA graphs).
+__global__ void phase_stamp_kernel(unsigned long long* buf, int i) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    buf[i] = t;
+}
+unsigned long long* g_ph_buf = nullptr;
 int g_ph_n = -1;  // -1: off
-#define WL_PHASE(st)                                                                       \
-    do {                                                                                   \
-        if (g_ph_n >= 0 && g_ph_n < 32) {                                                  \
-            if (!g_ph_ev[g_ph_n]) cudaEventCreate(&g_ph_ev[g_ph_n]);                       \
-            cudaEventRecord(g_ph_ev[g_ph_n++], st);                                        \
-        }                                                                                  \
+#define WL_PHASE(st)                                                                 \
+    do {                                                                             \
+        if (g_ph_n >= 0 && g_ph_n < 32 && g_ph_buf) {                                \
+            phase_stamp_kernel<<<1, 1, 0, st>>>(g_ph_buf, g_ph_n++);                \
+        }                                                                            \
     } while (0)
 #else
 #define WL_PHASE(st) \
@@ -311,14 +317,18 @@ int max_row_len(const wl_rows* rows, int32_t T) {
 
 // hist_ready: the histogram block of `ws` already holds this call's
 // first-level histogram (fused into the indexer) and cand_n is zero.
+bool lmax_le_reg(const wl_rows* rows, int32_t T) { return max_row_len(rows, T) <= kTopkRegMax; }
+
 // `co` (optional) also writes each selection as (score, base + key) candidates;
 // seg_len > 0 reads segmented rows (single-CTA register path only).
 int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, int32_t T, int32_t k,
                 const int32_t* cand_idx, int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
                 cudaStream_t st, const TopkWs* ws = nullptr, bool hist_ready = false,
-                const wl::CandOut* co = nullptr, int32_t seg_len = 0, int64_t seg_stride = 0) {
+                const wl::CandOut* co = nullptr, int32_t seg_len = 0, int64_t seg_stride = 0,
+                const wl::P2PRecv* ll = nullptr, int64_t ll_idx_off = 0) {
     const wl::CandOut cout = co ? *co : wl::CandOut{};
-    if (!index || !sel_out || k <= 0) return WL_ERR_ARG;
+    if (ll && !(lmax_le_reg(rows, T))) return WL_ERR_ARG;
+    if ((!index && !ll) || !sel_out || k <= 0) return WL_ERR_ARG;
     if (sel_stride < (k < T ? k : T)) return WL_ERR_ARG;
     const int lmax = max_row_len(rows, T);
     const bool cluster = lmax > kTopkClusterMin && lmax <= kTopkClusterMax;
@@ -393,6 +403,10 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
     p.n_out = sel_n_out;
     p.seg_len = seg_len;
     p.seg_stride = seg_stride;
+    if (ll) {
+        p.ll = *ll;
+        p.ll_idx_off = ll_idx_off;
+    }
     if (lmax <= kTopkRegMax) {
         const int vec4 = aligned16(index) && (index_stride & 3) == 0 && (seg_stride & 3) == 0;
         const dim3 g(rows->n_rows), b(wl::TOPK_THREADS);
@@ -482,14 +496,18 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
 int launch_merge(const float* o_part, const float* lse_part, int32_t n_rows, int32_t n_parts, int64_t row_stride,
                  int64_t part_stride, int64_t lse_row_stride, int64_t lse_part_stride, int32_t n_heads,
                  int32_t dv, float* ctx, float* lse, cudaStream_t st, int64_t ctx_row_stride = 0,
-                 int64_t lse_out_row_stride = 0) {
-    if (!o_part || !lse_part || !ctx || n_rows <= 0 || n_parts <= 0 || n_parts > 32 || (dv % 128) ||
+                 int64_t lse_out_row_stride = 0, const wl::P2PRecv* ll = nullptr, int64_t ll_lse_off = 0) {
+    if ((!ll && (!o_part || !lse_part)) || !ctx || n_rows <= 0 || n_parts <= 0 || n_parts > 32 || (dv % 128) ||
         n_heads <= 0 || n_rows > 65535)
         return WL_ERR_ARG;
     wl::MergeParams p{o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
                       lse_part_stride, n_heads, dv, ctx, lse,
                       ctx_row_stride > 0 ? ctx_row_stride : (int64_t)n_heads * dv,
                       lse_out_row_stride > 0 ? lse_out_row_stride : (int64_t)n_heads};
+    if (ll) {
+        p.ll = *ll;
+        p.ll_lse_off = ll_lse_off;
+    }
     WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
@@ -537,8 +555,9 @@ DecodeWs carve_decode(void* base, const wl_attn_cfg* cfg, int32_t T_max, int32_t
         if (base) w.topk = topk_ws_carve(tb, batch, T_max);
     }
     if (nranks > 1) {
-        w.cand_score = static_cast<float*>(take((size_t)batch * k * 4));
-        w.cand_idx = static_cast<int32_t*>(take((size_t)batch * k * 4));
+        // one block [scores B x k][indices B x k]: the peer exchange sends it whole
+        w.cand_score = static_cast<float*>(take((size_t)batch * k * 8));
+        w.cand_idx = reinterpret_cast<int32_t*>(w.cand_score + (size_t)batch * k);
         w.cand_score_all = static_cast<float*>(take((size_t)nranks * batch * k * 4));
         w.cand_idx_all = static_cast<int32_t*>(take((size_t)nranks * batch * k * 4));
         w.cand_score_rows = static_cast<float*>(take((size_t)nranks * batch * k * 4));
@@ -614,11 +633,133 @@ __global__ void candidates_to_rows_kernel(const float* s_all, const int* i_all, 
 
 }  // namespace
 
+// Capacity of the peer exchange (rows per call, selection length) and its
+// region layout; larger calls use the NCCL exchange.
+constexpr int kP2PMaxRows = 32;
+constexpr int kP2PMaxK = 4096;
+// Slots hold the wire format: 8 bytes per 4-byte payload word.
+constexpr long long kP2PCandSlot = (long long)kP2PMaxRows * kP2PMaxK * 2 * 8;                    // scores, indices
+constexpr long long kP2PPartSlot = (long long)kP2PMaxRows * (wl::AT_H * wl::AT_DV + wl::AT_H) * 8;  // (o, lse) rows
+
 struct wl_comm {
     ncclComm_t comm;
     int32_t nranks;
     int32_t rank;
+    // Peer exchange over NVLink (absent: p2p == false, NCCL carries both exchanges).
+    bool p2p;
+    uint8_t* region;                           // this rank's exchange region
+    uint8_t* peer[wl::P2P_MAX_RANKS];          // every rank's region, mapped here (peer[rank] = region)
+    unsigned* ctr;                             // epoch / CTA-done counters
 };
+
+namespace {
+
+long long p2p_off_part(int nranks) { return wl::P2P_OFF_CAND + nranks * kP2PCandSlot; }
+size_t p2p_region_bytes(int nranks) { return (size_t)(p2p_off_part(nranks) + 2LL * nranks * kP2PPartSlot); }
+
+bool p2p_allowed() {
+    static const bool on = [] {
+        const char* e = std::getenv("WL_NO_P2P");
+        return !(e && e[0] == '1');
+    }();
+    return on;
+}
+
+void p2p_release(wl_comm* c) {
+    for (int p = 0; p < c->nranks && p < wl::P2P_MAX_RANKS; ++p)
+        if (c->peer[p] && c->peer[p] != c->region) cudaIpcCloseMemHandle(c->peer[p]);
+    if (c->region) cudaFree(c->region);
+    if (c->ctr) cudaFree(c->ctr);
+    c->region = nullptr;
+    c->ctr = nullptr;
+    for (auto& q : c->peer) q = nullptr;
+    c->p2p = false;
+}
+
+// Collective: every rank allocates its region and maps every peer's through
+// CUDA IPC handles all-gathered over NCCL. Any failure on any rank leaves the
+// peer exchange off everywhere (the outcome is all-reduced).
+void p2p_setup(wl_comm* c) {
+    const int N = c->nranks;
+    if (N < 2 || N > wl::P2P_MAX_RANKS || !p2p_allowed()) return;
+    int ok = 1;
+    cudaIpcMemHandle_t mine{};
+    if (cudaMalloc(&c->region, p2p_region_bytes(N)) != cudaSuccess ||
+        cudaMemset(c->region, 0, p2p_region_bytes(N)) != cudaSuccess ||
+        cudaMalloc(&c->ctr, 64) != cudaSuccess || cudaMemset(c->ctr, 0, 64) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine, c->region) != cudaSuccess)
+        ok = 0;
+    cudaGetLastError();
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaStream_t st = nullptr;
+    uint8_t* dev = nullptr;
+    std::vector<uint8_t> all((size_t)N * 64);
+    bool comm_ok = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
+                   cudaMalloc(&dev, (size_t)N * 64 + 4 * N) == cudaSuccess &&
+                   cudaMemcpy(dev + (size_t)c->rank * 64, &mine, 64, cudaMemcpyHostToDevice) == cudaSuccess;
+    comm_ok = comm_ok && ncclAllGather(dev + (size_t)c->rank * 64, dev, 64, ncclUint8, c->comm, st) == ncclSuccess &&
+              cudaStreamSynchronize(st) == cudaSuccess &&
+              cudaMemcpy(all.data(), dev, (size_t)N * 64, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (comm_ok && ok) {
+        for (int p = 0; p < N; ++p) {
+            if (p == c->rank) {
+                c->peer[p] = c->region;
+                continue;
+            }
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, all.data() + (size_t)p * 64, 64);
+            void* ptr = nullptr;
+            if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                ok = 0;
+                cudaGetLastError();
+                break;
+            }
+            c->peer[p] = static_cast<uint8_t*>(ptr);
+        }
+    }
+    // Agree: the exchange is on only if every rank set it up.
+    int* flag = reinterpret_cast<int*>(dev + (size_t)N * 64);
+    int agreed = 0;
+    if (comm_ok) {
+        const int v = (ok && comm_ok) ? 1 : 0;
+        comm_ok = cudaMemcpy(flag, &v, 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+                  ncclAllReduce(flag, flag, 1, ncclInt32, ncclMin, c->comm, st) == ncclSuccess &&
+                  cudaStreamSynchronize(st) == cudaSuccess &&
+                  cudaMemcpy(&agreed, flag, 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    if (dev) cudaFree(dev);
+    if (st) cudaStreamDestroy(st);
+    c->p2p = comm_ok && agreed == 1;
+    if (!c->p2p) p2p_release(c);
+}
+
+wl::P2PArgs p2p_args(const wl_comm* c) {
+    wl::P2PArgs a{};
+    for (int p = 0; p < c->nranks; ++p) a.region[p] = c->peer[p];
+    a.nranks = c->nranks;
+    a.rank = c->rank;
+    a.ctr = c->ctr;
+    return a;
+}
+
+// `bytes` of payload (a multiple of 8) from `src` into slot `rank` of every region.
+int launch_put(const wl_comm* c, int type, const void* src, size_t bytes, long long dst_off, long long slot_bytes,
+               long long parity_bytes, cudaStream_t st) {
+    if (bytes % 8) return WL_ERR_ARG;
+    const long long n32 = (long long)(bytes / 4);
+    int grid = (int)ceil_div(n32 / 2, 256 * 2);
+    grid = grid < 1 ? 1 : (grid > sm_count() ? sm_count() : grid);
+    WL_CUDA_TRY(launch_pdl(wl::p2p_put_kernel, dim3(grid), dim3(256), 0, st, p2p_args(c), type,
+                           static_cast<const uint32_t*>(src), n32, dst_off, slot_bytes, parity_bytes));
+    return WL_OK;
+}
+
+wl::P2PRecv p2p_recv(const wl_comm* c, int type, long long off, long long slot_bytes, long long parity_bytes) {
+    return wl::P2PRecv{reinterpret_cast<const uint64_t*>(c->region + off), slot_bytes / 8, parity_bytes / 8,
+                       c->ctr + type};
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -986,12 +1127,25 @@ int wl_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank, wl_comm*
         delete c;
         return WL_ERR_NCCL;
     }
+    p2p_setup(c);
     *out = c;
     return WL_OK;
 }
 
 int wl_comm_destroy(wl_comm* c) {
     if (!c) return WL_ERR_ARG;
+    cudaDeviceSynchronize();  // this rank's exchanges are done
+    if (c->p2p) {
+        // Collective: no rank frees its region while a peer's put may still write it.
+        int* one = nullptr;
+        cudaStream_t st = nullptr;
+        if (cudaMalloc(&one, 4) == cudaSuccess && cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
+            ncclAllReduce(one, one, 1, ncclInt32, ncclSum, c->comm, st) == ncclSuccess)
+            cudaStreamSynchronize(st);
+        if (st) cudaStreamDestroy(st);
+        if (one) cudaFree(one);
+    }
+    p2p_release(c);
     const ncclResult_t r = ncclCommDestroy(c->comm);
     delete c;
     return r == ncclSuccess ? WL_OK : WL_ERR_NCCL;
@@ -1015,6 +1169,11 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     const int32_t B = io->batch, T = io->T, k = cfg->index_topk;
     const int64_t Tg = shard->T_global, t0 = shard->t0;
     const int32_t kg = (int32_t)(k < Tg ? k : Tg);
+    const int64_t rowsz = wl::AT_H * wl::AT_DV + wl::AT_H;
+    // Peer exchange when the comm has it and this call fits its slots (and the
+    // global top-k can read the candidate slots as segmented rows).
+    const bool p2p = comm->p2p && B <= kP2PMaxRows && k <= kP2PMaxK && (k % 32) == 0 &&
+                     (int64_t)N * k <= kTopkRegMax;
     WL_PHASE(st);
 
     const int32_t* gsel = nullptr;
@@ -1045,30 +1204,44 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
             WL_CUDA_TRY(cudaGetLastError());
         }
         WL_PHASE(st);
-        if (ncclGroupStart() != ncclSuccess) return WL_ERR_NCCL;
-        if (ncclAllGather(w.cand_score, w.cand_score_all, (size_t)B * k, ncclFloat32, comm->comm, st) != ncclSuccess ||
-            ncclAllGather(w.cand_idx, w.cand_idx_all, (size_t)B * k, ncclInt32, comm->comm, st) != ncclSuccess) {
-            ncclGroupEnd();
-            return WL_ERR_NCCL;
-        }
-        if (ncclGroupEnd() != ncclSuccess) return WL_ERR_NCCL;
-        WL_PHASE(st);
-        // Exact global top-k over the candidates; candidate order (rank-major,
-        // ascending within a rank) is global key order, so position ties resolve
-        // to the lowest global index. The all-gathered [rank][row][k] buffers are
-        // read in place as rows of N segments of k.
         const wl_rows crows{B, 1, N * k, 0};
-        if ((k % 32) == 0 && (int64_t)N * k <= kTopkRegMax) {
-            if (int e = launch_topk(w.cand_score_all, k, &crows, N * k, kg, w.cand_idx_all, io->sel_out,
-                                    io->sel_stride, io->sel_n_out, st, nullptr, false, nullptr, k, (int64_t)B * k))
+        if (p2p) {
+            // Candidates to every rank's slot `rank`; the global top-k waits for all
+            // N slots and reads them in place as rows of N segments of k.
+            if (int e = launch_put(comm, wl::XCH_CAND, w.cand_score, (size_t)B * k * 8, wl::P2P_OFF_CAND, kP2PCandSlot, 0,
+                                   st))
+                return e;
+            WL_PHASE(st);
+            const wl::P2PRecv rc = p2p_recv(comm, wl::XCH_CAND, wl::P2P_OFF_CAND, kP2PCandSlot, 0);
+            if (int e = launch_topk(nullptr, k, &crows, N * k, kg, nullptr, io->sel_out, io->sel_stride, io->sel_n_out,
+                                    st, nullptr, false, nullptr, k, rc.slot_words, &rc, (int64_t)B * k))
                 return e;
         } else {
-            candidates_to_rows_kernel<<<256, 256, 0, st>>>(w.cand_score_all, w.cand_idx_all, N, B, k,
-                                                          w.cand_score_rows, w.cand_idx_rows);
-            WL_CUDA_TRY(cudaGetLastError());
-            if (int e = launch_topk(w.cand_score_rows, (int64_t)N * k, &crows, N * k, kg, w.cand_idx_rows,
-                                    io->sel_out, io->sel_stride, io->sel_n_out, st))
-                return e;
+            if (ncclGroupStart() != ncclSuccess) return WL_ERR_NCCL;
+            if (ncclAllGather(w.cand_score, w.cand_score_all, (size_t)B * k, ncclFloat32, comm->comm, st) !=
+                    ncclSuccess ||
+                ncclAllGather(w.cand_idx, w.cand_idx_all, (size_t)B * k, ncclInt32, comm->comm, st) != ncclSuccess) {
+                ncclGroupEnd();
+                return WL_ERR_NCCL;
+            }
+            if (ncclGroupEnd() != ncclSuccess) return WL_ERR_NCCL;
+            WL_PHASE(st);
+            // Exact global top-k over the candidates; candidate order (rank-major,
+            // ascending within a rank) is global key order, so position ties
+            // resolve to the lowest global index. The all-gathered [rank][row][k]
+            // buffers are read in place as rows of N segments of k.
+            if ((k % 32) == 0 && (int64_t)N * k <= kTopkRegMax) {
+                if (int e = launch_topk(w.cand_score_all, k, &crows, N * k, kg, w.cand_idx_all, io->sel_out,
+                                        io->sel_stride, io->sel_n_out, st, nullptr, false, nullptr, k, (int64_t)B * k))
+                    return e;
+            } else {
+                candidates_to_rows_kernel<<<256, 256, 0, st>>>(w.cand_score_all, w.cand_idx_all, N, B, k,
+                                                              w.cand_score_rows, w.cand_idx_rows);
+                WL_CUDA_TRY(cudaGetLastError());
+                if (int e = launch_topk(w.cand_score_rows, (int64_t)N * k, &crows, N * k, kg, w.cand_idx_rows,
+                                        io->sel_out, io->sel_stride, io->sel_n_out, st))
+                    return e;
+            }
         }
         WL_PHASE(st);
         if (io->index_out) {
@@ -1100,7 +1273,6 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     }
     // Local partial over this rank's window, merged over its splits straight
     // into the exchange layout [row][64 * 512 + 64].
-    const int64_t rowsz = wl::AT_H * wl::AT_DV + wl::AT_H;
     long long n_max = Tg;
     int32_t sel_n = 0;
     if (io->mode == WL_MODE_OWNER) n_max = kg;
@@ -1112,11 +1284,23 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
                              gstride, n_max, st, rowsz, rowsz))
         return e;
     const size_t per = (size_t)B * rowsz;
+    float* lse = io->lse ? io->lse : w.lse_tmp;
+    if (p2p) {
+        WL_PHASE(st);
+        if (int e = launch_put(comm, wl::XCH_PART, w.part_send, per * 4, p2p_off_part(N), kP2PPartSlot,
+                               (long long)N * kP2PPartSlot, st))
+            return e;
+        WL_PHASE(st);
+        const wl::P2PRecv rp = p2p_recv(comm, wl::XCH_PART, p2p_off_part(N), kP2PPartSlot, (long long)N * kP2PPartSlot);
+        const int em = launch_merge(nullptr, nullptr, B, N, rowsz, rp.slot_words, rowsz, rp.slot_words, wl::AT_H,
+                                    wl::AT_DV, io->ctx, lse, st, 0, 0, &rp, wl::AT_H * wl::AT_DV);
+        WL_PHASE(st);
+        return em;
+    }
     WL_PHASE(st);
     if (ncclAllGather(w.part_send, w.part_recv, per, ncclFloat32, comm->comm, st) != ncclSuccess) return WL_ERR_NCCL;
     WL_PHASE(st);
     // part_recv: [rank][row][64*512 + 64]
-    float* lse = io->lse ? io->lse : w.lse_tmp;
     const int em = launch_merge(w.part_recv, w.part_recv + wl::AT_H * wl::AT_DV, B, N, rowsz, (int64_t)B * rowsz,
                                 rowsz, (int64_t)B * rowsz, wl::AT_H, wl::AT_DV, io->ctx, lse, st);
     WL_PHASE(st);
@@ -1124,15 +1308,26 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
 }
 
 #ifdef WL_TRACE
-void wl_phase_begin() { g_ph_n = 0; }
-// Milliseconds between consecutive phase events; returns their count.
-int wl_phase_read(float* ms, int max_n) {
+// One candidate-type put of `bytes` from `src` (exchange microbenchmarks).
+int wl_trace_put(wl_comm* c, const void* src, size_t bytes, void* stream) {
+    if (!c || !c->p2p) return WL_ERR_ARG;
+    return launch_put(c, wl::XCH_CAND, src, bytes, wl::P2P_OFF_CAND, kP2PCandSlot, 0, static_cast<cudaStream_t>(stream));
+}
+void wl_phase_begin() {
+    if (!g_ph_buf) cudaMalloc(&g_ph_buf, 32 * sizeof(unsigned long long));
+    g_ph_n = 0;
+}
+// Microseconds between consecutive stamps of the last stamped call (or graph
+// replay); returns their count. Stops stamping.
+int wl_phase_read(float* us, int max_n) {
     const int n = g_ph_n;
     g_ph_n = -1;
-    if (n <= 0) return 0;
-    cudaEventSynchronize(g_ph_ev[n - 1]);
+    if (n <= 1 || !g_ph_buf) return 0;
+    unsigned long long h[32];
+    cudaDeviceSynchronize();
+    cudaMemcpy(h, g_ph_buf, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
     int m = 0;
-    for (int i = 1; i < n && m < max_n; ++i) cudaEventElapsedTime(&ms[m++], g_ph_ev[i - 1], g_ph_ev[i]);
+    for (int i = 1; i < n && m < max_n; ++i) us[m++] = (float)((h[i] - h[i - 1]) * 1e-3);
     return m;
 }
 int wl_atrace_set(long long* buf) {
