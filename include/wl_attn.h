@@ -259,18 +259,25 @@ int wl_lse_merge(const float* o_part, const float* lse_part, int32_t n_rows,
                  int32_t n_heads, int32_t kv_lora,
                  float* ctx, float* lse, void* stream);
 
-/* ---- KV-sequence sharding over the GPUs of one node (NCCL) ----------------
+/* ---- KV-sequence sharding over the GPUs of one node ------------------------
  * Rank r holds keys [t0, t0 + io->T) of every cache. Each rank scores and
- * selects locally; one NCCL all-gather merges the (score, global index)
- * candidates into the exact single-GPU selection, each rank attends over its
+ * selects locally; an all-gather of the (score, global index) candidates
+ * gives every rank the exact single-GPU selection, each rank attends over its
  * part of it, and a second all-gather merges the (o, lse) partials. Every
  * rank returns the full ctx/lse and (owner) the global selection. No reference
- * counterpart: the reference is single-GPU (README.md:88). */
+ * counterpart: the reference is single-GPU (README.md:88).
+ * The all-gathers run over NVLink peer memory (each rank writes into every
+ * rank's exchange region; wl_comm_create maps them, collectively, through CUDA
+ * IPC), or over NCCL when that is unavailable, disabled (WL_NO_P2P=1) or a call
+ * exceeds the regions' capacity (32 rows, index_topk 4096). Creation and
+ * destruction are collective. */
 typedef struct wl_comm wl_comm;
 int wl_comm_unique_id(uint8_t id_out[128]);
 int wl_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank,
                    wl_comm** out);
 int wl_comm_destroy(wl_comm* comm);
+/* 1 when this communicator exchanges over NVLink peer memory, 0 over NCCL. */
+int wl_comm_p2p(const wl_comm* comm);
 
 typedef struct wl_shard {
     int64_t t0;        /* global position of this rank's cache row 0 */

@@ -1,9 +1,12 @@
-"""KV-sequence sharding over 2 GPUs through wl_attn_decode_sharded (NCCL).
+"""KV-sequence sharding over 2 GPUs through wl_attn_decode_sharded, with the
+exchanges over NVLink peer memory and over NCCL (WL_NO_P2P=1).
 
 Rank r holds keys [r*T/2, (r+1)*T/2) of every cache. The selection must equal
 the single-GPU selection exactly (a key's score does not depend on where it
 lives), and ctx must agree with the single-GPU result within 2 bf16 ulp of the
-output scale. Runs as two child processes; skipped with fewer than 2 GPUs."""
+output scale — on every one of several consecutive owner and consumer steps
+(the peer exchange tags each step with an epoch and alternates partial
+buffers). Runs as two child processes; skipped with fewer than 2 GPUs."""
 import os
 import socket
 
@@ -23,7 +26,9 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, T, B, out_path):
+def _worker(rank, world, port, T, B, out_path, exchange):
+    if exchange == "nccl":
+        os.environ["WL_NO_P2P"] = "1"
     import torch.distributed as dist
 
     from oracle import attn_ref as o
@@ -43,14 +48,17 @@ def _worker(rank, world, port, T, B, out_path):
     q_abs, q_idx, w_idx = d(st("q_abs"), torch.bfloat16), d(st("q_idx"), torch.bfloat16), d(st("w_idx"), torch.float32)
     cfg = A.glm52_cfg(T)
     comm = A.Comm(rank, world)
-    out = A.attn_decode_sharded(cfg, comm, lo, T, kv, q_abs, keys=keys, q_idx=q_idx, w_idx=w_idx)
-    torch.cuda.synchronize()
-    res = dict(sel=out["sel"].cpu().numpy(), ctx=out["ctx"].cpu().numpy(), lse=out["lse"].cpu().numpy())
-    # consumer layer reusing the global selection
-    con = A.attn_decode_sharded(cfg, comm, lo, T, kv, q_abs, mode=_lib.WL_MODE_CONSUMER, sel_in=out["sel"],
-                                sel_n_in=out["sel_n"], canonical=True)
-    torch.cuda.synchronize()
-    res["ctx_con"] = con["ctx"].cpu().numpy()
+    res = dict(p2p=np.array(int(comm.p2p)))
+    for step in range(3):
+        out = A.attn_decode_sharded(cfg, comm, lo, T, kv, q_abs, keys=keys, q_idx=q_idx, w_idx=w_idx)
+        # consumer layers reusing the global selection (one, then two in a row)
+        for c in range(1 + step % 2):
+            con = A.attn_decode_sharded(cfg, comm, lo, T, kv, q_abs, mode=_lib.WL_MODE_CONSUMER, sel_in=out["sel"],
+                                        sel_n_in=out["sel_n"], canonical=True)
+            torch.cuda.synchronize()
+            res[f"ctx_con{step}_{c}"] = con["ctx"].cpu().numpy()
+        res[f"sel{step}"] = out["sel"].cpu().numpy()
+        res[f"ctx{step}"] = out["ctx"].cpu().numpy()
     st_, word = A.device_error(clear=True)
     res["err"] = st_
     if rank == 0:
@@ -66,17 +74,22 @@ def _worker(rank, world, port, T, B, out_path):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
 @pytest.mark.parametrize("T", [20000, 100000])
-def test_sharded_decode_two_gpus(tmp_path, T):
+def test_sharded_decode_two_gpus(tmp_path, T, exchange):
     from oracle import attn_ref as o
     B = 2
     path = str(tmp_path / "res")
-    mp.start_processes(_worker, args=(2, _free_port(), T, B, path), nprocs=2, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), T, B, path, exchange), nprocs=2, start_method="spawn")
     r0, r1 = (dict(np.load(path + f".{r}.npz")) for r in range(2))
     assert int(r0["err"]) == 0 and int(r1["err"]) == 0
-    for s in range(B):
-        assert np.array_equal(r0["sel"][s], r0["sel1"][s]), "sharded selection differs from single-GPU"
-        assert np.array_equal(r0["sel"][s], r1["sel"][s])
-        assert o.bf16_ulp_error(r0["ctx1"][s], r0["ctx"][s]) <= 2.0
-        assert o.bf16_ulp_error(r0["ctx1"][s], r1["ctx"][s]) <= 2.0
-        assert o.bf16_ulp_error(r0["ctx"][s], r0["ctx_con"][s]) <= 2.0
+    assert int(r0["p2p"]) == (exchange == "p2p") and int(r1["p2p"]) == (exchange == "p2p")
+    for step in range(3):
+        for s in range(B):
+            sel = r0[f"sel{step}"][s]
+            assert np.array_equal(sel, r0["sel1"][s]), f"step {step}: sharded selection differs from single-GPU"
+            assert np.array_equal(sel, r1[f"sel{step}"][s])
+            for r in (r0, r1):
+                assert o.bf16_ulp_error(r0["ctx1"][s], r[f"ctx{step}"][s]) <= 2.0
+                for c in range(1 + step % 2):
+                    assert o.bf16_ulp_error(r0["ctx1"][s], r[f"ctx_con{step}_{c}"][s]) <= 2.0

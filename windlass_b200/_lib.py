@@ -97,6 +97,7 @@ SIGNATURES = {
     "wl_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "wl_comm_create": (C.c_int, [C.POINTER(C.c_uint8), i32, i32, C.POINTER(vp)]),
     "wl_comm_destroy": (C.c_int, [vp]),
+    "wl_comm_p2p": (C.c_int, [vp]),
     "wl_attn_sharded_workspace_bytes": (C.c_size_t, [C.POINTER(AttnCfg), i32, i32, i32]),
     "wl_attn_decode_sharded": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(DecodeIO),
                                          C.POINTER(Shard), vp, vp, C.c_size_t, vp]),

@@ -368,7 +368,8 @@ def device_error(clear: bool = True) -> tuple[int, int]:
 # ---- KV-sequence sharding ---------------------------------------------------------------------
 
 class Comm:
-    """NCCL communicator of the library, bootstrapped through torch.distributed."""
+    """The library's communicator (NVLink peer exchange, else NCCL), bootstrapped
+    through torch.distributed. Creation and close() are collective."""
 
     def __init__(self, rank: int, world: int, group=None):
         import torch.distributed as dist
@@ -381,6 +382,11 @@ class Comm:
         h = C.c_void_p()
         check(lib().wl_comm_create(uid, world, rank, C.byref(h)), "wl_comm_create")
         self.h, self.rank, self.world = h, rank, world
+
+    @property
+    def p2p(self) -> bool:
+        """True when the exchanges run over NVLink peer memory."""
+        return bool(lib().wl_comm_p2p(self.h))
 
     def close(self) -> None:
         if self.h:

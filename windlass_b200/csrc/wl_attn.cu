@@ -1132,6 +1132,8 @@ int wl_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank, wl_comm*
     return WL_OK;
 }
 
+int wl_comm_p2p(const wl_comm* c) { return c && c->p2p ? 1 : 0; }
+
 int wl_comm_destroy(wl_comm* c) {
     if (!c) return WL_ERR_ARG;
     cudaDeviceSynchronize();  // this rank's exchanges are done
