@@ -223,9 +223,11 @@ namespace wl {
 // head weight absorbs 1/s_h: w_h relu(x / s_h) = (w_h / s_h) relu(x), s_h > 0.
 //
 // The epilogue can also accumulate, per row, the histogram of the top
-// TOPK_HIST_BITS bits of the order-preserving score keys (warp-aggregated
-// global atomics) — the first radix pass of the top-k, fused here so that no
-// kernel re-reads the scores for it.
+// TOPK_HIST_BITS bits of the order-preserving score keys — the first radix pass
+// of the top-k, fused here so that no kernel re-reads the scores for it. Each
+// CTA counts into shared memory and adds its nonzero bins to the row's global
+// histogram at the end (warp-aggregating global atomics with __match_any_sync
+// measured slower).
 constexpr int IDX_NS = 8;    // TMA stages of fp8 keys
 constexpr int IDX_CTAS_PER_SM = 1;
 constexpr int IDX_NACC = 4;  // accumulator sets (hi, lo) in flight
@@ -240,8 +242,10 @@ struct IdxStreamLayout {
     static constexpr uint32_t OFF_K8 = 0;
     static constexpr uint32_t OFF_Q = OFF_K8 + IDX_NS * K8_TILE;  // hi, lo
     static constexpr uint32_t OFF_W = OFF_Q + 2 * QT;
-    static constexpr uint32_t OFF_BAR = OFF_W + IDX_H * 4;
-    static constexpr int N_BARS = 2 * IDX_NS + 2 * IDX_NACC;  // full, empty, acc_full, acc_empty
+    static constexpr uint32_t OFF_HIST = OFF_W + IDX_H * 4;  // this CTA's share of the row histogram
+    static constexpr uint32_t OFF_QRAW = OFF_HIST + TOPK_HIST_BINS * 4;  // the row's bf16 query, as copied
+    static constexpr uint32_t OFF_BAR = OFF_QRAW + IDX_H * IDX_D * 2;
+    static constexpr int N_BARS = 2 * IDX_NS + 2 * IDX_NACC + 1;  // full, empty, acc_full, acc_empty, query
     static constexpr uint32_t OFF_SLOT = OFF_BAR + N_BARS * 8;
     static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;
     static constexpr uint32_t TMEM_COLS = 64 * IDX_NACC;  // 256
@@ -282,6 +286,22 @@ struct IdxStreamParams {
 
 #ifdef WL_TRACE
 __device__ long long* g_trace;
+#define WL_TRB(slot)                                                                                    \
+    do {                                                                                                \
+        if (g_trace && threadIdx.x == 0) {                                                              \
+            unsigned long long t_;                                                                      \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
+            g_trace[512 + 2 * (blockIdx.y * gridDim.x + blockIdx.x) + (slot)] = (long long)t_;          \
+        }                                                                                               \
+    } while (0)
+#define WL_TRP(slot)                                                                                    \
+    do {                                                                                                \
+        if (g_trace && blockIdx.x == 0 && blockIdx.y == 0) {                                            \
+            unsigned long long t_;                                                                      \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
+            g_trace[900 + (slot)] = (long long)t_;                                                      \
+        }                                                                                               \
+    } while (0)
 #define WL_TR(slot, i)                                                                                  \
     do {                                                                                                \
         if (g_trace && blockIdx.x == 0 && blockIdx.y == 0 && (i) < 64) g_trace[(i) * 8 + (slot)] = clock64(); \
@@ -290,21 +310,31 @@ __device__ long long* g_trace;
 #define WL_TR(slot, i) \
     do {               \
     } while (0)
+#define WL_TRB(slot) \
+    do {             \
+    } while (0)
+#define WL_TRP(slot) \
+    do {             \
+    } while (0)
 #endif
 
 __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
     indexer_stream_kernel(IdxParams p, const __grid_constant__ IdxStreamParams sp, unsigned* hist, int tiles_per_cta) {
     using L = IdxStreamLayout;
     WL_KT_BEGIN(0);
+    WL_TRB(0);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* k8 = smem + L::OFF_K8;
     uint8_t* sQ = smem + L::OFF_Q;
     float* sW = reinterpret_cast<float*>(smem + L::OFF_W);
+    unsigned* sHist = reinterpret_cast<unsigned*>(smem + L::OFF_HIST);
+    const __nv_bfloat16* sQraw = reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_QRAW);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* empty = full + IDX_NS;
     uint64_t* acc_full = empty + IDX_NS;
     uint64_t* acc_empty = acc_full + IDX_NACC;
+    uint64_t* qbar = acc_empty + IDX_NACC;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_SLOT);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -331,27 +361,52 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
             mbar_init(acc_full + b, 1);
             mbar_init(acc_empty + b, 128);
         }
+        mbar_init(qbar, 1);
         fence_mbar_init();
+        // The producer (this thread) copies the row's query (8 KB) at once, so
+        // that it lands during the setup below, ahead of the key stream; every
+        // other warp converts it from shared memory. (Loading it with per-warp
+        // global loads queued behind the key stream, and issuing the first key
+        // tiles together with it let them overtake it: both delayed the first
+        // MMA by microseconds.)
+        pdl_wait();
+        mbar_expect_tx(qbar, IDX_H * IDX_D * 2);
+        bulk_g2s(smem + L::OFF_QRAW, p.q + (long long)r * IDX_H * IDX_D, IDX_H * IDX_D * 2, qbar);
     }
     if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);  // warp 1 allocates and frees
+    if (hist)
+        for (int b = tid; b < TOPK_HIST_BINS; b += IDX_STREAM_THREADS) sHist[b] = 0;
     tc_fence_before();
     __syncthreads();  // barriers initialised, TMEM address published
     tc_fence_after();
+    if (tid == 0) WL_TRP(0);
     pdl_wait();  // everything above overlaps the previous kernel; global data below
     pdl_trigger();
     const uint32_t tmem = *tmem_slot;
     const bool producer = warp == 0;
-    // Query -> two e4m3 terms per head, by every warp but the producer, which
-    // starts streaming keys at once; a named barrier joins the other warps.
-    for (int h = warp - 1; !producer && h < IDX_H; h += IDX_STREAM_THREADS / 32 - 1) {
-        const __nv_bfloat16* qh = p.q + ((long long)r * IDX_H + h) * IDX_D;
-        float x[4];
+    // Query -> two e4m3 terms per head, by every warp but the producer; a named
+    // barrier joins them.
+    constexpr int CONV_WARPS = IDX_STREAM_THREADS / 32 - 1;
+    float wv[(IDX_H + CONV_WARPS - 1) / CONV_WARPS];  // head weights, loaded while the query lands
+    if (!producer) {
+#pragma unroll
+        for (int k2 = 0; k2 < (IDX_H + CONV_WARPS - 1) / CONV_WARPS; ++k2) {
+            const int h = warp - 1 + k2 * CONV_WARPS;
+            wv[k2] = (lane == 0 && h < IDX_H) ? __ldg(p.w + (long long)r * IDX_H + h) : 0.f;
+        }
+        mbar_wait(qbar, 0, 9);
+    }
+#pragma unroll
+    for (int k2 = 0; k2 < (IDX_H + CONV_WARPS - 1) / CONV_WARPS; ++k2) {
+        const int h = warp - 1 + k2 * CONV_WARPS;
+        if (producer || h >= IDX_H) break;
+        const uint2 raw = *reinterpret_cast<const uint2*>(sQraw + h * IDX_D + lane * 4);
+        const __nv_bfloat162 q01 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+        const __nv_bfloat162 q23 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+        float x[4] = {__low2float(q01), __high2float(q01), __low2float(q23), __high2float(q23)};
         float mx = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            x[e] = __bfloat162float(qh[lane * 4 + e]);
-            mx = fmaxf(mx, fabsf(x[e]));
-        }
+        for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(x[e]));
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         // s_h = 2^(7 - floor(log2 mx)): the largest element lands in [128, 256).
         const int ex = mx > 0.f ? max(((__float_as_int(mx) >> 23) & 0xff) - 127, -100) : 0;
@@ -373,8 +428,9 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
         const uint32_t off = (uint32_t)h * 128u + ((((byte >> 4) ^ (uint32_t)h) & 7u) << 4) + (byte & 15u);
         *reinterpret_cast<uint32_t*>(sQ + off) = hi4;
         *reinterpret_cast<uint32_t*>(sQ + L::QT + off) = lo4;
-        if (lane == 0) sW[h] = __ldg(p.w + (long long)r * IDX_H + h) / s_h;
+        if (lane == 0) sW[h] = wv[k2] / s_h;
     }
+    if (tid == 32) WL_TRP(1);
     if (!producer) {
         fence_proxy_async_smem();  // the query tile is read by the tensor cores
         asm volatile("bar.sync 1, %0;" ::"n"(IDX_STREAM_THREADS - 32) : "memory");
@@ -387,6 +443,7 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
             if (i >= IDX_NS && !mbar_wait(empty + s, (uint32_t)(i / IDX_NS - 1) & 1u, 10)) break;
             if (lane == 0) {
                 WL_TR(0, i);
+                if (i == 0) WL_TRP(2);
                 const int t0 = (tb + i) * IDX_TILE;
                 mbar_expect_tx(full + s, L::K8_TILE);
                 tma_load3d(k8 + s * L::K8_TILE, &sp.tm_keys, 0, t0, seq, full + s);
@@ -403,6 +460,8 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
             tc_fence_after();
             if (lane == 0) {
                 WL_TR(3, i);
+                if (i == 0) WL_TRP(3);
+                if (i == n - 1) WL_TRP(4);
                 const uint32_t sA = smem_u32(k8 + s * L::K8_TILE);
                 const uint32_t d = tmem + (uint32_t)(a * 64);
 #pragma unroll
@@ -452,24 +511,30 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
             if (valid) out[t] = v;
 #endif
             if (key == 0) WL_TR(6, i);
-#ifdef WL_EXP_NOHIST
-            if (false) {
-#else
-            if (hrow) {
-#endif
-                const uint32_t bb = valid ? score_key(v) >> (32 - TOPK_HIST_BITS) : 0xFFFFFFFFu;
-                const unsigned peers = __match_any_sync(0xffffffffu, bb);
-                if (valid && lane == __ffs(peers) - 1) atomicAdd(hrow + bb, (unsigned)__popc(peers));
-            }
+            if (key == 0 && i == n - 1) WL_TRP(5);
+            if (hrow && valid) atomicAdd(&sHist[score_key(v) >> (32 - TOPK_HIST_BITS)], 1u);
         }
     }
     tc_fence_before();
+    if (tid == 0) WL_TRP(6);
     __syncthreads();
+    if (tid == 0) WL_TRP(7);
+    if (hrow) {  // this CTA's counts into the row's histogram: nonzero bins only
+        for (int b4 = tid; b4 < TOPK_HIST_BINS / 4; b4 += IDX_STREAM_THREADS) {
+            const uint4 c = reinterpret_cast<const uint4*>(sHist)[b4];
+            if (c.x) atomicAdd(hrow + 4 * b4, c.x);
+            if (c.y) atomicAdd(hrow + 4 * b4 + 1, c.y);
+            if (c.z) atomicAdd(hrow + 4 * b4 + 2, c.z);
+            if (c.w) atomicAdd(hrow + 4 * b4 + 3, c.w);
+        }
+    }
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, L::TMEM_COLS);
     }
     WL_KT_END(0);
+    WL_TRB(1);
+    if (tid == 0) WL_TRP(8);
 }
 
 }  // namespace wl

@@ -455,13 +455,14 @@ struct MergeParams {
 
 // grid (n_heads, dv / 128, n_rows), 32 threads: lane l owns 4 latent columns.
 // Up to 32 parts: lane s holds part s's lse; all parts' columns load at once.
+template <bool LL>
 __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
     WL_KT_BEGIN(3);
     pdl_wait();
     pdl_trigger();
     const int h = blockIdx.x, q = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
     const int c = q * 128 + lane * 4;
-    const bool ll = p.ll.base != nullptr;
+    constexpr bool ll = LL;  // parts arrive through the peer exchange (p.ll)
     const uint32_t epoch = ll ? p2p_epoch(p.ll) : 0u;
     const uint64_t* lb = ll ? p2p_slot(p.ll, epoch, 0) : nullptr;
     float ls = -INFINITY;
@@ -492,7 +493,7 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
             v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (use) {
                 const long long si = oi + (long long)s * p.part_stride;
-                if (ll) {  // raw words now (all loads in flight), tags checked below
+                if constexpr (LL) {  // raw words now (all loads in flight), tags checked below
                     uint64_t w0, w1, w2, w3;
                     ll_load2_raw(lb + si, w0, w1);
                     ll_load2_raw(lb + si + 2, w2, w3);
@@ -505,7 +506,7 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
                 }
             }
         }
-        if (ll) {
+        if constexpr (LL) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 if (wv[j] == 0.f) continue;

@@ -746,7 +746,7 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
 // times slower than letting the shared-memory unit serialise.)
 // Supports candidate-index mapping (`cand_idx`), segmented rows and candidate
 // outputs.
-template <int PER>
+template <int PER, bool LL>
 __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p, int vec4, CandOut co) {
     static_assert(PER % 4 == 0 && PER <= 32, "PER: whole float4s, one bit each in a 32-bit mask");
     WL_TRR(0);
@@ -767,16 +767,16 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
     auto off = [&](int i) -> long long {
         return p.seg_len > 0 ? (long long)(i / p.seg_len) * p.seg_stride + i % p.seg_len : (long long)i;
     };
-    const bool ll = p.ll.base != nullptr;
+    constexpr bool ll = LL;  // rows arrive through the peer exchange (p.ll)
     const uint32_t epoch = ll ? p2p_epoch(p.ll) : 0u;
     const uint64_t* lrow = ll ? p2p_slot(p.ll, epoch, 0) + (long long)r * p.in_stride : nullptr;
     auto score_at = [&](int i) -> float {
-        if (!ll) return row[off(i)];
+        if constexpr (!LL) return row[off(i)];
         const uint64_t* w = lrow + off(i);
         return __uint_as_float(ll_wait1(w, epoch, ll_load1_raw(w), 22));
     };
     auto key_at = [&](int i) -> int {
-        if (ll) {
+        if constexpr (LL) {
             const uint64_t* w = lrow + p.ll_idx_off + off(i);
             return (int)ll_wait1(w, epoch, ll_load1_raw(w), 22);
         }
@@ -800,7 +800,7 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
     {
         float f[PER];
         const long long o0 = nvalid > 0 ? off(i0) : 0;  // PER divides seg_len: one segment per thread
-        if (ll) {
+        if constexpr (LL) {
             uint64_t w[PER];
             if (nvalid == PER) {
 #pragma unroll

@@ -410,14 +410,17 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
     if (lmax <= kTopkRegMax) {
         const int vec4 = aligned16(index) && (index_stride & 3) == 0 && (seg_stride & 3) == 0;
         const dim3 g(rows->n_rows), b(wl::TOPK_THREADS);
-        if (lmax <= wl::TOPK_THREADS * 4)
-            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<4>, g, b, 0, st, p, vec4, cout));
-        else if (lmax <= wl::TOPK_THREADS * 8)
-            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<8>, g, b, 0, st, p, vec4, cout));
-        else if (lmax <= wl::TOPK_THREADS * 16)
-            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<16>, g, b, 0, st, p, vec4, cout));
+        const int per = lmax <= wl::TOPK_THREADS * 4 ? 4 : lmax <= wl::TOPK_THREADS * 8 ? 8
+                      : lmax <= wl::TOPK_THREADS * 16 ? 16 : 32;
+        auto go = [&](auto kernel) { return launch_pdl(kernel, g, b, 0, st, p, vec4, cout); };
+        cudaError_t e;
+        if (ll)
+            e = per == 4 ? go(wl::topk_reg_kernel<4, true>) : per == 8 ? go(wl::topk_reg_kernel<8, true>)
+              : per == 16 ? go(wl::topk_reg_kernel<16, true>) : go(wl::topk_reg_kernel<32, true>);
         else
-            WL_CUDA_TRY(launch_pdl(wl::topk_reg_kernel<32>, g, b, 0, st, p, vec4, cout));
+            e = per == 4 ? go(wl::topk_reg_kernel<4, false>) : per == 8 ? go(wl::topk_reg_kernel<8, false>)
+              : per == 16 ? go(wl::topk_reg_kernel<16, false>) : go(wl::topk_reg_kernel<32, false>);
+        WL_CUDA_TRY(e);
         return WL_OK;
     }
     const size_t smem = lmax <= wl::TOPK_SMEM_MAX ? (size_t)lmax * 4 : 0;
@@ -508,7 +511,10 @@ int launch_merge(const float* o_part, const float* lse_part, int32_t n_rows, int
         p.ll = *ll;
         p.ll_lse_off = ll_lse_off;
     }
-    WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
+    if (ll)
+        WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel<true>, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
+    else
+        WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel<false>, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
