@@ -256,7 +256,9 @@ def main():
         def step(i=0):
             _lib.check(L.wl_attn_decode_sharded(C.byref(cfg), C.byref(io), C.byref(shard), comm.h, ws.data_ptr(),
                                                 nbytes, torch.cuda.current_stream().cuda_stream))
-        launches_per_step = 9
+        # indexer, top-k, global top-k, attention, local merge, final merge
+        # (+ two put kernels with the peer exchange; NCCL's own kernels otherwise)
+        launches_per_step = 8 if comm.p2p else 6
     else:
         nbytes = L.wl_attn_workspace_bytes(C.byref(cfg), T, B)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -363,7 +365,8 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded on device, BASELINE distributions)",
             "config": {"workload": "cfg4: decode, 8 seq x T=131072, top-2048, owner layer",
-                       "batch": B, "T": T, "index_topk": K, "parallelism": f"kv-seq shard x{world}",
+                       "batch": B, "T": T, "index_topk": K, "parallelism": f"kv-seq shard x{world}" + ("" if comm is None else
+                                                                  (" (NVLink peer exchange)" if comm.p2p else " (NCCL)")),
                        "l2": "inputs (1.35 GB of caches) larger than L2", "graph": graph is not None},
             "tokens_per_s": round(B / (us * 1e-6), 1),
             "e2e": {"value": round(t_e2e.item() * 1e3, 2), "unit": "us/layer", "h2d_bytes_per_step": h2d,
