@@ -7,16 +7,11 @@
 // the key cache in fp8-e4m3 plus a per-key fp32 scale. The [H,T] score array
 // the reference writes to global memory and reads back never leaves TMEM here.
 //
-// Prefill form (many query rows over one cache; one CTA = 4 warps = one 128-key tile):
-//   * the TMA engine streams the tile's 16 KB of fp8 keys into shared memory
-//     (cp.async.bulk, one contiguous copy: rows are packed 128-byte lines);
-//   * each thread widens one key row e4m3 -> bf16 (exact) into a 128B-swizzled
-//     K-major tile — tcgen05 kind::f16 needs A and B of one type;
-//   * one thread issues tcgen05.mma with M = 128 keys, N = 32 heads x G query
-//     rows, K = 128, fp32 accumulators in TMEM;
-//   * each thread reads its key's N accumulators back with tcgen05.ld and
-//     applies scale, relu and the head-weighted sum in registers.
-// Bytes per key: 128 (fp8) + 4 (scale); the kernel is HBM-bound at decode.
+// One kernel, indexer_stream_kernel<R>: R query rows share each 128-key tile
+// (R = 1 at decode, where every row streams its own cache; R = 4 at prefill,
+// where consecutive rows of one sequence read the same keys). The fp8 keys go
+// to the tensor cores as they are (kind::f8f6f4); details below.
+// Bytes per key: 128 (fp8) + 4 (scale); the decode form is HBM-bound.
 #pragma once
 #include "ptx.cuh"
 
@@ -38,7 +33,6 @@ struct IdxParams {
     float* out;
     long long out_stride;
     float qk_scale;
-    int groups_per_cta;
 };
 
 __device__ __forceinline__ int rows_len(int r, int rows_per_seq, int len0, int len_step, int T) {
@@ -46,174 +40,21 @@ __device__ __forceinline__ int rows_len(int r, int rows_per_seq, int len0, int l
     return (int)(l < T ? l : T);
 }
 
-template <int G>
-struct IdxLayout {
-    static constexpr int N = 32 * G;
-    static constexpr uint32_t A_BYTES = IDX_TILE * IDX_D * 2;  // bf16 keys, 2 K-chunks
-    static constexpr uint32_t A_CHUNK = IDX_TILE * 128;
-    static constexpr uint32_t Q_CHUNK = N * 128;
-    static constexpr uint32_t Q_BYTES = 2 * Q_CHUNK;
-    static constexpr uint32_t K8_BYTES = IDX_TILE * IDX_D;
-    static constexpr uint32_t OFF_A = 0;
-    static constexpr uint32_t OFF_Q = OFF_A + A_BYTES;
-    static constexpr uint32_t OFF_K8 = OFF_Q + Q_BYTES;
-    static constexpr uint32_t OFF_W = OFF_K8 + K8_BYTES;
-    static constexpr uint32_t OFF_BAR = OFF_W + N * 4;
-    static constexpr uint32_t OFF_SLOT = OFF_BAR + 16;
-    static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;  // + alignment slack
-    static constexpr uint32_t TMEM_COLS = N;                   // 32..256, power of two
-    static constexpr uint32_t IDESC = idesc_bf16(128, N, 0, 0);
-};
-
-template <int G>
-__global__ void __launch_bounds__(128) indexer_scores_kernel(IdxParams p) {
-    using L = IdxLayout<G>;
-    static_assert(G == 1 || G == 2 || G == 4 || G == 8, "G must be a power of two <= 8");
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t sA = smem_u32(smem + L::OFF_A);
-    const uint32_t sQ = smem_u32(smem + L::OFF_Q);
-    uint8_t* k8 = smem + L::OFF_K8;
-    float* sW = reinterpret_cast<float*>(smem + L::OFF_W);
-    uint64_t* bar_tma = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-    uint64_t* bar_mma = bar_tma + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_SLOT);
-
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int t0 = blockIdx.x * IDX_TILE;
-    const int nk = min(IDX_TILE, p.T - t0);
-    const int n_groups = (p.n_rows + G - 1) / G;
-    const int g_begin = blockIdx.y * p.groups_per_cta;
-    const int g_end = min(g_begin + p.groups_per_cta, n_groups);
-    if (g_begin >= g_end || nk <= 0) return;
-    // Rows of one CTA share one sequence (host guarantees it).
-    const int seq = (g_begin * G) / p.rows_per_seq;
-    // Causal skip: nothing to do if the tile starts past every row's length.
-    // (len_step >= 0, so the last row of the CTA is the longest.)
-    {
-        const int last_row = min(g_end * G, p.n_rows) - 1;
-        if (t0 >= rows_len(last_row, p.rows_per_seq, p.len0, p.len_step, p.T)) return;
-    }
-
-    if (tid == 0) {
-        mbar_init(bar_tma, 1);
-        mbar_init(bar_mma, 1);
-        fence_mbar_init();
-        mbar_expect_tx(bar_tma, (uint32_t)nk * IDX_D);
-        bulk_g2s(k8, p.keys + (long long)seq * p.keys_seq + (long long)t0 * IDX_D, (uint32_t)nk * IDX_D,
-                 bar_tma);
-    }
-    if (warp == 0) tmem_alloc(tmem_slot, L::TMEM_COLS);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
-    const float sc = (tid < nk) ? __ldg(p.scale + (long long)seq * p.scale_seq + t0 + tid) * p.qk_scale : 0.f;
-
-    // Widen key row `tid` e4m3 -> bf16 into the swizzled K-major A tile.
-    bool ok = mbar_wait(bar_tma, 0, 1);
-    if (__syncthreads_and(ok)) {
-        const uint32_t src = smem_u32(k8) + tid * 128u;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t p8 = (uint32_t)(j + tid) & 7u;  // rotate: spread banks
-            uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-            if (tid < nk) {
-                const uint4 v = lds_v4(src + p8 * 16u);
-                lo.x = e4m3x2_to_bf16x2((uint16_t)(v.x & 0xffff));
-                lo.y = e4m3x2_to_bf16x2((uint16_t)(v.x >> 16));
-                lo.z = e4m3x2_to_bf16x2((uint16_t)(v.y & 0xffff));
-                lo.w = e4m3x2_to_bf16x2((uint16_t)(v.y >> 16));
-                hi.x = e4m3x2_to_bf16x2((uint16_t)(v.z & 0xffff));
-                hi.y = e4m3x2_to_bf16x2((uint16_t)(v.z >> 16));
-                hi.z = e4m3x2_to_bf16x2((uint16_t)(v.w & 0xffff));
-                hi.w = e4m3x2_to_bf16x2((uint16_t)(v.w >> 16));
-            }
-            const uint32_t chunk = p8 >> 2, c16 = (p8 & 3u) * 2u;
-            sts_v4(sA + chunk * L::A_CHUNK + sw128_off(tid, c16), lo);
-            sts_v4(sA + chunk * L::A_CHUNK + sw128_off(tid, c16 + 1), hi);
-        }
-
-        uint32_t phase = 0;
-        for (int g = g_begin; g < g_end; ++g) {
-            const int r0 = g * G;
-            // Query rows r0..r0+G-1 (32 heads each) -> swizzled K-major B tile.
-            for (int pid = tid; pid < L::N * 16; pid += 128) {
-                const int row = pid >> 4, pc = pid & 15;
-                const int qr = r0 + row / IDX_H;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (qr < p.n_rows)
-                    v = ldg_nc_v4(p.q + ((long long)qr * IDX_H + (row % IDX_H)) * IDX_D + pc * 8);
-                sts_v4(sQ + (uint32_t)(pc >> 3) * L::Q_CHUNK + sw128_off(row, pc & 7), v);
-            }
-            for (int i = tid; i < L::N; i += 128) {
-                const int qr = r0 + i / IDX_H;
-                sW[i] = (qr < p.n_rows) ? __ldg(p.w + (long long)qr * IDX_H + (i % IDX_H)) : 0.f;
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncthreads();
-            tc_fence_after();
-            if (tid == 0) {
-#pragma unroll
-                for (int kk = 0; kk < IDX_D / 16; ++kk) {
-                    const uint32_t c = kk >> 2, ko = (kk & 3) * 32;
-                    const uint64_t ad = desc_sw128(sA + c * L::A_CHUNK + ko, 16, 1024);
-                    const uint64_t bd = desc_sw128(sQ + c * L::Q_CHUNK + ko, 16, 1024);
-                    mma_bf16(tmem, ad, bd, L::IDESC, kk > 0 ? 1u : 0u);
-                }
-                mma_commit(bar_mma);
-            }
-            ok = mbar_wait(bar_mma, phase, 2);
-            phase ^= 1;
-            if (!__syncthreads_and(ok)) break;
-            tc_fence_after();
-
-            const int t = t0 + tid;
-#pragma unroll 1
-            for (int gg = 0; gg < G; ++gg) {
-                const int row = r0 + gg;
-                if (row >= p.n_rows) break;  // uniform across the CTA
-                float acc[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)(gg * 32), acc);
-                tmem_wait_ld();
-                float v = 0.f;
-#pragma unroll
-                for (int h = 0; h < 32; ++h) v = fmaf(sW[gg * 32 + h], fmaxf(acc[h] * sc, 0.f), v);
-                const int len = rows_len(row, p.rows_per_seq, p.len0, p.len_step, p.T);
-                if (tid < nk) p.out[(long long)row * p.out_stride + t] = (t < len) ? v : -INFINITY;
-            }
-            tc_fence_before();
-            __syncthreads();
-            tc_fence_after();
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc_fence_after();
-        tmem_dealloc(tmem, L::TMEM_COLS);
-    }
-}
-
-}  // namespace wl
-
-namespace wl {
-
-// ---- decode form: persistent, warp-specialised, fp8 tensor cores ---------------------------
-// One CTA per SM streams a contiguous range of 128-key tiles of one row's
-// cache. Roles (10 warps), connected by mbarriers only:
-//   warp 0      TMA producer: the tile's fp8 keys as one 128 x 128-byte box with
-//               128B swizzle (a tensor-map load; rows past the cache end read as
+// ---- warp-specialised, fp8 tensor cores ------------------------------------------------
+// A CTA streams a contiguous range of 128-key tiles of one cache for R query
+// rows (decode: one row, one CTA per SM across all rows; prefill: groups of 4
+// consecutive rows, one CTA per group). Roles (10 warps), connected by
+// mbarriers only:
+//   warp 0      TMA producer: the rows' bf16 queries (bulk copy during setup),
+//               then each tile's fp8 keys as one 128 x 128-byte box with 128B
+//               swizzle (a tensor-map load; rows past the cache end read as
 //               zero) into ring stage i % IDX_NS
 //   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4 straight on the fp8 keys
-//               (M = 128 keys, K = 32 per instruction), one chain of 4
-//               per tile: N = 64 = the query's hi and lo e4m3 terms side by side
-//   warps 2-9   epilogue:     tcgen05.ld both halves for one key, combine, scale,
-//               relu, head-weighted sum, store (+ fused top-k histogram); two
-//               groups of 4 warps take alternate tiles
+//               (M = 128 keys, K = 32 per instruction), one chain of 4 per
+//               tile: N = 64 R = each row's hi and lo e4m3 query terms
+//   warps 2-9   epilogue:     tcgen05.ld both halves for one (key, row), combine,
+//               scale, relu, head-weighted sum, store (+ fused top-k histogram
+//               at decode); two groups of 4 warps take alternate tiles
 //
 // The query in e4m3: per head, q * s_h (s_h a power of two putting the head's
 // largest element in [128, 256)) = hi + lo / 32 with hi = e4m3(q s_h) and
@@ -230,27 +71,37 @@ namespace wl {
 // measured slower).
 constexpr int IDX_NS = 8;    // TMA stages of fp8 keys
 constexpr int IDX_CTAS_PER_SM = 1;
-constexpr int IDX_NACC = 4;  // accumulator sets (hi, lo) in flight
-constexpr int IDX_EPI_GROUPS = 2;  // epilogue groups of 4 warps, alternating tiles
-constexpr int IDX_STREAM_THREADS = 64 + 128 * IDX_EPI_GROUPS;
 constexpr int TOPK_HIST_BITS = 13;
 constexpr int TOPK_HIST_BINS = 1 << TOPK_HIST_BITS;
 
-struct IdxStreamLayout {
+// R query rows per MMA (N = 64 R: each row's hi ‖ lo terms): R = 1 at decode
+// (each row streams its own cache), R = 4 at prefill (4 consecutive rows of one
+// sequence share every key tile).
+template <int R>
+struct IdxStream {
+    static_assert(R == 1 || R == 2 || R == 4, "N = 64 R <= 256");
+    static constexpr int NACC = R == 1 ? 4 : 2;            // accumulator sets in flight
+    static constexpr int EPI_GROUPS = 2;                   // epilogue groups of 4 warps, alternating tiles
+    // Each accumulator set must always be drained by the same group (tiles a,
+    // a + NACC, ...), or a group could wait on a set's next phase while its
+    // current one is still open (a parity wait two phases ahead passes at once).
+    static_assert(NACC % EPI_GROUPS == 0, "epilogue groups must divide the accumulator sets");
+    static constexpr int THREADS = 64 + 128 * EPI_GROUPS;  // producer + MMA warps + epilogue
+    static constexpr bool HIST = R == 1;                   // fused top-k histogram (decode)
     static constexpr uint32_t K8_TILE = IDX_TILE * IDX_D;  // 16 KB, 128B-swizzled (1024-aligned)
-    static constexpr uint32_t QT = IDX_H * IDX_D;          // one e4m3 query term, 4 KB
+    static constexpr uint32_t QROWS = 64 * R;              // B operand rows: per query row hi[32] ‖ lo[32]
     static constexpr uint32_t OFF_K8 = 0;
-    static constexpr uint32_t OFF_Q = OFF_K8 + IDX_NS * K8_TILE;  // hi, lo
-    static constexpr uint32_t OFF_W = OFF_Q + 2 * QT;
-    static constexpr uint32_t OFF_HIST = OFF_W + IDX_H * 4;  // this CTA's share of the row histogram
-    static constexpr uint32_t OFF_QRAW = OFF_HIST + TOPK_HIST_BINS * 4;  // the row's bf16 query, as copied
-    static constexpr uint32_t OFF_BAR = OFF_QRAW + IDX_H * IDX_D * 2;
-    static constexpr int N_BARS = 2 * IDX_NS + 2 * IDX_NACC + 1;  // full, empty, acc_full, acc_empty, query
+    static constexpr uint32_t OFF_Q = OFF_K8 + IDX_NS * K8_TILE;
+    static constexpr uint32_t OFF_W = OFF_Q + QROWS * 128;
+    static constexpr uint32_t OFF_HIST = OFF_W + R * IDX_H * 4;  // this CTA's share of the row histogram
+    static constexpr uint32_t OFF_QRAW = OFF_HIST + (HIST ? TOPK_HIST_BINS * 4 : 0);  // bf16 queries, as copied
+    static constexpr uint32_t OFF_BAR = OFF_QRAW + R * IDX_H * IDX_D * 2;
+    static constexpr int N_BARS = 2 * IDX_NS + 2 * NACC + 1;  // full, empty, acc_full, acc_empty, query
     static constexpr uint32_t OFF_SLOT = OFF_BAR + N_BARS * 8;
     static constexpr uint32_t BYTES = OFF_SLOT + 16 + 1024;
-    static constexpr uint32_t TMEM_COLS = 64 * IDX_NACC;  // 256
-    // kind::f8f6f4: E4M3 A and B (format 0), fp32 D; M = 128, N = 64 (hi ‖ lo)
-    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(2 * IDX_H >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    static constexpr uint32_t TMEM_COLS = QROWS * NACC;  // 256 or 512
+    // kind::f8f6f4: E4M3 A and B (format 0), fp32 D; M = 128, N = 64 R
+    static constexpr uint32_t IDESC = (1u << 4) | ((QROWS >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 };
 
 __device__ __forceinline__ uint32_t score_key(float f) {
@@ -318,9 +169,13 @@ __device__ long long* g_trace;
     } while (0)
 #endif
 
-__global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
+// grid (CTAs per group, row groups): a CTA takes R consecutive rows (one key
+// cache) and a contiguous range of `tiles_per_cta` tiles of their keys.
+template <int R>
+__global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
     indexer_stream_kernel(IdxParams p, const __grid_constant__ IdxStreamParams sp, unsigned* hist, int tiles_per_cta) {
-    using L = IdxStreamLayout;
+    using L = IdxStream<R>;
+    constexpr int NT = L::THREADS, NACC = L::NACC;
     WL_KT_BEGIN(0);
     WL_TRB(0);
     extern __shared__ uint8_t smem_raw[];
@@ -333,49 +188,50 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* empty = full + IDX_NS;
     uint64_t* acc_full = empty + IDX_NS;
-    uint64_t* acc_empty = acc_full + IDX_NACC;
-    uint64_t* qbar = acc_empty + IDX_NACC;
+    uint64_t* acc_empty = acc_full + NACC;
+    uint64_t* qbar = acc_empty + NACC;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_SLOT);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int r = blockIdx.y;
-    const int seq = r / p.rows_per_seq;
-    const int len = rows_len(r, p.rows_per_seq, p.len0, p.len_step, p.T);
-    const int ntiles = (len + IDX_TILE - 1) / IDX_TILE;
+    const int r0 = blockIdx.y * R;                      // first row of the group
+    const int nrows = min(R, p.n_rows - r0);            // rows of the group that exist
+    const int seq = r0 / p.rows_per_seq;                // all R rows read this cache
+    int len_max = 0;
+    for (int j = 0; j < nrows; ++j) len_max = max(len_max, rows_len(r0 + j, p.rows_per_seq, p.len0, p.len_step, p.T));
+    const int ntiles = (len_max + IDX_TILE - 1) / IDX_TILE;
     const int tb = blockIdx.x * tiles_per_cta;
     const int n = min(tb + tiles_per_cta, ntiles) - tb;
-    if (n <= 0) {
+    if (n <= 0 || nrows <= 0) {
         pdl_wait();
         return;
     }
     const float* scale = p.scale + (long long)seq * p.scale_seq;
-    float* out = p.out + (long long)r * p.out_stride;
-    unsigned* hrow = hist ? hist + (long long)r * TOPK_HIST_BINS : nullptr;
+    unsigned* hrow = (L::HIST && hist) ? hist + (long long)r0 * TOPK_HIST_BINS : nullptr;
 
     if (tid == 0) {
         for (int s = 0; s < IDX_NS; ++s) {
             mbar_init(full + s, 1);
             mbar_init(empty + s, 1);  // the MMA's commit
         }
-        for (int b = 0; b < IDX_NACC; ++b) {
+        for (int b = 0; b < NACC; ++b) {
             mbar_init(acc_full + b, 1);
             mbar_init(acc_empty + b, 128);
         }
         mbar_init(qbar, 1);
         fence_mbar_init();
-        // The producer (this thread) copies the row's query (8 KB) at once, so
-        // that it lands during the setup below, ahead of the key stream; every
-        // other warp converts it from shared memory. (Loading it with per-warp
-        // global loads queued behind the key stream, and issuing the first key
-        // tiles together with it let them overtake it: both delayed the first
-        // MMA by microseconds.)
+        // The producer (this thread) copies the group's queries (8 KB a row) at
+        // once, so that they land during the setup below, ahead of the key
+        // stream; every other warp converts them from shared memory. (Loading
+        // them with per-warp global loads queued behind the key stream, and
+        // issuing the first key tiles together with them let those overtake
+        // them: both delayed the first MMA by microseconds.)
         pdl_wait();
-        mbar_expect_tx(qbar, IDX_H * IDX_D * 2);
-        bulk_g2s(smem + L::OFF_QRAW, p.q + (long long)r * IDX_H * IDX_D, IDX_H * IDX_D * 2, qbar);
+        mbar_expect_tx(qbar, (uint32_t)nrows * IDX_H * IDX_D * 2);
+        bulk_g2s(smem + L::OFF_QRAW, p.q + (long long)r0 * IDX_H * IDX_D, (uint32_t)nrows * IDX_H * IDX_D * 2, qbar);
     }
     if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);  // warp 1 allocates and frees
-    if (hist)
-        for (int b = tid; b < TOPK_HIST_BINS; b += IDX_STREAM_THREADS) sHist[b] = 0;
+    if (hrow)
+        for (int b = tid; b < TOPK_HIST_BINS; b += NT) sHist[b] = 0;
     tc_fence_before();
     __syncthreads();  // barriers initialised, TMEM address published
     tc_fence_after();
@@ -384,26 +240,34 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
     pdl_trigger();
     const uint32_t tmem = *tmem_slot;
     const bool producer = warp == 0;
-    // Query -> two e4m3 terms per head, by every warp but the producer; a named
-    // barrier joins them.
-    constexpr int CONV_WARPS = IDX_STREAM_THREADS / 32 - 1;
-    float wv[(IDX_H + CONV_WARPS - 1) / CONV_WARPS];  // head weights, loaded while the query lands
+    // Queries -> two e4m3 terms per (row, head), by every warp but the
+    // producer; a named barrier joins them. B row (j, term, h) = j*64 + term*32 + h.
+    constexpr int CONV_WARPS = NT / 32 - 1;
+    constexpr int PER_WARP = (R * IDX_H + CONV_WARPS - 1) / CONV_WARPS;
+    float wv[PER_WARP];  // head weights, loaded while the queries land
     if (!producer) {
 #pragma unroll
-        for (int k2 = 0; k2 < (IDX_H + CONV_WARPS - 1) / CONV_WARPS; ++k2) {
-            const int h = warp - 1 + k2 * CONV_WARPS;
-            wv[k2] = (lane == 0 && h < IDX_H) ? __ldg(p.w + (long long)r * IDX_H + h) : 0.f;
+        for (int k2 = 0; k2 < PER_WARP; ++k2) {
+            const int hr = warp - 1 + k2 * CONV_WARPS;  // (row j, head h) = (hr / 32, hr % 32)
+            wv[k2] = (lane == 0 && hr < nrows * IDX_H) ? __ldg(p.w + (long long)r0 * IDX_H + hr) : 0.f;
         }
         mbar_wait(qbar, 0, 9);
     }
 #pragma unroll
-    for (int k2 = 0; k2 < (IDX_H + CONV_WARPS - 1) / CONV_WARPS; ++k2) {
-        const int h = warp - 1 + k2 * CONV_WARPS;
-        if (producer || h >= IDX_H) break;
-        const uint2 raw = *reinterpret_cast<const uint2*>(sQraw + h * IDX_D + lane * 4);
-        const __nv_bfloat162 q01 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-        const __nv_bfloat162 q23 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-        float x[4] = {__low2float(q01), __high2float(q01), __low2float(q23), __high2float(q23)};
+    for (int k2 = 0; k2 < PER_WARP; ++k2) {
+        const int hr = warp - 1 + k2 * CONV_WARPS;
+        if (producer || hr >= R * IDX_H) break;
+        const int j = hr / IDX_H, h = hr % IDX_H;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (j < nrows) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(sQraw + hr * IDX_D + lane * 4);
+            const __nv_bfloat162 q01 = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+            const __nv_bfloat162 q23 = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+            x[0] = __low2float(q01);
+            x[1] = __high2float(q01);
+            x[2] = __low2float(q23);
+            x[3] = __high2float(q23);
+        }
         float mx = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(x[e]));
@@ -416,24 +280,24 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
         for (int e = 0; e < 4; e += 2) {
             const float a0 = x[e] * s_h, a1 = x[e + 1] * s_h;
             const __nv_fp8x2_storage_t h2 = __nv_cvt_float2_to_fp8x2(make_float2(a0, a1), __NV_SATFINITE, __NV_E4M3);
-            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(h2, __NV_E4M3);
-            const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+            const __half2_raw hr2 = __nv_cvt_fp8x2_to_halfraw2(h2, __NV_E4M3);
+            const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hr2));
             const __nv_fp8x2_storage_t l2 =
                 __nv_cvt_float2_to_fp8x2(make_float2((a0 - hf.x) * 32.f, (a1 - hf.y) * 32.f), __NV_SATFINITE, __NV_E4M3);
             hi4 |= (uint32_t)h2 << (8 * e);
             lo4 |= (uint32_t)l2 << (8 * e);
         }
-        // 4 codes = 4 bytes at byte lane*4 of the 128-byte row h, 128B-swizzled
+        // 4 codes = 4 bytes at byte lane*4 of a 128-byte B row, 128B-swizzled
         const uint32_t byte = (uint32_t)lane * 4u;
-        const uint32_t off = (uint32_t)h * 128u + ((((byte >> 4) ^ (uint32_t)h) & 7u) << 4) + (byte & 15u);
-        *reinterpret_cast<uint32_t*>(sQ + off) = hi4;
-        *reinterpret_cast<uint32_t*>(sQ + L::QT + off) = lo4;
-        if (lane == 0) sW[h] = wv[k2] / s_h;
+        const uint32_t rh = (uint32_t)(j * 64 + h), rl = rh + 32;
+        *reinterpret_cast<uint32_t*>(sQ + rh * 128u + ((((byte >> 4) ^ rh) & 7u) << 4) + (byte & 15u)) = hi4;
+        *reinterpret_cast<uint32_t*>(sQ + rl * 128u + ((((byte >> 4) ^ rl) & 7u) << 4) + (byte & 15u)) = lo4;
+        if (lane == 0) sW[hr] = j < nrows ? wv[k2] / s_h : 0.f;
     }
     if (tid == 32) WL_TRP(1);
     if (!producer) {
-        fence_proxy_async_smem();  // the query tile is read by the tensor cores
-        asm volatile("bar.sync 1, %0;" ::"n"(IDX_STREAM_THREADS - 32) : "memory");
+        fence_proxy_async_smem();  // the query tiles are read by the tensor cores
+        asm volatile("bar.sync 1, %0;" ::"n"(NT - 32) : "memory");
     }
 
     if (producer) {
@@ -454,19 +318,19 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
         // ---------------- MMA issuer (whole warp loops, lane 0 issues) ----------------
         const uint32_t sQa = smem_u32(sQ);
         for (int i = 0; i < n; ++i) {
-            const int s = i % IDX_NS, a = i % IDX_NACC;
+            const int s = i % IDX_NS, a = i % NACC;
             if (!mbar_wait(full + s, (uint32_t)(i / IDX_NS) & 1u, 11)) break;
-            if (i >= IDX_NACC && !mbar_wait(acc_empty + a, (uint32_t)(i / IDX_NACC - 1) & 1u, 12)) break;
+            if (i >= NACC && !mbar_wait(acc_empty + a, (uint32_t)(i / NACC - 1) & 1u, 12)) break;
             tc_fence_after();
             if (lane == 0) {
                 WL_TR(3, i);
                 if (i == 0) WL_TRP(3);
                 if (i == n - 1) WL_TRP(4);
                 const uint32_t sA = smem_u32(k8 + s * L::K8_TILE);
-                const uint32_t d = tmem + (uint32_t)(a * 64);
+                const uint32_t d = tmem + (uint32_t)(a * L::QROWS);
 #pragma unroll
                 for (int kk = 0; kk < IDX_D / 32; ++kk) {
-                    // B = the 64 rows hi[0..31] ‖ lo[0..31], one swizzled block
+                    // B = the 64 R query rows, one swizzled block
                     mma_f8(d, desc_sw128(sA + kk * 32, 16, 1024), desc_sw128(sQa + kk * 32, 16, 1024), L::IDESC,
                            kk > 0 ? 1u : 0u);
                 }
@@ -477,42 +341,48 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
             __syncwarp();
         }
     } else {
-        // ------- epilogue (warps 2..9 -> TMEM lane quarters 2,3,0,1; group g takes tiles i = g mod 2) -------
+        // ------- epilogue (warps 2.. -> TMEM lane quarters by warp % 4; group g takes tiles i = g mod EPI_GROUPS) -------
         const int quarter = warp & 3;
         const int key = quarter * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         auto load_scale = [&](int i) {
             const int t = (tb + i) * IDX_TILE + key;
-            return (i < n && t < len) ? __ldg(scale + t) : 0.f;
+            return (i < n && t < len_max) ? __ldg(scale + t) : 0.f;
         };
         // Scales by plain loads one tile of this group ahead (a TMA copy per
         // tile this small would cost the copy engine as much time as the 16 KB
         // key tile).
-        float sc_next = load_scale((warp - 2) >> 2);
-        for (int i = (warp - 2) >> 2; i < n; i += IDX_EPI_GROUPS) {
-            const int a = i % IDX_NACC;
-            const int t0 = (tb + i) * IDX_TILE;
+        const int g0 = (warp - 2) >> 2;
+        float sc_next = load_scale(g0);
+        for (int i = g0; i < n; i += L::EPI_GROUPS) {
+            const int a = i % NACC;
+            const int t = (tb + i) * IDX_TILE + key;
             const float sc_raw = sc_next;
-            sc_next = load_scale(i + IDX_EPI_GROUPS);
-            if (!mbar_wait(acc_full + a, (uint32_t)(i / IDX_NACC) & 1u, 15)) break;
+            sc_next = load_scale(i + L::EPI_GROUPS);
+            if (!mbar_wait(acc_full + a, (uint32_t)(i / NACC) & 1u, 15)) break;
             if (key == 0) WL_TR(5, i);
             tc_fence_after();
             const float sc = sc_raw * p.qk_scale;
-            float acc[64];  // [0, 32): hi terms, [32, 64): lo terms
-            tmem_ld64(tmem + lane_base + (uint32_t)(a * 64), acc);
+#pragma unroll 1
+            for (int j = 0; j < nrows; ++j) {
+                float acc[64];  // [0, 32): hi terms, [32, 64): lo terms
+                tmem_ld64(tmem + lane_base + (uint32_t)(a * L::QROWS + j * 64), acc);
+                float v = 0.f;
+#pragma unroll
+                for (int h = 0; h < 32; ++h)
+                    v = fmaf(sW[j * IDX_H + h], fmaxf(fmaf(acc[32 + h], 0.03125f, acc[h]) * sc, 0.f), v);
+                const int r = r0 + j;
+                const bool valid = t < rows_len(r, p.rows_per_seq, p.len0, p.len_step, p.T);
+#ifndef WL_EXP_NOSTORE
+                if (valid) p.out[(long long)r * p.out_stride + t] = v;
+#endif
+                if constexpr (L::HIST)
+                    if (hrow && valid) atomicAdd(&sHist[score_key(v) >> (32 - TOPK_HIST_BITS)], 1u);
+            }
             tc_fence_before();
             mbar_arrive(acc_empty + a);
-            float v = 0.f;
-#pragma unroll
-            for (int h = 0; h < 32; ++h) v = fmaf(sW[h], fmaxf(fmaf(acc[32 + h], 0.03125f, acc[h]) * sc, 0.f), v);
-            const int t = t0 + key;
-            const bool valid = t < len;
-#ifndef WL_EXP_NOSTORE
-            if (valid) out[t] = v;
-#endif
             if (key == 0) WL_TR(6, i);
             if (key == 0 && i == n - 1) WL_TRP(5);
-            if (hrow && valid) atomicAdd(&sHist[score_key(v) >> (32 - TOPK_HIST_BITS)], 1u);
         }
     }
     tc_fence_before();
@@ -520,7 +390,7 @@ __global__ void __launch_bounds__(IDX_STREAM_THREADS, IDX_CTAS_PER_SM)
     __syncthreads();
     if (tid == 0) WL_TRP(7);
     if (hrow) {  // this CTA's counts into the row's histogram: nonzero bins only
-        for (int b4 = tid; b4 < TOPK_HIST_BINS / 4; b4 += IDX_STREAM_THREADS) {
+        for (int b4 = tid; b4 < TOPK_HIST_BINS / 4; b4 += NT) {
             const uint4 c = reinterpret_cast<const uint4*>(sHist)[b4];
             if (c.x) atomicAdd(hrow + 4 * b4, c.x);
             if (c.y) atomicAdd(hrow + 4 * b4 + 1, c.y);

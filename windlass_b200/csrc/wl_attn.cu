@@ -88,18 +88,16 @@ int ensure_attrs() {
     if (dev < 0 || dev >= kMaxDevices) return WL_ERR_CUDA;
     std::lock_guard<std::mutex> lk(g_attr_mu);
     if (g_attr_done[dev]) return WL_OK;
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_scores_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     wl::IdxLayout<1>::BYTES));
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_scores_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     wl::IdxLayout<8>::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      AttnLayout::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::sel_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      200 * 1024));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::TOPK_SMEM_MAX * 4));
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     wl::IdxStreamLayout::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::IdxStream<1>::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::indexer_stream_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::IdxStream<4>::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_partition_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::TOPKM_PART_SMEM));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -211,14 +209,16 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
     p.out_stride = out_stride;
     p.qk_scale = cfg->idx_qk_scale;
     const int ntiles = (int)ceil_div(T, wl::IDX_TILE);
-    if (rows->rows_per_seq >= rows->n_rows && rows->n_rows >= 8) {
-        // Many rows over one shared cache (prefill): 8 rows (N = 256) per MMA.
-        const int n_groups = (int)ceil_div(rows->n_rows, 8);
-        const int want_y = (int)ceil_div(4 * 148, ntiles);
-        const int gpc = (int)ceil_div(n_groups, want_y < 1 ? 1 : want_y);
-        p.groups_per_cta = gpc;
-        dim3 grid(ntiles, (unsigned)ceil_div(n_groups, gpc));
-        wl::indexer_scores_kernel<8><<<grid, 128, wl::IdxLayout<8>::BYTES, st>>>(p);
+    wl::IdxStreamParams sp{};
+    const int n_seq = (int)ceil_div(rows->n_rows, rows->rows_per_seq);
+    if (int e = encode_keys_map(&sp.tm_keys, cache->keys, T, n_seq, cache->keys_seq_stride)) return e;
+    if (rows->n_rows >= 8 && (rows->rows_per_seq % 4 == 0 || rows->rows_per_seq >= rows->n_rows)) {
+        // Many rows over shared caches (prefill): 4 consecutive rows of one
+        // sequence per MMA (N = 256), one CTA per group over all its tiles.
+        const int groups = (int)ceil_div(rows->n_rows, 4);
+        if (groups > 65535) return WL_ERR_ARG;
+        WL_CUDA_TRY(launch_pdl(wl::indexer_stream_kernel<4>, dim3(1, groups), dim3(wl::IdxStream<4>::THREADS),
+                               wl::IdxStream<4>::BYTES, st, p, sp, (unsigned*)nullptr, ntiles));
     } else {
         // Decode: each row streams its own cache; at most one CTA per SM in
         // total, each over a contiguous range of tiles.
@@ -228,11 +228,8 @@ int launch_indexer(const wl_attn_cfg* cfg, const wl_index_cache* cache, int32_t 
         if (cpr > ntiles) cpr = ntiles;
         const int tpc = (int)ceil_div(ntiles, cpr);
         dim3 grid((unsigned)ceil_div(ntiles, tpc), rows->n_rows);
-        wl::IdxStreamParams sp{};
-        const int n_seq = (int)ceil_div(rows->n_rows, rows->rows_per_seq);
-        const int e = encode_keys_map(&sp.tm_keys, cache->keys, T, n_seq, cache->keys_seq_stride);
-        if (e != WL_OK) return e;
-        WL_CUDA_TRY(launch_pdl(wl::indexer_stream_kernel, grid, dim3(wl::IDX_STREAM_THREADS), wl::IdxStreamLayout::BYTES, st, p, sp, hist, tpc));
+        WL_CUDA_TRY(launch_pdl(wl::indexer_stream_kernel<1>, grid, dim3(wl::IdxStream<1>::THREADS),
+                               wl::IdxStream<1>::BYTES, st, p, sp, hist, tpc));
     }
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
