@@ -20,6 +20,7 @@
 #include "../../include/wl_attn.h"
 #include "indexer.cuh"
 #include "mla_attn.cuh"
+#include "mla_prefill.cuh"
 #include "p2p.cuh"
 #include "topk.cuh"
 
@@ -90,6 +91,8 @@ int ensure_attrs() {
     if (g_attr_done[dev]) return WL_OK;
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      AttnLayout::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::PfLayout::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::sel_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      200 * 1024));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -171,6 +174,25 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     cfg.attrs = at;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// The absorbed queries [n_rows][64][576] bf16 as a 2D tensor {576, 64 n_rows},
+// 64 x 64 boxes, 128B swizzle (the prefill attention's query tiles).
+int encode_q_map(CUtensorMap* tm, const void* q_abs, int32_t n_rows) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return WL_ERR_CUDA;
+    const cuuint64_t dims[2] = {(cuuint64_t)wl::AT_D, (cuuint64_t)wl::AT_H * n_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)wl::AT_D * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)wl::AT_H};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(q_abs), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::fprintf(stderr, "wl_attn: cuTensorMapEncodeTiled (queries) failed (%d)\n", (int)r);
+        return WL_ERR_CUDA;
+    }
+    return WL_OK;
 }
 
 int rows_ok(const wl_rows* r, int32_t T) {
@@ -453,7 +475,7 @@ int launch_normalize(const int32_t* in, int64_t in_stride, const int32_t* n_in_d
 int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int64_t len_T,
                 const wl_rows* rows, const void* q_abs, const int32_t* sel, int64_t sel_stride,
                 const int32_t* sel_n_dev, int32_t sel_n, int64_t win_lo, int64_t win_hi, int32_t split_keys,
-                float* o_part, float* lse_part, int32_t max_splits, cudaStream_t st) {
+                float* o_part, float* lse_part, int32_t max_splits, cudaStream_t st, bool many_rows = false) {
     if (!c || !c->c_kv || !c->k_rot || !q_abs || !o_part || !lse_part) return WL_ERR_ARG;
     if (!aligned16(c->c_kv) || !aligned16(c->k_rot) || !aligned16(q_abs)) return WL_ERR_ARG;
     if ((c->c_kv_row_stride & 7) || (c->k_rot_row_stride & 7) || (c->c_kv_seq_stride & 7) ||
@@ -487,6 +509,15 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     p.o_part = o_part;
     p.lse_part = lse_part;
     p.scale_log2 = cfg->softmax_scale * 1.4426950408889634f;
+    if (many_rows && split_keys == 0 && max_splits == 1 && win_lo <= 0 && win_hi >= len_T) {
+        // Many query rows, each over its whole list (prefill): heads as M,
+        // gather / QK / softmax / P.V pipelined within the row.
+        wl::PfParams pp{};
+        if (int e = encode_q_map(&pp.tm_q, q_abs, rows->n_rows)) return e;
+        WL_CUDA_TRY(launch_pdl(wl::mla_prefill_kernel, dim3(rows->n_rows), dim3(wl::PF_THREADS), wl::PfLayout::BYTES,
+                               st, p, pp));
+        return WL_OK;
+    }
     dim3 grid(max_splits, rows->n_rows);
     WL_CUDA_TRY(launch_pdl(wl::mla_sparse_attn_kernel, grid, dim3(wl::AT_THREADS), AttnLayout::BYTES, st, p));
     WL_CUDA_TRY(cudaGetLastError());
@@ -1106,7 +1137,8 @@ int wl_attn_prefill(const wl_attn_cfg* cfg, const wl_attn_prefill_io* io, void* 
         return WL_ERR_ARG;
     }
     float* lse = io->lse ? io->lse : w_lse;
-    return launch_attn(cfg, &io->latent, T, T, &rows, io->q_abs, sel, stride, cnt, 0, 0, T, 0, io->ctx, lse, 1, st);
+    return launch_attn(cfg, &io->latent, T, T, &rows, io->q_abs, sel, stride, cnt, 0, 0, T, 0, io->ctx, lse, 1, st,
+                       true);
 }
 
 // ---- sharded decode ----------------------------------------------------------------------------
@@ -1334,6 +1366,9 @@ int wl_phase_read(float* us, int max_n) {
     int m = 0;
     for (int i = 1; i < n && m < max_n; ++i) us[m++] = (float)((h[i] - h[i - 1]) * 1e-3);
     return m;
+}
+int wl_pftrace_set(long long* buf) {
+    return cudaMemcpyToSymbol(wl::g_trace_pf, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
 }
 int wl_atrace_set(long long* buf) {
     return cudaMemcpyToSymbol(wl::g_trace_attn, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
