@@ -373,9 +373,7 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
                     v = fmaf(sW[j * IDX_H + h], fmaxf(fmaf(acc[32 + h], 0.03125f, acc[h]) * sc, 0.f), v);
                 const int r = r0 + j;
                 const bool valid = t < rows_len(r, p.rows_per_seq, p.len0, p.len_step, p.T);
-#ifndef WL_EXP_NOSTORE
                 if (valid) p.out[(long long)r * p.out_stride + t] = v;
-#endif
                 if constexpr (L::HIST)
                     if (hrow && valid) atomicAdd(&sHist[score_key(v) >> (32 - TOPK_HIST_BITS)], 1u);
             }
