@@ -9,6 +9,7 @@ Usage: ``python -m windlass_b200.build`` (or ``build()`` from Python).
 """
 from __future__ import annotations
 
+import glob
 import os
 import shutil
 import subprocess
@@ -19,9 +20,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libwl_attn.so")
 SOURCES = [os.path.join(CSRC, "wl_attn.cu")]
-DEPS = SOURCES + [os.path.join(CSRC, f) for f in ("ptx.cuh", "indexer.cuh", "topk.cuh", "mla_attn.cuh")] + [
-    os.path.join(ROOT, "include", "wl_attn.h")
-]
+DEPS = SOURCES + sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(ROOT, "include", "wl_attn.h")]
 
 
 def _nvcc() -> str:

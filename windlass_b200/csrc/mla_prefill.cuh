@@ -8,20 +8,23 @@
 //   O[h, :] += P[h, j] . c_kv[key j]                   (M = 64, N = 2 x 256 latent, K = 64 keys)
 // One CTA per query row; warp roles, connected by mbarriers:
 //   warps 4-11 gather:  the next 64 selected rows with 16-byte cp.async into one
-//              of two 72 KB key tiles (9 128B-swizzled chunks of 64 rows),
-//              while the tensor cores work on the other;
-//   warp 12    MMA:     P.V of tile i into O, then QK of tile i + 1 into one of
-//              two S accumulators;
-//   warps 0-3  softmax: per head, its 64 scores of a tile (TMEM lanes 16-31 of
-//              the warp's quarter, two threads per head), running max and sum,
-//              P (bf16) into shared memory as the A operand of P.V; rescale of
-//              O (TMEM lanes 0-15) when needed; the final O / l and lse.
-// TMEM (512 columns): an M = 64 accumulator occupies lanes 0-15 of each 32-lane
-// quarter (row m at lane 32 (m / 16) + m % 16); O sits there in all 512 columns,
-// the two S tiles at lane offset 16, each as PF_KSPLIT partial accumulators
-// (columns [64 (3 b + q), + 64)) that the softmax adds. Threads
-// reach one 16-lane half with the 16x32bx2 access shape, so the softmax and
-// the O accesses never touch each other's lanes.
+//              of three 72 KB key tiles (9 128B-swizzled chunks of 64 rows), the
+//              row indices prefetched a tile ahead;
+//   warp 12    MMA:     QK of tile i + 1 into one of two S accumulators, then P.V
+//              of tile i into O — the softmax of tile i overlaps QK(i + 1);
+//   warps 0-3  softmax: per head, its 64 scores of a tile (two threads per
+//              head), running max and sum, P (bf16) into shared memory as the A
+//              operand of P.V; rescale of O when needed; 1 / l and lse.
+// Tensor memory (512 columns x 128 lanes). An M = 64 accumulator occupies
+// lanes 0-15 of each 32-lane quarter (row m at lane 32 (m / 16) + m % 16), or
+// lanes 16-31 with a lane offset of 16:
+//   lanes 0-15:   O [64 x 512] fp32, all columns;
+//   lanes 16-31:  S tiles (columns [0, 64), [64, 128)) and the query as the QK
+//                 A operand (columns [128, 416): two bf16 per column) — an A
+//                 operand in tensor memory sits in its accumulator's lanes.
+// Threads reach one 16-lane half with the 16x32bx2 access shape, so the
+// softmax's and O's accesses never touch each other's lanes. The query passes
+// through the third key tile's space once, on its way into tensor memory.
 // Rescaling is lazy: a head's running max moves only when a tile's maximum
 // exceeds it by more than 2^8 (P <= 256 stays exact in bf16's relative
 // precision and fp32 sums), so O is rarely rescaled; P and l always use the
@@ -43,23 +46,24 @@ __device__ long long* g_trace_pf;
     } while (0)
 #endif
 
-constexpr int PF_TILE = 64;      // keys per tile
-constexpr int PF_KSPLIT = 3;     // independent QK accumulators per tile (3 K-chunks each)
-constexpr int PF_GATHER = 256;   // gather threads (warps 4-11)
+constexpr int PF_TILE = 64;       // keys per tile
+constexpr int PF_NBUF = 3;        // key tiles in shared memory
+constexpr int PF_GATHER = 256;    // gather threads (warps 4-11)
 constexpr int PF_THREADS = 128 + PF_GATHER + 32;  // softmax warps, gather warps, one MMA warp
 constexpr int PF_MMA_WARP = (128 + PF_GATHER) / 32;
 constexpr float PF_RESCALE_LOG2 = 8.f;
+constexpr uint32_t PF_TM_Q = 128;  // query columns in tensor memory (lanes 16-31)
 
 struct PfLayout {
     static constexpr uint32_t CHUNK = PF_TILE * 128;                     // 8 KB: 64 rows x 64 bf16
-    static constexpr uint32_t Q_CHUNK = AT_H * 128;                      // 8 KB
-    static constexpr uint32_t OFF_Q = 0;                                 // 9 chunks
-    static constexpr uint32_t OFF_K = OFF_Q + AT_CHUNKS * Q_CHUNK;       // 2 tiles x 9 chunks
-    static constexpr uint32_t OFF_P = OFF_K + 2 * AT_CHUNKS * CHUNK;     // 64 heads x 64 keys bf16
-    static constexpr uint32_t OFF_ROWS = OFF_P + AT_H * 128;             // 2 x 64 row indices
-    static constexpr uint32_t OFF_INVL = OFF_ROWS + 2 * PF_TILE * 4;  // [64] 1 / l per head
+    static constexpr uint32_t TILE = AT_CHUNKS * CHUNK;                  // 72 KB
+    static constexpr uint32_t OFF_K = 0;                                 // PF_NBUF tiles
+    static constexpr uint32_t OFF_P = OFF_K + PF_NBUF * TILE;            // 64 heads x 64 keys bf16
+    static constexpr uint32_t OFF_ROWS = OFF_P + AT_H * 128;             // PF_NBUF x 64 row indices
+    static constexpr uint32_t OFF_INVL = OFF_ROWS + PF_NBUF * PF_TILE * 4;  // [64] 1 / l per head
     static constexpr uint32_t OFF_BAR = OFF_INVL + AT_H * 4;
-    static constexpr int N_BARS = 2 + 2 + 2 + 2 + 1 + 1 + 1;  // kfull, kfree, sfull, sfree, pready, pvdone, q
+    // kfull, kfree (per tile buffer), sfull, sfree (per S buffer), pready, pvdone, qload, qtmem
+    static constexpr int N_BARS = 2 * PF_NBUF + 2 * 2 + 4;
     static constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;
     static constexpr uint32_t BYTES = OFF_MISC + 32 + 1024;
     static constexpr uint32_t TMEM_COLS = 512;
@@ -67,9 +71,10 @@ struct PfLayout {
     static constexpr uint32_t IDESC_PV = idesc_bf16(64, 256, 0, 1);
 };
 static_assert(PfLayout::BYTES <= 232448, "one CTA per SM");
+static_assert(PF_TM_Q + AT_D / 2 <= 512, "query columns fit beside the S tiles");
 
 // The absorbed queries as a bf16 tensor {576, 64 rows}: 64 x 64 boxes with
-// 128B swizzle land exactly as the K-major chunks the MMA reads.
+// 128B swizzle land as the K-major chunks the MMA reads.
 struct PfParams {
     CUtensorMap tm_q;  // {AT_D, 64 * n_rows}, box {64, 64}
 };
@@ -87,18 +92,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     using L = PfLayout;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t sQ = smem_u32(smem + L::OFF_Q);
     const uint32_t sK = smem_u32(smem + L::OFF_K);
     const uint32_t sP = smem_u32(smem + L::OFF_P);
+    const uint32_t sQstage = sK + (PF_NBUF - 1) * L::TILE;  // the query's way in (last tile's space)
     int* rows_sh = reinterpret_cast<int*>(smem + L::OFF_ROWS);
     float* inv_l_sh = reinterpret_cast<float*>(smem + L::OFF_INVL);
     uint64_t* kfull = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-    uint64_t* kfree = kfull + 2;
-    uint64_t* sfull = kfree + 2;
+    uint64_t* kfree = kfull + PF_NBUF;
+    uint64_t* sfull = kfree + PF_NBUF;
     uint64_t* sfree = sfull + 2;
     uint64_t* pready = sfree + 2;
     uint64_t* pvdone = pready + 1;
-    uint64_t* qbar = pvdone + 1;
+    uint64_t* qload = pvdone + 1;
+    uint64_t* qtmem = qload + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -122,19 +128,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const int n_tiles = (n_keys + PF_TILE - 1) / PF_TILE;
 
     if (tid == 0) {
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < PF_NBUF; ++b) {
             mbar_init(kfull + b, PF_GATHER);  // the gather threads
-            mbar_init(kfree + b, 1);    // the P.V commit
+            mbar_init(kfree + b, 1);          // the P.V commit
+        }
+        for (int b = 0; b < 2; ++b) {
             mbar_init(sfull + b, 1);    // the QK commit
             mbar_init(sfree + b, 128);  // the softmax threads
         }
         mbar_init(pready, 128);
         mbar_init(pvdone, 1);
-        mbar_init(qbar, 1);
+        mbar_init(qload, 1);
+        mbar_init(qtmem, 128);  // the softmax threads, once the query is in tensor memory
         fence_mbar_init();
-        // the row's absorbed query [64][576]: 9 TMA boxes (the MMA waits on qbar)
-        mbar_expect_tx(qbar, AT_CHUNKS * L::Q_CHUNK);
-        for (int c = 0; c < AT_CHUNKS; ++c) tma_load2d(sQ + (uint32_t)c * L::Q_CHUNK, &pp.tm_q, c * 64, r * AT_H, qbar);
+        // the row's absorbed query [64][576]: 9 TMA boxes into the staging tile
+        mbar_expect_tx(qload, AT_CHUNKS * L::CHUNK);
+        for (int c = 0; c < AT_CHUNKS; ++c) tma_load2d(sQstage + (uint32_t)c * L::CHUNK, &pp.tm_q, c * 64, r * AT_H, qload);
     }
     if (warp == PF_MMA_WARP) tmem_alloc(tmem_slot, L::TMEM_COLS);
     tc_fence_before();
@@ -161,15 +170,21 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         };
         int key_next = key_of(0);  // indices one tile ahead: their load latency hides behind a tile
         for (int i = 0; i < n_tiles; ++i) {
-            const int b = i & 1;
-            // one thread waits for the buffer and tells the others, so that all
-            // gather threads leave together on a timeout (the named barriers need all)
-            if (g == 0) *go = (i < 2 || mbar_wait_fast(kfree + b, (uint32_t)((i >> 1) - 1) & 1u, 30)) ? 1 : 0;
+            const int b = i % PF_NBUF;
+            // One thread waits for the buffer (and, for the staging tile's first
+            // use, for the query to have left it) and tells the others, so that
+            // all gather threads leave together on a timeout.
+            if (g == 0) {
+                bool ok = true;
+                if (i >= PF_NBUF) ok = mbar_wait_fast(kfree + b, (uint32_t)(i / PF_NBUF - 1) & 1u, 30);
+                else if (b == PF_NBUF - 1) ok = mbar_wait_fast(qtmem, 0, 29);
+                *go = ok ? 1 : 0;
+            }
             if (g < PF_TILE) rows_sh[b * PF_TILE + g] = key_next;
             asm volatile("bar.sync 2, %0;" ::"n"(PF_GATHER) : "memory");
             if (!*go) break;
             key_next = key_of(i + 1);
-            const uint32_t tile = sK + (uint32_t)b * AT_CHUNKS * L::CHUNK;
+            const uint32_t tile = sK + (uint32_t)b * L::TILE;
 #pragma unroll 3
             for (int k2 = 0; k2 < AT_CHUNKS * PF_TILE * 8 / PF_GATHER; ++k2) {  // 18 pieces of 16 B per thread
                 const int pid = k2 * PF_GATHER + g;
@@ -186,48 +201,40 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             fence_proxy_async_smem();
             mbar_arrive(kfull + b);
             if (g == 0) WL_TPF(1, i);
-            asm volatile("bar.sync 2, %0;" ::"n"(PF_GATHER) : "memory");  // rows_sh[b] is rewritten two tiles on
+            asm volatile("bar.sync 2, %0;" ::"n"(PF_GATHER) : "memory");  // rows_sh[b] is rewritten PF_NBUF tiles on
         }
     } else if (warp == PF_MMA_WARP) {
         // ---------------- MMA ----------------
-        // PV(i) goes before QK(i + 1): it frees tile i's buffer early, so the
-        // gather of tile i + 2 hides behind QK(i + 1) and the softmax.
+        const uint32_t tq = tmem + (16u << 16) + PF_TM_Q;  // the query, A operand of QK
         auto issue_qk = [&](int i) -> bool {
-            const int b = i & 1;
-            if (!mbar_wait_fast(kfull + b, (uint32_t)(i >> 1) & 1u, 32)) return false;
-            if (i >= 2 && !mbar_wait_fast(sfree + b, (uint32_t)((i >> 1) - 1) & 1u, 33)) return false;
+            const int b = i % PF_NBUF, s = i & 1;
+            if (!mbar_wait_fast(kfull + b, (uint32_t)(i / PF_NBUF) & 1u, 32)) return false;
+            if (i >= 2 && !mbar_wait_fast(sfree + s, (uint32_t)((i >> 1) - 1) & 1u, 33)) return false;
             tc_fence_after();
             if (lane == 0) {
                 WL_TPF(2, i);
-                const uint32_t tile = sK + (uint32_t)b * AT_CHUNKS * L::CHUNK;
-                // K split over PF_KSPLIT accumulators, interleaved so consecutive
-                // MMAs never wait on each other (one accumulator chains them)
+                const uint32_t tile = sK + (uint32_t)b * L::TILE;
+                const uint32_t d = tmem + (16u << 16) + (uint32_t)(s * PF_TILE);
 #pragma unroll 1
-                for (int c0 = 0; c0 < AT_CHUNKS / PF_KSPLIT; ++c0) {
+                for (int c = 0; c < AT_CHUNKS; ++c) {
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-                        for (int q = 0; q < PF_KSPLIT; ++q) {
-                            const int c = q * (AT_CHUNKS / PF_KSPLIT) + c0;
-                            const uint32_t d = tmem + (16u << 16) + (uint32_t)((b * PF_KSPLIT + q) * PF_TILE);
-                            mma_bf16(d, desc_sw128(sQ + (uint32_t)c * L::Q_CHUNK + kk * 32, 16, 1024),
-                                     desc_sw128(tile + (uint32_t)c * L::CHUNK + kk * 32, 16, 1024), L::IDESC_QK,
-                                     (c0 | kk) != 0 ? 1u : 0u);
-                        }
-                    }
+                    for (int kk = 0; kk < 4; ++kk)  // K = 16: 8 columns of the query per step
+                        mma_bf16_ts(d, tq + (uint32_t)(c * 32 + kk * 8),
+                                    desc_sw128(tile + (uint32_t)c * L::CHUNK + kk * 32, 16, 1024), L::IDESC_QK,
+                                    (c | kk) != 0 ? 1u : 0u);
                 }
-                mma_commit(sfull + b);
+                mma_commit(sfull + s);
             }
             __syncwarp();
             return true;
         };
         auto issue_pv = [&](int i) -> bool {
-            const int b = i & 1;
+            const int b = i % PF_NBUF;
             if (!mbar_wait_fast(pready, (uint32_t)i & 1u, 34)) return false;
             tc_fence_after();
             if (lane == 0) {
                 WL_TPF(3, i);
-                const uint32_t tile = sK + (uint32_t)b * AT_CHUNKS * L::CHUNK;
+                const uint32_t tile = sK + (uint32_t)b * L::TILE;
 #pragma unroll
                 for (int ks = 0; ks < PF_TILE / 16; ++ks) {
 #pragma unroll
@@ -242,11 +249,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             __syncwarp();
             return true;
         };
-        bool ok = mbar_wait_fast(qbar, 0, 38);
-        ok = ok && issue_qk(0);
+        bool ok = mbar_wait_fast(qtmem, 0, 38) && issue_qk(0);
         for (int i = 0; ok && i < n_tiles; ++i) {
-            ok = issue_pv(i);
-            if (ok && i + 1 < n_tiles) ok = issue_qk(i + 1);
+            if (i + 1 < n_tiles) ok = issue_qk(i + 1);
+            if (ok) ok = issue_pv(i);
         }
     } else {
         // ---------------- softmax (warps 0-3) ----------------
@@ -256,25 +262,42 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const int h = 16 * warp + (lane & 15);
         const bool hi_half = lane >= 16;
         const uint32_t lane_o = (uint32_t)(32 * warp) << 16, lane_s = (uint32_t)(32 * warp + 16) << 16;
+        // The query into tensor memory, lanes 16-31, columns PF_TM_Q + [0, 288):
+        // column c = elements (2c, 2c + 1) of the row; thread t < 16 writes
+        // columns [16 k, 16 k + 16), thread t + 16 columns 144 + [16 k, 16 k + 16).
+        bool ok = mbar_wait_fast(qload, 0, 39);
+        if (ok) {
+#pragma unroll 1
+            for (int k = 0; k < 9; ++k) {
+                const int e0 = 32 * k + (hi_half ? 288 : 0);  // first element of this thread's 16 columns
+                const uint32_t src = sQstage + (uint32_t)(e0 >> 6) * L::CHUNK + (uint32_t)h * 128u;
+                const int seg0 = (e0 & 63) >> 3;             // 16-byte pieces: 8 elements each
+                uint32_t v[16];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 x = lds_v4(src + ((((uint32_t)(seg0 + q)) ^ (uint32_t)h) & 7u) * 16u);
+                    v[4 * q] = x.x;
+                    v[4 * q + 1] = x.y;
+                    v[4 * q + 2] = x.z;
+                    v[4 * q + 3] = x.w;
+                }
+                tmem_st16x2_16u<144>(tmem + lane_s + PF_TM_Q + (uint32_t)(16 * k), v);
+            }
+            tmem_wait_st();
+        }
+        tc_fence_before();
+        mbar_arrive(qtmem);  // the MMA may read the query; the staging tile is free for keys
         float m_run = -INFINITY, l_run = 0.f;
-        bool ok = true;
         for (int i = 0; i < n_tiles && ok; ++i) {
-            const int b = i & 1;
+            const int s = i & 1;
             const int nv = min(PF_TILE, n_keys - i * PF_TILE);
-            if (!(ok = mbar_wait_fast(sfull + b, (uint32_t)(i >> 1) & 1u, 35))) break;
+            if (!(ok = mbar_wait_fast(sfull + s, (uint32_t)(i >> 1) & 1u, 35))) break;
             if (tid == 0) WL_TPF(4, i);
             tc_fence_after();
             float sv[32];
-            tmem_ld16x2_32<32>(tmem + lane_s + (uint32_t)(b * PF_KSPLIT * PF_TILE), sv);
-#pragma unroll
-            for (int q = 1; q < PF_KSPLIT; ++q) {
-                float sq[32];
-                tmem_ld16x2_32<32>(tmem + lane_s + (uint32_t)((b * PF_KSPLIT + q) * PF_TILE), sq);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) sv[j] += sq[j];
-            }
+            tmem_ld16x2_32<32>(tmem + lane_s + (uint32_t)(s * PF_TILE), sv);
             tc_fence_before();
-            mbar_arrive(sfree + b);
+            mbar_arrive(sfree + s);
             const int j0 = hi_half ? 32 : 0;
             float tmax = -INFINITY;
 #pragma unroll
@@ -340,7 +363,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const int q4 = warp & 3, hq = 16 * q4 + (lane & 15);
         const bool hi = lane >= 16;
         const uint32_t lane_o = (uint32_t)(32 * q4) << 16;
-        bool done = mbar_wait_fast(pvdone, (uint32_t)(n_tiles - 1) & 1u, 37);
+        const bool done = mbar_wait_fast(pvdone, (uint32_t)(n_tiles - 1) & 1u, 37);
         tc_fence_after();
         if (done) {
             const float inv = inv_l_sh[hq];
