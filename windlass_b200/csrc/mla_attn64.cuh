@@ -1,12 +1,14 @@
-// mla_prefill.cuh — sparse absorbed-MLA attention for many query rows
-// (chunked prefill): the 64 heads of one query row form the M dimension.
+// mla_attn64.cuh — sparse absorbed-MLA attention with the 64 heads of one
+// query row as the M dimension (chunked prefill and split-K decode).
 //
 // Same computation as mla_sparse_attn_kernel (src/glm_layer_runner.cuh:251-298
-// with the index mask of src/glm_kernels.cuh:526-545), organised for rows that
-// each attend over up to thousands of keys:
+// with the index mask of src/glm_kernels.cuh:526-545), organised as a pipeline
+// over 64-key tiles of one row's selection (or of a split of it):
 //   S[h, j]  = q_abs[h] . [c_kv | k_rot][key j]        (M = 64 heads, N = 64 keys, K = 576)
 //   O[h, :] += P[h, j] . c_kv[key j]                   (M = 64, N = 2 x 256 latent, K = 64 keys)
-// One CTA per query row; warp roles, connected by mbarriers:
+// grid (splits, rows): one CTA per (query row, range of its list inside the key
+// window), writing that range's normalised o and lse (one partial, merged by
+// lse_merge_kernel when a row has several). Warp roles, connected by mbarriers:
 //   warps 4-11 gather:  the next 64 selected rows with 16-byte cp.async into one
 //              of three 72 KB key tiles (9 128B-swizzled chunks of 64 rows), the
 //              row indices prefetched a tile ahead;
@@ -38,7 +40,7 @@ namespace wl {
 __device__ long long* g_trace_pf;
 #define WL_TPF(slot, i)                                                                              \
     do {                                                                                             \
-        if (g_trace_pf && blockIdx.x == 100 && (i) < 64) g_trace_pf[(i) * 8 + (slot)] = clock64();  \
+        if (g_trace_pf && blockIdx.y == 100 && blockIdx.x == 0 && (i) < 64) g_trace_pf[(i) * 8 + (slot)] = clock64();  \
     } while (0)
 #else
 #define WL_TPF(slot, i) \
@@ -65,7 +67,7 @@ struct PfLayout {
     // kfull, kfree (per tile buffer), sfull, sfree (per S buffer), pready, pvdone, qload, qtmem
     static constexpr int N_BARS = 2 * PF_NBUF + 2 * 2 + 4;
     static constexpr uint32_t OFF_MISC = OFF_BAR + N_BARS * 8;
-    static constexpr uint32_t BYTES = OFF_MISC + 32 + 1024;
+    static constexpr uint32_t BYTES = OFF_MISC + 32 + 1024;  // misc: TMEM slot, gather flag, e0, e1
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t IDESC_QK = idesc_bf16(64, PF_TILE, 0, 0);
     static constexpr uint32_t IDESC_PV = idesc_bf16(64, 256, 0, 1);
@@ -88,7 +90,7 @@ __device__ __forceinline__ void tma_load2d(uint32_t dst, const CUtensorMap* tm, 
 }
 
 __global__ void __launch_bounds__(PF_THREADS, 1)
-    mla_prefill_kernel(AttnParams p, const __grid_constant__ PfParams pp) {
+    mla_attn64_kernel(AttnParams p, const __grid_constant__ PfParams pp) {
     using L = PfLayout;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -109,16 +111,66 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) WL_TPF(7, 0);
-    const int r = blockIdx.x;
+    const int r = blockIdx.y, split = blockIdx.x;
     const int seq = r / p.rows_per_seq;
     const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
-    const int len = (int)(lraw < p.len_T ? lraw : p.len_T);
+    const long long len = lraw < p.len_T ? lraw : p.len_T;
     const int* list = p.sel ? p.sel + (long long)r * p.sel_stride : nullptr;
     pdl_wait();
     pdl_trigger();
-    const int n_keys = list ? (p.sel_n_dev ? __ldg(p.sel_n_dev + r) : p.sel_n) : len;
-    float* ctx = p.o_part + (long long)r * (AT_H * AT_DV);
-    float* lse_out = p.lse_part + (long long)r * AT_H;
+    // Entry range [e0, e1) of the list (or key range) inside the key window
+    // [win_lo, win_hi) — a 32-ary lower-bound search on the ascending list by
+    // warps 0 and 1 when the window cuts the row — then this CTA's split of it.
+    int* misc = reinterpret_cast<int*>(smem + L::OFF_MISC) + 2;  // [0] e0, [1] e1
+    {
+        const long long lo_key = p.win_lo > 0 ? p.win_lo : 0;
+        const long long hi_key = p.win_hi < len ? p.win_hi : len;
+        if (!list) {
+            if (tid == 0) {
+                misc[0] = (int)lo_key;
+                misc[1] = (int)(hi_key > lo_key ? hi_key : lo_key);
+            }
+        } else {
+            const int n = p.sel_n_dev ? __ldg(p.sel_n_dev + r) : p.sel_n;
+            if (p.win_lo <= 0 && p.win_hi >= len) {
+                if (tid == 0) {
+                    misc[0] = 0;
+                    misc[1] = n;
+                }
+            } else if (warp < 2) {
+                const long long key = warp == 0 ? lo_key : hi_key;
+                int lo = 0, hi = n;  // first position whose key is >= `key` (or n)
+                while (hi > lo) {
+                    const int step = (hi - lo + 31) / 32;
+                    const int pos = lo + lane * step;
+                    const bool less = pos < hi && (long long)__ldg(list + pos) < key;
+                    const int cnt = __popc(__ballot_sync(0xffffffffu, less));
+                    if (cnt == 0) break;
+                    const int nlo = lo + (cnt - 1) * step + 1;
+                    hi = min(hi, lo + cnt * step);
+                    lo = nlo;
+                }
+                if (lane == 0) misc[warp] = lo;
+            }
+        }
+    }
+    __syncthreads();
+    int cb, ce;
+    {
+        const int e0 = misc[0], e1 = max(misc[1], misc[0]);
+        if (p.split_keys > 0) {
+            cb = e0 + split * p.split_keys;
+            ce = min(cb + p.split_keys, e1);
+        } else {
+            cb = e0;
+            ce = split == 0 ? e1 : e0;
+        }
+        ce = max(ce, cb);
+    }
+    __syncthreads();  // misc is reused below
+    const int n_keys = ce - cb;
+    float* ctx = p.o_part + ((long long)r * p.max_splits + split) * (AT_H * AT_DV);
+    float* lse_out = p.lse_part + ((long long)r * p.max_splits + split) * AT_H;
     if (n_keys <= 0) {
         for (int i = tid; i < AT_H * AT_DV / 4; i += PF_THREADS)
             reinterpret_cast<float4*>(ctx)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -158,15 +210,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         // ---------------- gather ----------------
         const int g = tid - 128;
         volatile int* go = reinterpret_cast<volatile int*>(tmem_slot + 1);
-        auto key_of = [&](int i) -> int {  // this thread's row index of tile i (g < PF_TILE), -1 past the list
+        auto key_of = [&](int i) -> int {  // this thread's cache row of tile i (g < PF_TILE), -1 past the range
             const int e = i * PF_TILE + g;
             if (g >= PF_TILE || i >= n_tiles || e >= n_keys) return -1;
-            const long long key = list ? (long long)__ldg(list + e) : (long long)e;
-            if (key < 0 || key >= p.T) {
+            const long long key = list ? (long long)__ldg(list + cb + e) : (long long)(cb + e);
+            const long long row = key - p.win_lo;  // the cache holds the window's keys
+            if (row < 0 || row >= p.T) {
                 set_error(ERRC_BOUNDS, 31);
                 return -1;
             }
-            return (int)key;
+            return (int)row;
         };
         int key_next = key_of(0);  // indices one tile ahead: their load latency hides behind a tile
         for (int i = 0; i < n_tiles; ++i) {

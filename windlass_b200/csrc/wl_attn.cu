@@ -20,7 +20,7 @@
 #include "../../include/wl_attn.h"
 #include "indexer.cuh"
 #include "mla_attn.cuh"
-#include "mla_prefill.cuh"
+#include "mla_attn64.cuh"
 #include "p2p.cuh"
 #include "topk.cuh"
 
@@ -48,7 +48,6 @@ int g_ph_n = -1;  // -1: off
     } while (0)
 #endif
 
-using wl::AttnLayout;
 constexpr int kMaxSplits = 16;   // split-K CTAs per decode row
 constexpr int kMaxDevices = 64;
 
@@ -89,9 +88,7 @@ int ensure_attrs() {
     if (dev < 0 || dev >= kMaxDevices) return WL_ERR_CUDA;
     std::lock_guard<std::mutex> lk(g_attr_mu);
     if (g_attr_done[dev]) return WL_OK;
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     AttnLayout::BYTES));
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_attn64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::PfLayout::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::sel_normalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      200 * 1024));
@@ -509,17 +506,13 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     p.o_part = o_part;
     p.lse_part = lse_part;
     p.scale_log2 = cfg->softmax_scale * 1.4426950408889634f;
-    if (many_rows && split_keys == 0 && max_splits == 1 && win_lo <= 0 && win_hi >= len_T) {
-        // Many query rows, each over its whole list (prefill): heads as M,
-        // gather / QK / softmax / P.V pipelined within the row.
-        wl::PfParams pp{};
-        if (int e = encode_q_map(&pp.tm_q, q_abs, rows->n_rows)) return e;
-        WL_CUDA_TRY(launch_pdl(wl::mla_prefill_kernel, dim3(rows->n_rows), dim3(wl::PF_THREADS), wl::PfLayout::BYTES,
-                               st, p, pp));
-        return WL_OK;
-    }
-    dim3 grid(max_splits, rows->n_rows);
-    WL_CUDA_TRY(launch_pdl(wl::mla_sparse_attn_kernel, grid, dim3(wl::AT_THREADS), AttnLayout::BYTES, st, p));
+    // Heads as M = 64, gather / QK / softmax / P.V pipelined over 64-key tiles;
+    // grid (splits, rows), each CTA one (o, lse) partial.
+    (void)many_rows;
+    wl::PfParams pp{};
+    if (int e = encode_q_map(&pp.tm_q, q_abs, rows->n_rows)) return e;
+    WL_CUDA_TRY(launch_pdl(wl::mla_attn64_kernel, dim3(max_splits, rows->n_rows), dim3(wl::PF_THREADS),
+                           wl::PfLayout::BYTES, st, p, pp));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
 }
