@@ -79,7 +79,19 @@ static_assert(PF_TM_Q + AT_D / 2 <= 512, "query columns fit beside the S tiles")
 // 128B swizzle land as the K-major chunks the MMA reads.
 struct PfParams {
     CUtensorMap tm_q;  // {AT_D, 64 * n_rows}, box {64, 64}
+    // The (o) partials [rows][splits][64][512] fp32 as {512, 64 * rows * splits},
+    // 32 x 64 boxes with 128B swizzle: O leaves through shared memory and TMA
+    // stores (o_tma), else with plain stores.
+    CUtensorMap tm_o;
+    int o_tma;
 };
+
+__device__ __forceinline__ void tma_store2d(const CUtensorMap* tm, int x, int y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+}
 
 __device__ __forceinline__ void tma_load2d(uint32_t dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -418,7 +430,24 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const uint32_t lane_o = (uint32_t)(32 * q4) << 16;
         const bool done = mbar_wait_fast(pvdone, (uint32_t)(n_tiles - 1) & 1u, 37);
         tc_fence_after();
-        if (done) {
+        if (done && pp.o_tma) {
+            // stage: box k = columns [32 k, 32 k + 32), row hq, 16-byte chunks
+            // swizzled by the row (every key tile is consumed by now)
+            const float inv = inv_l_sh[hq];
+#pragma unroll 1
+            for (int c = grp * 32; c < 256; c += 32 * ngrp) {
+                float ov[32];
+                tmem_ld16x2_32<256>(tmem + lane_o + (uint32_t)c, ov);
+                const int k = (c >> 5) + (hi ? 8 : 0);
+                const uint32_t row = sK + (uint32_t)k * (AT_H * 128) + (uint32_t)hq * 128u;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    sts_v4(row + ((((uint32_t)j) ^ (uint32_t)hq) & 7u) * 16u,
+                           make_uint4(__float_as_uint(ov[4 * j] * inv), __float_as_uint(ov[4 * j + 1] * inv),
+                                      __float_as_uint(ov[4 * j + 2] * inv), __float_as_uint(ov[4 * j + 3] * inv)));
+            }
+            fence_proxy_async_smem();
+        } else if (done) {
             const float inv = inv_l_sh[hq];
             float* crow = ctx + (long long)hq * AT_DV + (hi ? 256 : 0);
 #pragma unroll 1
@@ -429,6 +458,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                 for (int e = 0; e < 32; e += 4)
                     *reinterpret_cast<float4*>(crow + c + e) =
                         make_float4(ov[e] * inv, ov[e + 1] * inv, ov[e + 2] * inv, ov[e + 3] * inv);
+            }
+        }
+        if (pp.o_tma) {
+            asm volatile("bar.sync 3, %0;" ::"n"(PF_MMA_WARP * 32) : "memory");  // the staged boxes are complete
+            if (tid == 0 && done) {
+                const int row0 = (r * p.max_splits + split) * AT_H;
+                for (int k = 0; k < AT_DV / 32; ++k)
+                    tma_store2d(&pp.tm_o, 32 * k, row0, sK + (uint32_t)k * (AT_H * 128));
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // written before the CTA retires
             }
         }
     }

@@ -192,6 +192,21 @@ int encode_q_map(CUtensorMap* tm, const void* q_abs, int32_t n_rows) {
     return WL_OK;
 }
 
+// The (o) partials [rows * splits][64][512] fp32 as {512, 64 rows * splits},
+// 32 x 64 boxes, 128B swizzle (the attention's staged output).
+int encode_o_map(CUtensorMap* tm, void* o_part, int64_t n_parts) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return WL_ERR_CUDA;
+    const cuuint64_t dims[2] = {(cuuint64_t)wl::AT_DV, (cuuint64_t)(wl::AT_H * n_parts)};
+    const cuuint64_t strides[1] = {(cuuint64_t)wl::AT_DV * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)wl::AT_H};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, o_part, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? WL_OK : WL_ERR_CUDA;
+}
+
 int rows_ok(const wl_rows* r, int32_t T) {
     if (!r || r->n_rows <= 0 || r->rows_per_seq <= 0 || r->len0 < 0 || r->len_step < 0 || T <= 0)
         return WL_ERR_ARG;
@@ -511,6 +526,7 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     (void)many_rows;
     wl::PfParams pp{};
     if (int e = encode_q_map(&pp.tm_q, q_abs, rows->n_rows)) return e;
+    pp.o_tma = aligned16(o_part) && encode_o_map(&pp.tm_o, o_part, (int64_t)rows->n_rows * max_splits) == WL_OK;
     WL_CUDA_TRY(launch_pdl(wl::mla_attn64_kernel, dim3(max_splits, rows->n_rows), dim3(wl::PF_THREADS),
                            wl::PfLayout::BYTES, st, p, pp));
     WL_CUDA_TRY(cudaGetLastError());
