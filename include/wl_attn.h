@@ -221,8 +221,9 @@ int wl_indexer_topk(const float* index, int64_t index_stride, const wl_rows* row
                     int32_t T, int32_t k, const int32_t* cand_idx,
                     int32_t* sel_out, int64_t sel_stride, int32_t* sel_n_out,
                     void* workspace, size_t workspace_bytes, void* stream);
-/* Workspace that lets wl_indexer_topk split rows longer than 40960 keys over
- * many CTAs (without it such rows run one CTA each). */
+/* Workspace that lets wl_indexer_topk spread a row over many CTAs: rows of
+ * 8 193 - 196 608 keys select on an 8-CTA thread-block cluster, longer ones in
+ * a multi-CTA partition pass (without it every row runs on one CTA). */
 size_t wl_indexer_topk_workspace_bytes(int32_t n_rows, int32_t T);
 
 /* a5 semantics: turn an arbitrary index list (any order, duplicates, entries

@@ -8,7 +8,9 @@
 //   consumer -> (require) -> [normalise list] -> sparse attention
 //   dense    -> attention over every key
 // followed by the split-K (o, lse) merge. All launches go on the caller's
-// stream; nothing allocates; every failure is a status code.
+// stream, with programmatic dependent launch between the library's kernels;
+// no call allocates (a communicator allocates its peer-exchange region once,
+// at creation); every failure is a status code.
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
