@@ -474,3 +474,17 @@ def test_topk_multi_cta_with_heavy_ties():
     x[rng.choice(60000, 100, replace=False)] = 1.0
     _topk_case(x, 2048)
     _topk_case(rng.integers(0, 3, 220000).astype(np.float32), 2048)  # partitioned path
+
+
+@pytest.mark.parametrize("n_cross", [4096, 4097])
+def test_topk_cluster_crossing_bin_at_gather_capacity(n_cross):
+    """The cluster top-k gathers the keys of the first-level bin holding the
+    k-th key into one CTA when there are at most 4096 of them, else refines
+    over the cluster; both sides of that limit select numpy's set."""
+    rng = np.random.default_rng(n_cross)
+    T = 100000
+    x = rng.uniform(0.0, 0.5, T).astype(np.float32)
+    pos = rng.permutation(T)
+    x[pos[:1500]] = 10.0 + rng.uniform(0, 1, 1500).astype(np.float32)  # above the crossing bin
+    x[pos[1500:1500 + n_cross]] = rng.uniform(1.0, 1.0625, n_cross).astype(np.float32)  # one 13-bit bin
+    _topk_case(x, 2048)

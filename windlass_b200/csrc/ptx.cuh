@@ -196,6 +196,24 @@ __device__ __forceinline__ uint32_t dsmem_ld_u32(const void* local, uint32_t ran
     asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(ra) : "memory");
     return v;
 }
+// Address of `local`'s counterpart in CTA `rank` of the cluster; remote access by it.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    return ra;
+}
+__device__ __forceinline__ uint32_t dsmem_atom_add(uint32_t ra, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(ra), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void dsmem_st_v2(uint32_t ra, uint32_t a, uint32_t b) {
+    asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(ra), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void dsmem_st_v4(uint32_t ra, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
 __device__ __forceinline__ void cluster_arrive() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }

@@ -507,17 +507,22 @@ __global__ void __launch_bounds__(TOPKM_THREADS) topk_emit_kernel(TopkMParams p)
 // (PER consecutive keys per thread), read once. With the first-level histogram
 // (top HBITS bits) from the indexer's epilogue:
 //   1. every CTA finds the bin b1 holding the k-th key from that histogram;
-//   2. two refinement passes (10 + 9 bits) over the keys in b1: each CTA builds
-//      its shared-memory histogram, the cluster barrier publishes them, every
-//      CTA sums the TOPKC_CL histograms over distributed shared memory and
-//      finds the next bin — giving the exact k-th key `thr` and how many keys
-//      equal to it are taken (`need`);
-//   3. each CTA counts its keys > thr and == thr (block scan), the CTAs
-//      exchange their totals over distributed shared memory, and every thread
+//   2. two refinement passes (10 + 9 bits) over the keys in b1, giving the
+//      exact k-th key `thr` and how many keys equal to it are taken (`need`).
+//      When b1 holds at most TOPKC_GCAP keys, every warp stores its keys of b1
+//      into CTA 0's shared memory (slots reserved by one distributed-shared-
+//      memory atomic per warp); CTA 0 refines over them, counts every CTA's
+//      keys > thr and == thr, and writes each CTA its thr, need and output
+//      bases (two cluster barriers). Otherwise each CTA builds its shared-
+//      memory histogram, a cluster barrier publishes them, every CTA sums the
+//      TOPKC_CL histograms over distributed shared memory and finds the next
+//      bin, and the CTAs exchange their totals of > thr and == thr;
+//   3. each CTA's block scan gives every thread its offsets, and every thread
 //      writes its selected keys at their final, ascending positions.
 // One launch, no global scratch beyond the histogram.
 constexpr int TOPKC_CL = 8;
 constexpr int TOPKC_THREADS = 1024;
+constexpr int TOPKC_GCAP = 4096;  // keys of the crossing bin CTA 0 gathers (else the distributed refinement)
 
 #ifdef WL_TRACE
 __device__ long long* g_trace_topk;
@@ -542,10 +547,12 @@ __device__ long long* g_trace_topk;
 // consecutive bins [t * PERB, (t + 1) * PERB) with counts c[0..PERB) (higher t
 // and higher j = higher bins). Every thread returns the bin b where the running
 // count from the top crosses `need` (count(bins > b) < need <= count(bins >= b))
-// and count(bins > b). `sh` holds >= 35 words. Requires need <= total.
+// and count(bins > b), and with `out_count` the count of bin b. `sh` holds >= 35
+// words (36 with `out_count`). Requires need <= total.
 template <int PERB>
 __device__ __forceinline__ void block_find_from_top(const uint32_t (&c)[PERB], uint32_t need, uint32_t* sh,
-                                                    uint32_t* out_bin, uint32_t* out_above) {
+                                                    uint32_t* out_bin, uint32_t* out_above,
+                                                    uint32_t* out_count = nullptr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint32_t s = 0;
 #pragma unroll
@@ -570,6 +577,7 @@ __device__ __forceinline__ void block_find_from_top(const uint32_t (&c)[PERB], u
         for (int j = PERB - 1; j >= 0; --j) {
             if (above < need && need <= above + c[j]) {
                 b = (uint32_t)(threadIdx.x * PERB + j);
+                if (out_count) sh[35] = c[j];
                 break;
             }
             above += c[j];
@@ -580,6 +588,7 @@ __device__ __forceinline__ void block_find_from_top(const uint32_t (&c)[PERB], u
     __syncthreads();
     *out_bin = sh[33];
     *out_above = sh[34];
+    if (out_count) *out_count = sh[35];
     __syncthreads();
 }
 
@@ -593,6 +602,12 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     __shared__ uint32_t hloc[2][1024];  // this CTA's refinement histograms (read by the cluster)
     __shared__ uint32_t scan_sh[36];
     __shared__ uint32_t tot[2];  // this CTA's count of keys > thr, == thr (read by the cluster)
+    __shared__ uint2 gcand[TOPKC_GCAP];  // CTA 0: the crossing bin's (key, position) from every CTA
+    // CTA 0: [0] candidates gathered; [1 + c] CTA c's keys above the crossing bin;
+    // [1 + CL + c], [1 + 2 CL + c] CTA c's candidates > thr, == thr
+    __shared__ uint32_t gctl[1 + 3 * TOPKC_CL];
+    // written by CTA 0 (one 16-byte store): thr, need, this CTA's output bases (> thr, == thr)
+    __shared__ __align__(16) uint32_t res[4];
     const int tid = threadIdx.x, r = blockIdx.y;
     const uint32_t rank = cluster_ctarank();
     const int len = topk_row_len(p, r);
@@ -637,12 +652,16 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
         for (int j = 0; j < PER; ++j) f[j] = j < nvalid ? in[i0 + j] : 0.f;
     }
     for (int i = tid; i < 2 * 1024; i += TOPKC_THREADS) (&hloc[0][0])[i] = 0;
+    if (tid < 1 + 3 * TOPKC_CL) gctl[tid] = 0;
+    // Every CTA of the cluster has started and CTA 0's counters are zero
+    // before any remote access (the wait follows level 1).
+    cluster_arrive();
     WL_TRK(1);
     // ---- level 1: the bin b1 of the indexer's histogram holding the k-th key ----
-    uint32_t b1, above1;
+    uint32_t b1, above1, bcount;
     {
         const uint32_t c8[8] = {hx.x, hx.y, hx.z, hx.w, hy.x, hy.y, hy.z, hy.w};
-        block_find_from_top<8>(c8, (uint32_t)kk, scan_sh, &b1, &above1);
+        block_find_from_top<8>(c8, (uint32_t)kk, scan_sh, &b1, &above1, &bcount);
     }
     uint32_t u[PER];
 #pragma unroll
@@ -659,6 +678,116 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     }
     mabove &= valid;
     mcand &= valid;
+    cluster_wait();
+    if (bcount <= (uint32_t)TOPKC_GCAP) {  // uniform: the row's histogram
+        // ---- the crossing bin's keys gathered into CTA 0, one slot range per warp ----
+        const int lane = tid & 31, warp = tid >> 5;
+        const uint32_t nc = __popc(mcand);
+        uint32_t incl = nc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint32_t wtot = __shfl_sync(0xffffffffu, incl, 31);
+        const uint32_t na = __reduce_add_sync(0xffffffffu, (uint32_t)__popc(mabove));
+        uint32_t wbase = 0;
+        if (lane == 0) {
+            if (wtot) wbase = dsmem_atom_add(dsmem_addr(&gctl[0], 0), wtot);
+            if (na) dsmem_atom_add(dsmem_addr(&gctl[1 + rank], 0), na);
+        }
+        uint32_t slot = __shfl_sync(0xffffffffu, wbase, 0) + incl - nc;
+        const uint32_t gc0 = dsmem_addr(gcand, 0);
+        for (uint32_t m = mcand; m; m &= m - 1, ++slot) {
+            const int j = __ffs(m) - 1;
+            if (slot < (uint32_t)TOPKC_GCAP) dsmem_st_v2(gc0 + slot * 8u, u[j], (uint32_t)(i0 + j));
+        }
+        WL_TRK(3);
+        cluster_sync_all();  // the candidates and counts are in CTA 0
+        WL_TRK(4);
+        if (rank == 0) {
+            // ---- levels 2, 3 (10 + 9 bits) over the gathered keys ----
+            const uint32_t n = min(gctl[0], (uint32_t)TOPKC_GCAP);
+            uint32_t prefix = b1 << (32 - HBITS), mask_hi = ~0u << (32 - HBITS), remaining = (uint32_t)kk - above1;
+#pragma unroll 1
+            for (int pass = 0; pass < 2; ++pass) {
+                const int shift = pass == 0 ? 9 : 0;
+                const uint32_t nb = pass == 0 ? 1024u : 512u;
+                uint32_t* h = hloc[pass];
+                for (uint32_t i = tid; i < n; i += TOPKC_THREADS) {
+                    const uint32_t x = gcand[i].x;
+                    if ((x & mask_hi) == prefix) atomicAdd(&h[(x >> shift) & (nb - 1)], 1u);
+                }
+                __syncthreads();
+                uint32_t c1[1] = {tid < (int)nb ? h[tid] : 0u};
+                uint32_t b, above;
+                block_find_from_top<1>(c1, remaining, scan_sh, &b, &above);
+                prefix |= b << shift;
+                mask_hi |= (nb - 1) << shift;
+                remaining -= above;
+            }
+            const uint32_t thr = prefix;
+            // per source CTA: its candidates > thr and == thr
+            for (uint32_t b0 = (uint32_t)warp * 32u; b0 < n; b0 += TOPKC_THREADS) {
+                const uint32_t i = b0 + lane;
+                const uint2 g = i < n ? gcand[i] : make_uint2(0u, 0u);
+                const uint32_t src = g.y / (uint32_t)(TOPKC_THREADS * PER);
+                const bool gt = i < n && g.x > thr, eq = i < n && g.x == thr;
+#pragma unroll
+                for (int c = 0; c < TOPKC_CL; ++c) {
+                    const uint32_t bg = __ballot_sync(0xffffffffu, gt && src == (uint32_t)c);
+                    const uint32_t be = __ballot_sync(0xffffffffu, eq && src == (uint32_t)c);
+                    if (lane == 0 && bg) atomicAdd(&gctl[1 + TOPKC_CL + c], (uint32_t)__popc(bg));
+                    if (lane == 0 && be) atomicAdd(&gctl[1 + 2 * TOPKC_CL + c], (uint32_t)__popc(be));
+                }
+            }
+            __syncthreads();
+            if (tid < TOPKC_CL) {
+                uint32_t gb = 0, eb = 0;
+                for (int c = 0; c < tid; ++c) {
+                    gb += gctl[1 + c] + gctl[1 + TOPKC_CL + c];
+                    eb += gctl[1 + 2 * TOPKC_CL + c];
+                }
+                dsmem_st_v4(dsmem_addr(res, (uint32_t)tid), thr, remaining, gb, eb);
+            }
+        }
+        WL_TRK(5);
+        cluster_sync_all();  // every CTA's thr, need and output bases written; no remote access after this
+        WL_TRK(6);
+        const uint32_t thr = res[0], need = res[1];
+        uint32_t mgt = mabove, meq = 0;
+        for (uint32_t m = mcand; m; m &= m - 1) {
+            const int j = __ffs(m) - 1;
+            const uint32_t x = u[j];
+            mgt |= (x > thr ? 1u : 0u) << j;
+            meq |= (x == thr ? 1u : 0u) << j;
+        }
+        uint32_t total;
+        const uint32_t ex =
+            block_excl_scan(((uint32_t)__popc(meq) << 16) | (uint32_t)__popc(mgt), scan_sh, &total);
+        uint32_t gt_b = res[2] + (ex & 0xffffu), eq_b = res[3] + (ex >> 16);
+        for (uint32_t m = mgt | meq; m; m &= m - 1) {
+            const int j = __ffs(m) - 1;
+            int pos = -1;
+            if ((mgt >> j) & 1u) {
+                pos = (int)(gt_b + min(eq_b, need));
+                ++gt_b;
+            } else {
+                if (eq_b < need) pos = (int)(gt_b + eq_b);
+                ++eq_b;
+            }
+            if (pos >= 0) {
+                out[pos] = i0 + j;
+                if (co.score) {
+                    co.score[(long long)r * co.stride + pos] = key_to_float(u[j]);
+                    co.gidx[(long long)r * co.stride + pos] = (int)(co.base + i0 + j);
+                }
+            }
+        }
+        WL_TRK(12);
+        WL_KT_END(1);
+        return;
+    }
     // ---- levels 2, 3 over the cluster: bin `tid` of each pass summed over the CTAs ----
     uint32_t prefix = b1 << (32 - HBITS), mask_hi = ~0u << (32 - HBITS), remaining = (uint32_t)kk - above1;
 #pragma unroll 1
