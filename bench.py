@@ -256,9 +256,10 @@ def main():
         def step(i=0):
             _lib.check(L.wl_attn_decode_sharded(C.byref(cfg), C.byref(io), C.byref(shard), comm.h, ws.data_ptr(),
                                                 nbytes, torch.cuda.current_stream().cuda_stream))
-        # indexer, top-k, global top-k, attention, local merge, final merge
-        # (+ two put kernels with the peer exchange; NCCL's own kernels otherwise)
-        launches_per_step = 8 if comm.p2p else 6
+        # histogram zeroing, indexer, top-k, global top-k, attention, local merge,
+        # final merge (+ two put kernels with the peer exchange; NCCL's own
+        # kernels otherwise)
+        launches_per_step = 9 if comm.p2p else 7
     else:
         nbytes = L.wl_attn_workspace_bytes(C.byref(cfg), T, B)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -266,7 +267,7 @@ def main():
         def step(i=0):
             _lib.check(L.wl_attn_decode(C.byref(cfg), C.byref(io), ws.data_ptr(), nbytes,
                                         torch.cuda.current_stream().cuda_stream))
-        launches_per_step = 4
+        launches_per_step = 5  # histogram zeroing, indexer, top-k, attention, merge
 
     for _ in range(max(args.warmup, 3)):
         step()

@@ -501,6 +501,16 @@ __global__ void __launch_bounds__(TOPKM_THREADS) topk_emit_kernel(TopkMParams p)
                                 p.cnt_eq[(long long)r * p.n_chunks + c], 0xFFFFFFFFu, out, scan_sh);
 }
 
+// Zeroes the fused histograms before the indexer adds to them. A kernel rather
+// than a memset node so that the launch chain stays programmatic: the
+// indexer's setup overlaps this kernel, this kernel overlaps the launch of the
+// previous kernel's tail.
+__global__ void __launch_bounds__(256) hist_zero_kernel(unsigned* h, long long n) {
+    pdl_wait();
+    pdl_trigger();
+    for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n; i += (long long)gridDim.x * 256) h[i] = 0u;
+}
+
 // ---- cluster top-k for decode rows ----------------------------------------------------
 // One thread-block cluster of TOPKC_CL CTAs per row; CTA `rank` holds the
 // scores [rank * 1024 * PER, (rank + 1) * 1024 * PER) of the row in registers

@@ -175,6 +175,13 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Zeroes n_rows fused top-k histograms (HB + 1 words each) in the launch chain.
+cudaError_t hist_zero(unsigned* hist, int32_t n_rows, cudaStream_t st) {
+    const long long n = (long long)n_rows * (wl::HB + 1);
+    const int blocks = (int)std::min<long long>(148, (n + 2047) / 2048);
+    return launch_pdl(wl::hist_zero_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, st, hist, n);
+}
+
 // The absorbed queries [n_rows][64][576] bf16 as a 2D tensor {576, 64 n_rows},
 // 64 x 64 boxes, 128B swizzle (the prefill attention's query tiles).
 int encode_q_map(CUtensorMap* tm, const void* q_abs, int32_t n_rows) {
@@ -395,7 +402,7 @@ int launch_topk(const float* index, int64_t index_stride, const wl_rows* rows, i
         p.cnt_eq = ws->cnt_eq;
         p.thr = ws->thr;
         if (!hist_ready) {
-            WL_CUDA_TRY(cudaMemsetAsync(ws->hist, 0, (size_t)rows->n_rows * (wl::HB + 1) * 4, st));
+            WL_CUDA_TRY(hist_zero(ws->hist, rows->n_rows, st));
             topk_hist_kernel<<<dim3((unsigned)ceil_div(lmax, 8192), rows->n_rows), 256, 0, st>>>(
                 index, index_stride, rows->len0, rows->len_step, rows->rows_per_seq, T, ws->hist);
             WL_CUDA_TRY(cudaGetLastError());
@@ -972,7 +979,7 @@ static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, co
         float* index = io->index_out ? io->index_out : w.index;
         const int64_t istride = io->index_out ? io->index_stride : T;
         const bool fuse = topk_wants_hist(T, cfg->index_topk);
-        if (fuse) WL_CUDA_TRY(cudaMemsetAsync(w.topk.hist, 0, (size_t)B * (wl::HB + 1) * 4, st));
+        if (fuse) WL_CUDA_TRY(hist_zero(w.topk.hist, B, st));
         if (int e = launch_indexer(cfg, &io->index, T, &rows, io->q_idx, io->w_idx, index, istride, st,
                                    fuse ? w.topk.hist : nullptr))
             return e;
@@ -1232,7 +1239,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         const wl_rows lrows{B, 1, T, 0};
         float* index = w.index;
         const bool fuse = topk_wants_hist(T, k);
-        if (fuse) WL_CUDA_TRY(cudaMemsetAsync(w.topk.hist, 0, (size_t)B * (wl::HB + 1) * 4, st));
+        if (fuse) WL_CUDA_TRY(hist_zero(w.topk.hist, B, st));
         if (int e = launch_indexer(cfg, &io->index, T, &lrows, io->q_idx, io->w_idx, index, T, st,
                                    fuse ? w.topk.hist : nullptr))
             return e;
