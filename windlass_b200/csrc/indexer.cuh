@@ -81,7 +81,7 @@ template <int R>
 struct IdxStream {
     static_assert(R == 1 || R == 2 || R == 4, "N = 64 R <= 256");
     static constexpr int NACC = R == 1 ? 4 : 2;            // accumulator sets in flight
-    static constexpr int EPI_GROUPS = 2;                   // epilogue groups of 4 warps, alternating tiles
+    static constexpr int EPI_GROUPS = R == 1 ? 4 : 2;      // epilogue groups of 4 warps, alternating tiles
     // Each accumulator set must always be drained by the same group (tiles a,
     // a + NACC, ...), or a group could wait on a set's next phase while its
     // current one is still open (a parity wait two phases ahead passes at once).
