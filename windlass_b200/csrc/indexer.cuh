@@ -43,8 +43,8 @@ __device__ __forceinline__ int rows_len(int r, int rows_per_seq, int len0, int l
 // ---- warp-specialised, fp8 tensor cores ------------------------------------------------
 // A CTA streams a contiguous range of 128-key tiles of one cache for R query
 // rows (decode: one row, one CTA per SM across all rows; prefill: groups of 4
-// consecutive rows, one CTA per group). Roles (10 warps), connected by
-// mbarriers only:
+// consecutive rows, one CTA per group). Roles (18 warps at decode, 10 at
+// prefill), connected by mbarriers only:
 //   warp 0      TMA producer: the rows' bf16 queries (bulk copy during setup),
 //               then each tile's fp8 keys as one 128 x 128-byte box with 128B
 //               swizzle (a tensor-map load; rows past the cache end read as
@@ -52,9 +52,10 @@ __device__ __forceinline__ int rows_len(int r, int rows_per_seq, int len0, int l
 //   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4 straight on the fp8 keys
 //               (M = 128 keys, K = 32 per instruction), one chain of 4 per
 //               tile: N = 64 R = each row's hi and lo e4m3 query terms
-//   warps 2-9   epilogue:     tcgen05.ld both halves for one (key, row), combine,
+//   warps 2..   epilogue:     tcgen05.ld both halves for one (key, row), combine,
 //               scale, relu, head-weighted sum, store (+ fused top-k histogram
-//               at decode); two groups of 4 warps take alternate tiles
+//               at decode); groups of 4 warps (four groups at decode, two at
+//               prefill) take the tiles in turn
 //
 // The query in e4m3: per head, q * s_h (s_h a power of two putting the head's
 // largest element in [128, 256)) = hi + lo / 32 with hi = e4m3(q s_h) and
