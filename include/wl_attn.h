@@ -302,6 +302,41 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io,
  * (different streams, or different host threads) race and must not. */
 int wl_attn_decode_noalloc(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, void* stream);
 
+/* ---- the cache write path ---------------------------------------------------
+ * Appends n tokens to the caches: for token i at row pos[i] of sequence seq[i]
+ * (seq NULL: sequence 0), given the projections' outputs,
+ *  - index key (owner layers; skipped when k_raw is NULL): LayerNorm of
+ *    wk(x) with weight/bias (eps ln_eps), RoPE on its leading rope_dim dims,
+ *    rounded to bf16 (the value the reference caches), then stored as
+ *    fp8-e4m3 with the per-key scale amax / 448 into `index`;
+ *  - latent row (skipped when kv_raw is NULL): the first kv_lora of
+ *    kv_a_proj_with_mqa(x) RMS-normalised with the kv_a_layernorm weight (eps
+ *    rms_eps), the trailing rope_dim roped, both stored as bf16 into `latent`.
+ * RoPE is the interleaved-in, halves-out form with the token's table row
+ * cos/sin [n][rope_dim/2] (the caller's table, as in the reference).
+ * Replaces launch_indexer_key (glm_kernels.cuh:432-448) and the latent row
+ * write of run_attention (glm_layer_runner.cuh:544-570). Rows outside
+ * [0, cfg->T_max) set the device error word and are skipped. The caches'
+ * pointers are written through (their `const` is the readers' view). */
+typedef struct wl_cache_append_io {
+    int32_t n;                  /* tokens                                      */
+    const int32_t* pos;         /* device [n]: cache row of each token         */
+    const int32_t* seq;         /* device [n] or NULL: sequence of each token  */
+    const float* cos;           /* device fp32 [n, rope_dim/2]                 */
+    const float* sin;           /* device fp32 [n, rope_dim/2]                 */
+    const float* k_raw;         /* device fp32 [n, idx_dim]: wk(x), or NULL    */
+    const void*  k_norm_w;      /* device bf16 [idx_dim] LayerNorm weight      */
+    const void*  k_norm_b;      /* device bf16 [idx_dim] LayerNorm bias        */
+    float        ln_eps;        /* 1e-6 (INDEXER_LN_EPS)                       */
+    wl_index_cache index;
+    const float* kv_raw;        /* device fp32 [n, kv_lora + rope_dim], or NULL */
+    const void*  kv_norm_w;     /* device bf16 [kv_lora] kv_a_layernorm weight */
+    float        rms_eps;       /* 1e-6 (LORA_NORM_EPS)                        */
+    wl_latent_cache latent;
+} wl_cache_append_io;
+
+int wl_cache_append(const wl_attn_cfg* cfg, const wl_cache_append_io* io, void* stream);
+
 /* ---- diagnostics ------------------------------------------------------------ */
 /* Device-side error word of the calling thread's current device: bounds-check
  * failures and bounded-wait timeouts of any kernel of this library set it.
@@ -311,7 +346,7 @@ int wl_device_error(int32_t clear, uint32_t* detail);
 
 /* sizeof of each public struct, for binding checks: fills up to n entries in
  * the order cfg, latent_cache, index_cache, rows, index_share, decode_io,
- * prefill_io, shard; returns how many exist. */
+ * prefill_io, shard, cache_append_io; returns how many exist. */
 int32_t wl_struct_sizes(int64_t* out, int32_t n);
 int32_t wl_abi_version(void);
 

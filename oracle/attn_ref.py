@@ -18,6 +18,11 @@ function citing the reference it follows (paths inside ssubbotin/windlass):
                    attn_block's s = q.K, drop -> -inf, softmax, p.V,
                    tools/ref_glm_chain.py:616-638)
   lse_merge        the standard (o, lse) combination of disjoint key sets
+  cache_append     the cache write path: indexer_keys (ref_glm_chain.py:
+                   465-480; launch_indexer_key, src/glm_kernels.cuh:432-448)
+                   and the latent row of attn_block (rms_norm + rope_interleave,
+                   ref_glm_chain.py:63-106, 576-581; glm_layer_runner.cuh:
+                   544-570), in the kernel's fixed summation order
   quantize_e4m3    BASELINE's fp8 index-key format (not in the reference):
                    e4m3 (OCP "fn", round-to-nearest-even) with one fp32 scale
                    per key = amax / 448.
@@ -221,6 +226,69 @@ def sharded_decode(inp: dict, k: int, nranks: int):
         ls_.append(l)
     ctx, lse = lse_merge(os_, ls_)
     return dict(sel=glob, ctx=ctx, lse=lse)
+
+
+# ---- the cache write path ------------------------------------------------------------------
+
+def _lane_tree(p: np.ndarray) -> np.ndarray:
+    """Sum of 32 per-lane fp32 partials [..., 32] in a warp's tree order:
+    lanes l < o add lane l + o for o = 16, 8, 4, 2, 1; lane 0 holds the sum."""
+    p = np.array(p, dtype=np.float32, copy=True)
+    for o in (16, 8, 4, 2, 1):
+        p[..., :o] = p[..., :o] + p[..., o:2 * o]
+    return p[..., 0]
+
+
+def _rope_halves(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    a, b = x[..., 0::2], x[..., 1::2]
+    return np.concatenate([a * cos - b * sin, b * cos + a * sin], axis=-1).astype(np.float32)
+
+
+def cache_append(k_raw, k_norm_w, k_norm_b, kv_raw, kv_norm_w, cos, sin, ln_eps=1e-6, rms_eps=1e-6) -> dict:
+    """The cache rows of n tokens from the projections' outputs.
+
+    Index key (indexer_keys, ref_glm_chain.py:465-480; glm_kernels.cuh:255-285):
+    LayerNorm of k_raw [n, 128] (biased variance, eps ln_eps) with weight and
+    bias, RoPE (interleaved in, halves out) on the leading 64 dims, rounded to
+    bf16, then quantize_e4m3. Latent row (attn_block, ref_glm_chain.py:576-581
+    and 596): rms_norm of kv_raw[:, :512] with the weight (eps rms_eps), RoPE
+    of kv_raw[:, 512:], both rounded to bf16. cos/sin [n, 32] fp32.
+
+    The formulas are the reference's; the order of the fp32 sums and of the
+    roundings is the kernel's (lane l of a warp sums its elements in order,
+    then the lanes combine as in _lane_tree; x - mean, then * inv, then * w,
+    then + b), so the result matches the kernel to the bit. The reference's own
+    order differs only within fp32 rounding (checked against its outputs in
+    tests/test_oracle.py)."""
+    f = np.float32
+    cos, sin = np.asarray(cos, f), np.asarray(sin, f)
+    out = {}
+    k = np.asarray(k_raw, f)
+    n = k.shape[0]
+    ks = k.reshape(n, 32, 4)
+    mean = _lane_tree(((ks[..., 0] + ks[..., 1]) + ks[..., 2]) + ks[..., 3]) / f(128)
+    d = (k - mean[:, None]).astype(f)
+    dd = (d * d).reshape(n, 32, 4)
+    var = _lane_tree(((dd[..., 0] + dd[..., 1]) + dd[..., 2]) + dd[..., 3]) / f(128)
+    inv = (f(1) / np.sqrt((var + f(ln_eps)).astype(f))).astype(f)
+    y = ((d * inv[:, None]) * np.asarray(k_norm_w, f) + np.asarray(k_norm_b, f)).astype(f)
+    key = np.concatenate([_rope_halves(y[:, :64], cos, sin), y[:, 64:]], axis=-1)
+    out["key_f32"] = key
+    out["key_bf16"] = bf16_round(key)
+    out["idx_bits"], out["idx_scale"] = quantize_e4m3(out["key_bf16"])
+    x = np.asarray(kv_raw, f)
+    c = x[:, :512].reshape(n, 4, 32, 4)  # element j*128 + 4l + e
+    acc = np.zeros((n, 32), f)
+    for j in range(4):
+        for e in range(4):
+            acc = (acc + c[:, j, :, e] * c[:, j, :, e]).astype(f)
+    ms = _lane_tree(acc) / f(512)
+    inv = (f(1) / np.sqrt((ms + f(rms_eps)).astype(f))).astype(f)
+    out["c_kv_f32"] = ((x[:, :512] * inv[:, None]) * np.asarray(kv_norm_w, f)).astype(f)
+    out["c_kv"] = bf16_round(out["c_kv_f32"])
+    out["k_rot_f32"] = _rope_halves(x[:, 512:576], cos, sin)
+    out["k_rot"] = bf16_round(out["k_rot_f32"])
+    return out
 
 
 # ---- seeded inputs (BASELINE configs) ------------------------------------------------------------

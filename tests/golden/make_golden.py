@@ -11,6 +11,12 @@ Writes two files next to this script:
                    seed 20260801, T=1024, index_topk=512, scale 1.0):
                    ref_q [32*128] fp32, ref_k_bf16 [1024,128] uint16,
                    ref_w [32], ref_index [1024], ref_topk [512].
+  cache_ref.npz    the cache write path at GLM-5.2's dimensions: the
+                   reference's indexer_keys (wk -> LayerNorm -> RoPE on the
+                   leading 64) and the latent row of attn_block (rms_norm of
+                   the first 512 of kv_a_proj_with_mqa, RoPE of the trailing
+                   64) for 16 tokens at scattered positions, with the
+                   projections' outputs the kernel takes as inputs.
   chain_ref.npz    tools/ref_glm_chain.attn_block (the direct, non-absorbed
                    MLA form with the DSA indexer and IndexShare) run over
                    positions 0..T-1 of a two-layer group (layer 0 "full",
@@ -104,14 +110,46 @@ def chain_fixture(ref: str) -> dict:
     return out
 
 
+def cache_fixture(ref: str) -> dict:
+    sys.path.insert(0, os.path.join(ref, "tools"))
+    import ref_glm_chain as R  # noqa: E402
+
+    from oracle.attn_ref import bf16_round  # noqa: E402
+
+    n, HID = 16, 64
+    rng = np.random.default_rng(20260805)
+    f32 = lambda *s, sd=1.0: (rng.standard_normal(s) * sd).astype(np.float32)  # noqa: E731
+    W = dict(ix_wk=f32(128, HID, sd=0.15), ix_k_norm_w=bf16_round(1 + f32(128, sd=0.1)),
+             ix_k_norm_b=bf16_round(f32(128, sd=0.05)), kv_a_proj_with_mqa=f32(576, HID, sd=0.15),
+             kv_a_layernorm=bf16_round(1 + f32(512, sd=0.1)))
+    cfg = dict(qk_rope=64)
+    pos = np.array([0, 1, 2, 3, 17, 100, 511, 1000, 2047, 4095, 8191, 12345, 40000, 65535, 100000, 131071])
+    cos, sin = R.rope_tables(131072, 64, 1e6)
+    x = f32(n, HID)
+    ckv = x @ W["kv_a_proj_with_mqa"].T
+    return dict(pos=pos.astype(np.int32), cos=cos[pos], sin=sin[pos],
+                k_raw=(x.astype(np.float32) @ W["ix_wk"].T).astype(np.float32), kv_raw=ckv.astype(np.float32),
+                k_norm_w=W["ix_k_norm_w"], k_norm_b=W["ix_k_norm_b"], kv_norm_w=W["kv_a_layernorm"],
+                ref_key=R.indexer_keys(x, W, cfg, pos, cos, sin).astype(np.float32),
+                ref_kc=R.rms_norm(ckv[:, :512], W["kv_a_layernorm"], R.LORA_NORM_EPS).astype(np.float32),
+                ref_krot=R.rope_interleave(ckv[:, 512:], cos[pos], sin[pos]).astype(np.float32))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("WINDLASS_REF", ""), help="reference checkout")
+    ap.add_argument("--which", default="indexer,chain,cache", help="fixtures to write (comma-separated)")
     a = ap.parse_args()
     if not a.ref or not os.path.isdir(os.path.join(a.ref, "tools")):
         raise SystemExit("pass --ref <path to the reference checkout>")
-    np.savez_compressed(os.path.join(HERE, "indexer_ref.npz"), **indexer_fixture(a.ref))
-    np.savez_compressed(os.path.join(HERE, "chain_ref.npz"), **chain_fixture(a.ref))
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))  # the repository root, for oracle/
+    which = set(a.which.split(","))
+    if "indexer" in which:
+        np.savez_compressed(os.path.join(HERE, "indexer_ref.npz"), **indexer_fixture(a.ref))
+    if "chain" in which:
+        np.savez_compressed(os.path.join(HERE, "chain_ref.npz"), **chain_fixture(a.ref))
+    if "cache" in which:
+        np.savez_compressed(os.path.join(HERE, "cache_ref.npz"), **cache_fixture(a.ref))
     print("wrote", HERE)
 
 

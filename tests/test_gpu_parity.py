@@ -488,3 +488,90 @@ def test_topk_cluster_crossing_bin_at_gather_capacity(n_cross):
     x[pos[:1500]] = 10.0 + rng.uniform(0, 1, 1500).astype(np.float32)  # above the crossing bin
     x[pos[1500:1500 + n_cross]] = rng.uniform(1.0, 1.0625, n_cross).astype(np.float32)  # one 13-bit bin
     _topk_case(x, 2048)
+
+
+# ---- the cache write path (wl_cache_append) vs the oracle: bit-exact -----------------------
+
+def _append_case(n, T_max, pos, seq=None, n_seq=1, seed=0, golden=None):
+    """Random (or golden) projections for n tokens -> wl_cache_append into
+    sentinel-filled caches; returns (caches as numpy, oracle rows)."""
+    rng = np.random.default_rng(seed)
+    if golden is not None:
+        g = golden
+        k_raw, kv_raw, cs, sn = g["k_raw"], g["kv_raw"], g["cos"], g["sin"]
+        kw, kb, kvw = g["k_norm_w"], g["k_norm_b"], g["kv_norm_w"]
+    else:
+        k_raw = (rng.standard_normal((n, 128)) * 2 + 0.3).astype(np.float32)
+        kv_raw = rng.standard_normal((n, 576)).astype(np.float32) * 1.7
+        ang = rng.uniform(0, 2 * np.pi, (n, 32))
+        cs, sn = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+        kw = o.bf16_round(1 + 0.1 * rng.standard_normal(128).astype(np.float32))
+        kb = o.bf16_round(0.05 * rng.standard_normal(128).astype(np.float32))
+        kvw = o.bf16_round(1 + 0.1 * rng.standard_normal(512).astype(np.float32))
+    keys = A.IndexKeys(torch.full((n_seq, T_max, 128), 0x5A, dtype=torch.uint8, device="cuda"),
+                       torch.full((n_seq, T_max), -7.0, dtype=torch.float32, device="cuda"))
+    packed = torch.full((n_seq, T_max, 576), 3.0, dtype=torch.bfloat16, device="cuda")
+    kv = A.LatentKV.packed(packed)
+    A.cache_append(A.glm52_cfg(T_max), dev(pos, torch.int32), dev(cs, torch.float32), dev(sn, torch.float32),
+                   keys=keys, k_raw=dev(k_raw, torch.float32), k_norm_w=dev(kw, torch.bfloat16),
+                   k_norm_b=dev(kb, torch.bfloat16), kv=kv, kv_raw=dev(kv_raw, torch.float32),
+                   kv_norm_w=dev(kvw, torch.bfloat16), seq=None if seq is None else dev(seq, torch.int32))
+    torch.cuda.synchronize()
+    ref = o.cache_append(k_raw, kw, kb, kv_raw, kvw, cs, sn)
+    return (cpu(keys.keys), cpu(keys.scale), cpu(packed.float())), ref
+
+
+def _check_append(got, ref, pos, seq, n_seq, T_max):
+    kbits, kscale, lat = got
+    seq = np.zeros(len(pos), np.int64) if seq is None else np.asarray(seq)
+    assert np.array_equal(kbits[seq, pos], ref["idx_bits"]), "index key bits"
+    assert np.array_equal(kscale[seq, pos], ref["idx_scale"]), "index key scales"
+    assert np.array_equal(lat[seq, pos, :512], ref["c_kv"]), "c_kv rows"
+    assert np.array_equal(lat[seq, pos, 512:], ref["k_rot"]), "k_rot rows"
+    untouched = np.ones((n_seq, T_max), bool)
+    untouched[seq, pos] = False
+    assert np.all(kbits[untouched] == 0x5A) and np.all(kscale[untouched] == -7.0)
+    assert np.all(lat[untouched] == 3.0), "rows other than the appended ones changed"
+
+
+def test_cache_append_golden_positions():
+    """The reference fixture's 16 tokens (scattered positions up to 131071)."""
+    import os
+    g = dict(np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "cache_ref.npz")))
+    pos = g["pos"]
+    got, ref = _append_case(len(pos), 131072, pos, golden=g)
+    _check_append(got, ref, pos, None, 1, 131072)
+    # and the fixture's reference rows themselves, in the stored formats
+    assert np.array_equal(got[0][0, pos], o.quantize_e4m3(o.bf16_round(g["ref_key"]))[0])
+    assert np.array_equal(got[2][0, pos, :512], o.bf16_round(g["ref_kc"]))
+
+
+@pytest.mark.parametrize("n", [1, 5, 4096])
+def test_cache_append_prefill_chunk(n):
+    """A prefill chunk: n consecutive positions after a prefix."""
+    T_max = 8192
+    pos = np.arange(T_max - n - 3, T_max - 3)
+    got, ref = _append_case(n, T_max, pos, seed=n)
+    _check_append(got, ref, pos, None, 1, T_max)
+
+
+def test_cache_append_decode_batch_of_sequences():
+    """Decode: one token for each of 8 sequences, each at its own position."""
+    T_max, B = 4096, 8
+    pos = np.array([0, 4095, 17, 2048, 1, 3000, 77, 4094])
+    seq = np.arange(B)
+    got, ref = _append_case(B, T_max, pos, seq=seq, n_seq=B, seed=3)
+    _check_append(got, ref, pos, seq, B, T_max)
+
+
+def test_cache_append_row_out_of_range_sets_error_and_skips():
+    T_max = 256
+    pos = np.array([3, 256, 7])  # 256 is outside the cache
+    got, ref = _append_case(3, T_max, pos, seed=9)
+    st, word = A.device_error(clear=True)
+    assert st == _lib.WL_ERR_DEVICE
+    ok = np.array([0, 2])
+    kbits, kscale, lat = got
+    assert np.array_equal(kbits[0, pos[ok]], ref["idx_bits"][ok])
+    assert np.array_equal(lat[0, pos[ok], :512], ref["c_kv"][ok])
+    assert np.all(kbits[0, 255] == 0x5A) and np.all(lat[0, 255] == 3.0)

@@ -114,6 +114,33 @@ def test_shared_layer_consumes_owner_selection(ch):
     assert rel(ch["l1_attn_out"][pos], _absorbed_attn_out(ch, 1, pos, sel, drop_mask=False)) > 1e-3
 
 
+# ---- pin 3: the cache write path (indexer_keys and attn_block's latent row) ----
+
+def test_cache_append_matches_reference_fixture():
+    """The restatement (fixed fp32 summation order) against the reference's
+    numpy at GLM-5.2's dimensions: fp32 rows within fp32 rounding, the RoPE
+    part exact, and every stored bf16 / e4m3 value and scale identical to the
+    same format applied to the reference's rows."""
+    g = dict(np.load(os.path.join(GOLD, "cache_ref.npz")))
+    r = o.cache_append(g["k_raw"], g["k_norm_w"], g["k_norm_b"], g["kv_raw"], g["kv_norm_w"], g["cos"], g["sin"])
+    assert rel(g["ref_key"], r["key_f32"]) <= 1e-6
+    assert rel(g["ref_kc"], r["c_kv_f32"]) <= 1e-6
+    assert np.array_equal(g["ref_krot"], r["k_rot_f32"])
+    bits, scale = o.quantize_e4m3(o.bf16_round(g["ref_key"]))
+    assert np.array_equal(bits, r["idx_bits"]) and np.array_equal(scale, r["idx_scale"])
+    assert np.array_equal(o.bf16_round(g["ref_kc"]), r["c_kv"])
+    assert np.array_equal(o.bf16_round(g["ref_krot"]), r["k_rot"])
+
+
+def test_cache_append_negative_control_layernorm_bias():
+    """Dropping the LayerNorm bias (reusing an RMSNorm-like form for the
+    indexer key) is visible at the fixture's tolerance."""
+    g = dict(np.load(os.path.join(GOLD, "cache_ref.npz")))
+    r = o.cache_append(g["k_raw"], g["k_norm_w"], np.zeros_like(g["k_norm_b"]), g["kv_raw"], g["kv_norm_w"],
+                       g["cos"], g["sin"])
+    assert rel(g["ref_key"], r["key_f32"]) > 1e-3
+
+
 # ---- properties ----------------------------------------------------------------------
 
 def test_e4m3_quantisation_roundtrip():

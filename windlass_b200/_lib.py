@@ -68,7 +68,13 @@ class Shard(C.Structure):
     _fields_ = [("t0", i64), ("T_global", i64)]
 
 
-STRUCTS = [AttnCfg, LatentCache, IndexCache, Rows, IndexShareC, DecodeIO, PrefillIO, Shard]
+class CacheAppendIO(C.Structure):
+    _fields_ = [("n", i32), ("pos", vp), ("seq", vp), ("cos", vp), ("sin", vp), ("k_raw", vp),
+                ("k_norm_w", vp), ("k_norm_b", vp), ("ln_eps", f32), ("index", IndexCache),
+                ("kv_raw", vp), ("kv_norm_w", vp), ("rms_eps", f32), ("latent", LatentCache)]
+
+
+STRUCTS = [AttnCfg, LatentCache, IndexCache, Rows, IndexShareC, DecodeIO, PrefillIO, Shard, CacheAppendIO]
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -103,6 +109,7 @@ SIGNATURES = {
                                          C.POINTER(Shard), vp, vp, C.c_size_t, vp]),
     "wl_device_error": (C.c_int, [i32, C.POINTER(u32)]),
     "wl_attn_decode_noalloc": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(DecodeIO), vp]),
+    "wl_cache_append": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(CacheAppendIO), vp]),
 }
 
 _lib = None

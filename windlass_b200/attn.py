@@ -182,6 +182,56 @@ def lse_merge(o_part: torch.Tensor, lse_part: torch.Tensor):
     return ctx, lse
 
 
+# ---- the cache write path ---------------------------------------------------------------------
+
+def cache_append(cfg: AttnCfg, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *,
+                 keys: IndexKeys | None = None, k_raw: torch.Tensor | None = None,
+                 k_norm_w: torch.Tensor | None = None, k_norm_b: torch.Tensor | None = None,
+                 ln_eps: float = 1e-6, kv: LatentKV | None = None, kv_raw: torch.Tensor | None = None,
+                 kv_norm_w: torch.Tensor | None = None, rms_eps: float = 1e-6,
+                 seq: torch.Tensor | None = None) -> None:
+    """Write n tokens into the caches (``wl_cache_append``): the reference's
+    ``launch_indexer_key`` (src/glm_kernels.cuh:432-448; numpy
+    ``indexer_keys``, tools/ref_glm_chain.py:465-480) into ``keys`` from
+    ``k_raw`` = wk(x) [n, 128] fp32, and the latent row write of
+    ``run_attention`` (src/glm_layer_runner.cuh:544-570) into ``kv`` from
+    ``kv_raw`` = kv_a_proj_with_mqa(x) [n, 576] fp32. ``pos`` [n] int32 rows,
+    ``seq`` [n] int32 sequences (None: 0), ``cos``/``sin`` [n, 32] fp32 the
+    tokens' RoPE table rows; norm weights/bias bf16."""
+    _need(pos, torch.int32, "pos")
+    _need(cos, torch.float32, "cos")
+    _need(sin, torch.float32, "sin")
+    n = pos.numel()
+    io = _lib.CacheAppendIO()
+    io.n = n
+    hold = [pos.contiguous(), cos.contiguous(), sin.contiguous()]
+    io.pos, io.cos, io.sin = (t.data_ptr() for t in hold)
+    if seq is not None:
+        _need(seq, torch.int32, "seq")
+        hold.append(seq.contiguous())
+        io.seq = hold[-1].data_ptr()
+    if k_raw is not None:
+        if keys is None or k_norm_w is None or k_norm_b is None:
+            raise ValueError("k_raw needs keys, k_norm_w and k_norm_b")
+        _need(k_raw, torch.float32, "k_raw")
+        _need(k_norm_w, torch.bfloat16, "k_norm_w")
+        _need(k_norm_b, torch.bfloat16, "k_norm_b")
+        hold += [k_raw.contiguous(), k_norm_w.contiguous(), k_norm_b.contiguous()]
+        io.k_raw, io.k_norm_w, io.k_norm_b = (t.data_ptr() for t in hold[-3:])
+        io.ln_eps = ln_eps
+        io.index = keys.c()
+    if kv_raw is not None:
+        if kv is None or kv_norm_w is None:
+            raise ValueError("kv_raw needs kv and kv_norm_w")
+        _need(kv_raw, torch.float32, "kv_raw")
+        _need(kv_norm_w, torch.bfloat16, "kv_norm_w")
+        hold += [kv_raw.contiguous(), kv_norm_w.contiguous()]
+        io.kv_raw, io.kv_norm_w = (t.data_ptr() for t in hold[-2:])
+        io.rms_eps = rms_eps
+        io.latent = kv.c()
+    check(lib().wl_cache_append(C.byref(cfg), C.byref(io), _stream()), "wl_cache_append")
+
+
 # ---- the substep ----------------------------------------------------------------------------
 
 def decode_io(cfg: AttnCfg, kv: LatentKV, q_abs: torch.Tensor, *, keys: IndexKeys | None = None,

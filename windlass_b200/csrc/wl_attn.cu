@@ -20,6 +20,7 @@
 #include <nccl.h>
 
 #include "../../include/wl_attn.h"
+#include "cache_append.cuh"
 #include "indexer.cuh"
 #include "mla_attn.cuh"
 #include "mla_attn64.cuh"
@@ -837,7 +838,8 @@ int32_t wl_struct_sizes(int64_t* out, int32_t n) {
     const int64_t s[] = {(int64_t)sizeof(wl_attn_cfg),     (int64_t)sizeof(wl_latent_cache),
                          (int64_t)sizeof(wl_index_cache),  (int64_t)sizeof(wl_rows),
                          (int64_t)sizeof(wl_index_share),  (int64_t)sizeof(wl_attn_decode_io),
-                         (int64_t)sizeof(wl_attn_prefill_io), (int64_t)sizeof(wl_shard)};
+                         (int64_t)sizeof(wl_attn_prefill_io), (int64_t)sizeof(wl_shard),
+                         (int64_t)sizeof(wl_cache_append_io)};
     const int32_t m = (int32_t)(sizeof(s) / sizeof(s[0]));
     for (int32_t i = 0; i < n && i < m && out; ++i) out[i] = s[i];
     return m;
@@ -943,6 +945,61 @@ int wl_lse_merge(const float* o_part, const float* lse_part, int32_t n_rows, int
                  int32_t kv_lora, float* ctx, float* lse, void* stream) {
     return launch_merge(o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
                         lse_part_stride, n_heads, kv_lora, ctx, lse, static_cast<cudaStream_t>(stream));
+}
+
+// ---- the cache write path -------------------------------------------------------------
+int wl_cache_append(const wl_attn_cfg* cfg, const wl_cache_append_io* io, void* stream) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (!io || io->n < 0) return WL_ERR_ARG;
+    if (io->n == 0) return WL_OK;
+    if (!io->pos || !io->cos || !io->sin || (!io->k_raw && !io->kv_raw)) return WL_ERR_ARG;
+    wl::AppendParams p{};
+    p.n = io->n;
+    p.pos = io->pos;
+    p.seq = io->seq;
+    p.T_max = cfg->T_max;
+    p.cos = io->cos;
+    p.sin = io->sin;
+    if (io->k_raw) {
+        const wl_index_cache& c = io->index;
+        if (!io->k_norm_w || !io->k_norm_b || !c.keys || !c.scale || !aligned16(io->k_raw) || !aligned16(c.keys) ||
+            (c.keys_seq_stride & 15) || c.keys_seq_stride < 0 || c.scale_seq_stride < 0)
+            return WL_ERR_ARG;
+        if (io->seq && (c.keys_seq_stride < (int64_t)cfg->T_max * wl::IDX_D || c.scale_seq_stride < cfg->T_max))
+            return WL_ERR_ARG;
+        p.k_raw = io->k_raw;
+        p.k_w = static_cast<const __nv_bfloat16*>(io->k_norm_w);
+        p.k_b = static_cast<const __nv_bfloat16*>(io->k_norm_b);
+        p.ln_eps = io->ln_eps;
+        p.keys = static_cast<uint8_t*>(const_cast<void*>(c.keys));
+        p.keys_seq = c.keys_seq_stride;
+        p.scale = const_cast<float*>(c.scale);
+        p.scale_seq = c.scale_seq_stride;
+    }
+    if (io->kv_raw) {
+        const wl_latent_cache& c = io->latent;
+        if (!io->kv_norm_w || !c.c_kv || !c.k_rot || !aligned16(io->kv_raw) || !aligned16(c.c_kv) ||
+            !aligned16(c.k_rot) || (c.c_kv_row_stride & 7) || (c.k_rot_row_stride & 7) ||
+            c.c_kv_row_stride < wl::AT_DV || c.k_rot_row_stride < wl::AT_D - wl::AT_DV || (c.c_kv_seq_stride & 7) ||
+            (c.k_rot_seq_stride & 7) || c.c_kv_seq_stride < 0 || c.k_rot_seq_stride < 0)
+            return WL_ERR_ARG;
+        if (io->seq && (c.c_kv_seq_stride < (int64_t)cfg->T_max * c.c_kv_row_stride ||
+                        c.k_rot_seq_stride < (int64_t)cfg->T_max * c.k_rot_row_stride))
+            return WL_ERR_ARG;
+        p.kv_raw = io->kv_raw;
+        p.kv_w = static_cast<const __nv_bfloat16*>(io->kv_norm_w);
+        p.rms_eps = io->rms_eps;
+        p.c_kv = static_cast<__nv_bfloat16*>(const_cast<void*>(c.c_kv));
+        p.ckv_row = c.c_kv_row_stride;
+        p.ckv_seq = c.c_kv_seq_stride;
+        p.k_rot = static_cast<__nv_bfloat16*>(const_cast<void*>(c.k_rot));
+        p.krot_row = c.k_rot_row_stride;
+        p.krot_seq = c.k_rot_seq_stride;
+    }
+    const unsigned blocks = (unsigned)ceil_div(io->n, wl::CA_WARPS);
+    WL_CUDA_TRY(launch_pdl(wl::cache_append_kernel, dim3(blocks), dim3(32 * wl::CA_WARPS), 0,
+                           static_cast<cudaStream_t>(stream), p));
+    return WL_OK;
 }
 
 // ---- decode --------------------------------------------------------------------------
