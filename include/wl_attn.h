@@ -302,6 +302,27 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io,
  * (different streams, or different host threads) race and must not. */
 int wl_attn_decode_noalloc(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, void* stream);
 
+/* ---- the absorption around the attention ------------------------------------
+ * kv_b = kv_b_proj, device bf16 [n_heads * (qk_nope 192 + v_head 256), kv_lora]
+ * (per head: 192 W_UK rows, then 256 W_UV rows), 16-byte aligned.
+ *
+ * wl_mla_absorb_q: for n query rows, q fp32 [n][n_heads][256] (qk_nope 192 |
+ * roped qk_rope 64; row stride q_row_stride floats) ->
+ *   q_abs[r][h][c]       = sum_{d<192} q[r][h][d] * kv_b[h*448 + d][c]   (c < 512)
+ *   q_abs[r][h][512 + j] = q[r][h][192 + j]                              (j < 64)
+ * in bf16 (row stride q_abs_row_stride elements): the absorbed query the
+ * attention entry points read. Replaces mla_absorb_q (glm_layer_runner.cuh:
+ * 196-215) plus the q_rot half of the reference's mla_decode_absorbed input.
+ *
+ * wl_mla_project_v: ctx fp32 [n][n_heads][512] (row stride ctx_row_stride
+ * floats, a multiple of 4) -> out[r][h][v] = sum_c ctx[r][h][c] *
+ * kv_b[h*448 + 192 + v][c], fp32 [n][n_heads][256] (row stride out_row_stride).
+ * Replaces mla_project_v (glm_layer_runner.cuh:217-234). fp32 accumulation. */
+int wl_mla_absorb_q(const wl_attn_cfg* cfg, int32_t n, const float* q, int64_t q_row_stride,
+                    const void* kv_b, void* q_abs, int64_t q_abs_row_stride, void* stream);
+int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_t ctx_row_stride,
+                     const void* kv_b, float* out, int64_t out_row_stride, void* stream);
+
 /* ---- the cache write path ---------------------------------------------------
  * Appends n tokens to the caches: for token i at row pos[i] of sequence seq[i]
  * (seq NULL: sequence 0), given the projections' outputs,

@@ -17,6 +17,9 @@ function citing the reference it follows (paths inside ssubbotin/windlass):
   mla_absorbed     src/glm_layer_runner.cuh:251-298 (absorbed form of
                    attn_block's s = q.K, drop -> -inf, softmax, p.V,
                    tools/ref_glm_chain.py:616-638)
+  mla_absorb_q     src/glm_layer_runner.cuh:196-215 (q_nope through W_UK),
+                   with the roped part appended: the attention's input row
+  mla_project_v    src/glm_layer_runner.cuh:217-234 (ctx through W_UV)
   lse_merge        the standard (o, lse) combination of disjoint key sets
   cache_append     the cache write path: indexer_keys (ref_glm_chain.py:
                    465-480; launch_indexer_key, src/glm_kernels.cuh:432-448)
@@ -143,6 +146,25 @@ def mla_sparse(q_abs, c_kv, k_rot, sel, scale, dtype=np.float64):
     T = c_kv.shape[0]
     keep = canonical(sel, T)
     return mla_absorbed(q_abs, c_kv[keep], k_rot[keep], None, scale, dtype)
+
+
+def mla_absorb_q(q: np.ndarray, kv_b: np.ndarray, nope: int = 192, v_head: int = 256) -> np.ndarray:
+    """q [..., H, nope + rope] (rope part already roped), kv_b [H * (nope + v_head), L]
+    -> [..., H, L + rope]: sum_d q[h][d] kv_b[h*(nope+v_head) + d][c], then q[h][nope:]
+    (glm_layer_runner.cuh:196-215; float64)."""
+    q = np.asarray(q, np.float64)
+    H = q.shape[-2]
+    W = np.asarray(kv_b, np.float64).reshape(H, nope + v_head, -1)
+    return np.concatenate([np.einsum("...hd,hdc->...hc", q[..., :nope], W[:, :nope]), q[..., nope:]], -1)
+
+
+def mla_project_v(ctx: np.ndarray, kv_b: np.ndarray, nope: int = 192, v_head: int = 256) -> np.ndarray:
+    """ctx [..., H, L] -> [..., H, v_head]: sum_c ctx[h][c] kv_b[h*(nope+v_head) + nope + v][c]
+    (glm_layer_runner.cuh:217-234; float64)."""
+    ctx = np.asarray(ctx, np.float64)
+    H = ctx.shape[-2]
+    W = np.asarray(kv_b, np.float64).reshape(H, nope + v_head, -1)
+    return np.einsum("...hc,hvc->...hv", ctx, W[:, nope:])
 
 
 def lse_merge(os: list[np.ndarray], lses: list[np.ndarray]) -> tuple[np.ndarray, np.ndarray]:

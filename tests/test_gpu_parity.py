@@ -575,3 +575,52 @@ def test_cache_append_row_out_of_range_sets_error_and_skips():
     assert np.array_equal(kbits[0, pos[ok]], ref["idx_bits"][ok])
     assert np.array_equal(lat[0, pos[ok], :512], ref["c_kv"][ok])
     assert np.all(kbits[0, 255] == 0x5A) and np.all(lat[0, 255] == 3.0)
+
+
+# ---- the absorption around the attention (wl_mla_absorb_q / wl_mla_project_v) ----------------
+
+def _kv_b(rng):
+    return o.bf16_round((rng.standard_normal((64 * 448, 512)) * 0.05).astype(np.float32))
+
+
+@pytest.mark.parametrize("n", [1, 8, 13])
+def test_absorb_q_vs_oracle(n):
+    """fp32 accumulation, bf16 output: within one bf16 ulp of the output scale
+    (the rounding of the stored value), the roped part copied exactly."""
+    rng = np.random.default_rng(100 + n)
+    q = rng.standard_normal((n, 64, 256)).astype(np.float32)
+    kvb = _kv_b(rng)
+    got = cpu(A.mla_absorb_q(A.glm52_cfg(4096), dev(q, torch.float32), dev(kvb, torch.bfloat16)).float())
+    ref = o.mla_absorb_q(q, kvb)
+    assert_ulp(ref[..., :512], got[..., :512], tol=1.0, what="absorbed query")
+    assert np.array_equal(got[..., 512:], o.bf16_round(q[..., 192:]))
+
+
+@pytest.mark.parametrize("n", [1, 8, 13])
+def test_project_v_vs_oracle(n):
+    rng = np.random.default_rng(200 + n)
+    ctx = rng.standard_normal((n, 64, 512)).astype(np.float32)
+    kvb = _kv_b(rng)
+    got = cpu(A.mla_project_v(A.glm52_cfg(4096), dev(ctx, torch.float32), dev(kvb, torch.bfloat16)))
+    ref = o.mla_project_v(ctx, kvb)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_absorb_attend_project_chain():
+    """q -> absorb -> decode attention (dense, T below index_topk) -> project,
+    through the library, against the oracle's chain: 2 bf16 ulp of the output
+    scale (the reference's layer gate)."""
+    rng = np.random.default_rng(5)
+    T = 1024
+    inp = o.make_inputs(T, 0)
+    q = rng.standard_normal((1, 64, 256)).astype(np.float32)
+    kvb = _kv_b(rng)
+    cfg = A.glm52_cfg(T)
+    q_abs = A.mla_absorb_q(cfg, dev(q, torch.float32), dev(kvb, torch.bfloat16))
+    g = to_gpu(inp)
+    out = A.attn_decode(cfg, g["kv"], q_abs, mode=_lib.WL_MODE_DENSE)
+    got = cpu(A.mla_project_v(cfg, out["ctx"], dev(kvb, torch.bfloat16)))[0]
+    qa = o.bf16_round(o.mla_absorb_q(q, kvb).astype(np.float32))[0]
+    ctx, _ = o.mla_absorbed(qa, inp["c_kv"], inp["k_rot"], None, inp["scale"])
+    ref = o.mla_project_v(ctx, kvb)
+    assert_ulp(ref, got, what="absorb -> attention -> project")

@@ -62,13 +62,13 @@ def ch():
 
 def _absorbed_attn_out(ch, layer, pos, sel, drop_mask=True):
     HN, NP, RP, VD, L, HID, QL, IH, ID, TOPK, T = ch["dims"].tolist()
-    kvb = ch[f"l{layer}_kv_b_proj"].reshape(HN, NP + VD, L)
-    q_abs = np.concatenate([np.einsum("hn,hnl->hl", ch[f"l{layer}_q_nope"][pos], kvb[:, :NP]),
-                            ch[f"l{layer}_q_rot"][pos]], -1)
+    kvb = ch[f"l{layer}_kv_b_proj"]
+    q = np.concatenate([ch[f"l{layer}_q_nope"][pos], ch[f"l{layer}_q_rot"][pos]], -1)
+    q_abs = o.mla_absorb_q(q, kvb, nope=NP, v_head=VD)
     n = pos + 1
     drop = o.index_drop_mask(sel, n) if drop_mask else None
     ctx, _ = o.mla_absorbed(q_abs, ch[f"l{layer}_kc"][:n], ch[f"l{layer}_k_rot"][:n], drop, (NP + RP) ** -0.5)
-    v = np.einsum("hl,hvl->hv", ctx, kvb[:, NP:]).reshape(HN * VD)
+    v = o.mla_project_v(ctx, kvb, nope=NP, v_head=VD).reshape(HN * VD)
     return v @ ch[f"l{layer}_o_proj"].T
 
 

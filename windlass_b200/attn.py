@@ -182,6 +182,33 @@ def lse_merge(o_part: torch.Tensor, lse_part: torch.Tensor):
     return ctx, lse
 
 
+# ---- the absorption around the attention ------------------------------------------------------
+
+def mla_absorb_q(cfg: AttnCfg, q: torch.Tensor, kv_b: torch.Tensor) -> torch.Tensor:
+    """q fp32 [n, 64, 256] (qk_nope | roped qk_rope), kv_b bf16 [64 * 448, 512]
+    -> the attention's absorbed query, bf16 [n, 64, 576] (``wl_mla_absorb_q``;
+    mla_absorb_q, src/glm_layer_runner.cuh:196-215)."""
+    _need(q, torch.float32, "q")
+    _need(kv_b, torch.bfloat16, "kv_b")
+    q, kv_b = q.reshape(-1, N_HEADS * 256).contiguous(), kv_b.contiguous()
+    out = torch.empty(q.shape[0], N_HEADS, D_QK, dtype=torch.bfloat16, device=q.device)
+    check(lib().wl_mla_absorb_q(C.byref(cfg), q.shape[0], _ptr(q), q.stride(0), _ptr(kv_b), _ptr(out),
+                                N_HEADS * D_QK, _stream()), "wl_mla_absorb_q")
+    return out
+
+
+def mla_project_v(cfg: AttnCfg, ctx: torch.Tensor, kv_b: torch.Tensor) -> torch.Tensor:
+    """ctx fp32 [n, 64, 512] -> fp32 [n, 64, 256] through W_UV (``wl_mla_project_v``;
+    mla_project_v, src/glm_layer_runner.cuh:217-234)."""
+    _need(ctx, torch.float32, "ctx")
+    _need(kv_b, torch.bfloat16, "kv_b")
+    ctx, kv_b = ctx.reshape(-1, N_HEADS * KV_LORA).contiguous(), kv_b.contiguous()
+    out = torch.empty(ctx.shape[0], N_HEADS, 256, dtype=torch.float32, device=ctx.device)
+    check(lib().wl_mla_project_v(C.byref(cfg), ctx.shape[0], _ptr(ctx), ctx.stride(0), _ptr(kv_b), _ptr(out),
+                                 N_HEADS * 256, _stream()), "wl_mla_project_v")
+    return out
+
+
 # ---- the cache write path ---------------------------------------------------------------------
 
 def cache_append(cfg: AttnCfg, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *,

@@ -24,6 +24,7 @@
 #include "indexer.cuh"
 #include "mla_attn.cuh"
 #include "mla_attn64.cuh"
+#include "mla_proj.cuh"
 #include "p2p.cuh"
 #include "topk.cuh"
 
@@ -945,6 +946,38 @@ int wl_lse_merge(const float* o_part, const float* lse_part, int32_t n_rows, int
                  int32_t kv_lora, float* ctx, float* lse, void* stream) {
     return launch_merge(o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
                         lse_part_stride, n_heads, kv_lora, ctx, lse, static_cast<cudaStream_t>(stream));
+}
+
+// ---- the absorption around the attention ---------------------------------------------
+int wl_mla_absorb_q(const wl_attn_cfg* cfg, int32_t n, const float* q, int64_t q_row_stride, const void* kv_b,
+                    void* q_abs, int64_t q_abs_row_stride, void* stream) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (n < 0) return WL_ERR_ARG;
+    if (n == 0) return WL_OK;
+    if (!q || !kv_b || !q_abs || (reinterpret_cast<uintptr_t>(kv_b) & 3) ||
+        (reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(q_abs) & 1) ||
+        q_row_stride < wl::PJ_H * wl::PJ_QK || q_abs_row_stride < wl::PJ_H * (wl::PJ_L + wl::PJ_ROPE))
+        return WL_ERR_ARG;
+    WL_CUDA_TRY(launch_pdl(wl::mla_absorb_q_kernel, dim3(wl::PJ_L / 64, wl::PJ_H), dim3(wl::PJ_THREADS), 0,
+                           static_cast<cudaStream_t>(stream), (int)n, q, (long long)q_row_stride,
+                           static_cast<const __nv_bfloat16*>(kv_b), static_cast<__nv_bfloat16*>(q_abs),
+                           (long long)q_abs_row_stride));
+    return WL_OK;
+}
+
+int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_t ctx_row_stride,
+                     const void* kv_b, float* out, int64_t out_row_stride, void* stream) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (n < 0) return WL_ERR_ARG;
+    if (n == 0) return WL_OK;
+    if (!ctx || !kv_b || !out || !aligned16(kv_b) || !aligned16(ctx) || (ctx_row_stride & 3) ||
+        (reinterpret_cast<uintptr_t>(out) & 3) || ctx_row_stride < wl::PJ_H * wl::PJ_L ||
+        out_row_stride < wl::PJ_H * wl::PJ_V)
+        return WL_ERR_ARG;
+    WL_CUDA_TRY(launch_pdl(wl::mla_project_v_kernel, dim3(wl::PJ_V / 32, wl::PJ_H), dim3(wl::PJ_THREADS), 0,
+                           static_cast<cudaStream_t>(stream), (int)n, ctx, (long long)ctx_row_stride,
+                           static_cast<const __nv_bfloat16*>(kv_b), out, (long long)out_row_stride));
+    return WL_OK;
 }
 
 // ---- the cache write path -------------------------------------------------------------
