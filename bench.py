@@ -537,7 +537,66 @@ def side_configs(torch, A, _lib, device, stream):
     att_flops = n_q * 2048 * 64 * (2 * 576 + 2 * 512)
     out["cfg3_prefill"] = {"ms": round(ms, 3), "tflops": round((idx_flops + att_flops) / (ms * 1e-3) / 1e12, 1),
                            "idx_gflop": round(idx_flops / 1e9, 1), "attn_gflop": round(att_flops / 1e9, 1)}
+    del d
+    torch.cuda.empty_cache()
+    out["around"] = around_kernels(torch, A, device, stream)
     return out
+
+
+def around_kernels(torch, A, device, stream):
+    """The kernels either side of the substep at config 4's decode batch (8
+    rows) and config 3's prefill chunk (4096 tokens): the absorption GEMVs
+    (weights rotated over 8 instances, 233 MB > L2, so they stream from HBM)
+    and the cache write. Each timed as a CUDA graph of back-to-back calls."""
+    res = {}
+    cfg = A.glm52_cfg(8192)
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    n_w = 8
+    kvbs = [(torch.randn(64 * 448, 512, device=device, generator=g) * 0.05).to(torch.bfloat16) for _ in range(n_w)]
+    B = 8
+    q = torch.randn(B, 64, 256, device=device, generator=g)
+    ctx = torch.randn(B, 64, 512, device=device, generator=g)
+
+    def graph_us(fns, reps=20):
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for f in fns:
+                f()
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        return elapsed_ms(torch, lambda i: gr.replay(), reps, stream) / (reps * len(fns)) * 1e3
+
+    us = graph_us([lambda w=w: A.mla_absorb_q(cfg, q, w) for w in kvbs])
+    wb = 64 * 192 * 512 * 2
+    res["absorb_q_b8"] = {"us": round(us, 2), "weight_bytes": wb, "achieved_gbs": round(wb / (us * 1e-6) / 1e9, 1)}
+    us = graph_us([lambda w=w: A.mla_project_v(cfg, ctx, w) for w in kvbs])
+    wb = 64 * 256 * 512 * 2
+    res["project_v_b8"] = {"us": round(us, 2), "weight_bytes": wb, "achieved_gbs": round(wb / (us * 1e-6) / 1e9, 1)}
+    del kvbs
+    for name, n, T_max in (("cache_append_decode_b8", 8, 8192), ("cache_append_prefill_4096", 4096, 8192)):
+        n_seq = 8 if n == 8 else 1
+        keys = A.IndexKeys(torch.empty(n_seq, T_max, 128, dtype=torch.uint8, device=device),
+                           torch.empty(n_seq, T_max, dtype=torch.float32, device=device))
+        kv = A.LatentKV.packed(torch.empty(n_seq, T_max, 576, dtype=torch.bfloat16, device=device))
+        pos = (torch.arange(n, device=device, dtype=torch.int32) % T_max) if n_seq == 1 else \
+            torch.full((n,), T_max - 1, dtype=torch.int32, device=device)
+        seq = torch.arange(n, device=device, dtype=torch.int32) if n_seq > 1 else None
+        cs, sn = torch.rand(n, 32, device=device, generator=g), torch.rand(n, 32, device=device, generator=g)
+        k_raw, kv_raw = torch.randn(n, 128, device=device, generator=g), torch.randn(n, 576, device=device, generator=g)
+        kw = torch.ones(128, dtype=torch.bfloat16, device=device)
+        kb = torch.zeros(128, dtype=torch.bfloat16, device=device)
+        kvw = torch.ones(512, dtype=torch.bfloat16, device=device)
+        fn = lambda: A.cache_append(cfg, pos, cs, sn, keys=keys, k_raw=k_raw, k_norm_w=kw, k_norm_b=kb, kv=kv,  # noqa: E731
+                                    kv_raw=kv_raw, kv_norm_w=kvw, seq=seq)
+        us = graph_us([fn] * 8)
+        nb = n * (128 * 4 + 576 * 4 + 2 * 32 * 4 + 4 + 128 + 4 + 576 * 2)
+        res[name] = {"us": round(us, 2), "bytes": nb, "achieved_gbs": round(nb / (us * 1e-6) / 1e9, 1)}
+    return res
 
 
 if __name__ == "__main__":

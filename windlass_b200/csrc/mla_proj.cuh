@@ -10,10 +10,12 @@
 // giving the attention's input row [absorbed 512 | q_rot 64] in bf16.
 //
 // At decode these are matrix-vector products over 29 MB of bf16 weights (12.6
-// MB for W_UK, 16.8 MB for W_UV): HBM-bound, so each CTA streams its weight
-// tile once, coalesced, and applies it to a chunk of up to PJ_ROWS query rows
-// held in shared memory; fp32 accumulation; every cross-warp sum in a fixed
-// order (the results do not depend on scheduling).
+// MB of W_UK, 16.8 MB of W_UV): HBM-bound. Each CTA pulls its weight slice —
+// contiguous rows of kv_b — into shared memory with one bulk copy (the TMA
+// engine, no per-thread loads), keeps it there, and streams the query rows
+// through in chunks of PJ_ROWS; fp32 accumulation; every sum that spans
+// threads or CTAs runs in a fixed order, so results do not depend on
+// scheduling.
 #pragma once
 #include "ptx.cuh"
 
@@ -24,130 +26,200 @@ constexpr int PJ_KVB_ROWS = PJ_NOPE + PJ_V;  // kv_b rows per head
 constexpr int PJ_ROWS = 8;                   // query rows per chunk
 constexpr int PJ_THREADS = 256;
 
-// grid (512 / 64 column blocks, 64 heads). Warp w sums d in [24 w, 24 w + 24)
-// for the block's 64 columns (two per lane, one 128-byte weight row segment
-// per d); the 8 warps' partials are added in warp order.
-__global__ void __launch_bounds__(PJ_THREADS) mla_absorb_q_kernel(int n, const float* __restrict__ q,
-                                                                  long long q_row, const __nv_bfloat16* __restrict__ kvb,
-                                                                  __nv_bfloat16* __restrict__ q_abs, long long o_row) {
+// ---- absorb_q: a cluster of AQ_SPLIT CTAs per head, each over 48 of the 192 d ----
+constexpr int AQ_SPLIT = 4, AQ_D = PJ_NOPE / AQ_SPLIT;
+struct AqLayout {
+    static constexpr uint32_t OFF_W = 0;                                  // [48][512] bf16
+    static constexpr uint32_t OFF_PART = OFF_W + AQ_D * PJ_L * 2;         // [8][512] fp32 partial sums
+    static constexpr uint32_t OFF_Q = OFF_PART + PJ_ROWS * PJ_L * 4;      // [8][48] fp32
+    static constexpr uint32_t OFF_BAR = OFF_Q + PJ_ROWS * AQ_D * 4;
+    static constexpr uint32_t BYTES = OFF_BAR + 16;
+};
+
+// grid (AQ_SPLIT, 64 heads), cluster (AQ_SPLIT): CTA k of head h holds W_UK rows
+// [48 k, 48 k + 48). Thread t owns columns [8 (t % 64), + 8) and chunk rows
+// 2 (t / 64), + 1, summing its CTA's 48 d (one 16-byte weight load and one
+// 8-byte query load per 16 FMAs); then CTA k adds the AQ_SPLIT partials of
+// columns [128 k, 128 k + 128) over distributed shared memory in rank order.
+__global__ void __cluster_dims__(AQ_SPLIT, 1, 1) __launch_bounds__(PJ_THREADS, 2)
+    mla_absorb_q_kernel(int n, const float* __restrict__ q, long long q_row, const __nv_bfloat16* __restrict__ kvb,
+                        __nv_bfloat16* __restrict__ q_abs, long long o_row) {
+    using L = AqLayout;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const __nv_bfloat16* ws = reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_W);
+    float* part = reinterpret_cast<float*>(smem + L::OFF_PART);
+    float* qs = reinterpret_cast<float*>(smem + L::OFF_Q);  // [48 d][8 rows]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    const int h = blockIdx.y, tid = threadIdx.x;
+    const int cg = tid & 63, rg = tid >> 6;
+    const uint32_t rank = cluster_ctarank();
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
-    __shared__ float qs[PJ_ROWS][PJ_NOPE];
-    __shared__ float part[8][PJ_ROWS][64];
-    const int h = blockIdx.y, c0 = blockIdx.x * 64;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const __nv_bfloat16* w = kvb + (long long)h * PJ_KVB_ROWS * PJ_L + c0 + 2 * lane;
-    constexpr int DW = PJ_NOPE / 8;  // d per warp
-    __nv_bfloat162 wv[DW];           // this lane's weights, read once
-#pragma unroll
-    for (int j = 0; j < DW; ++j)
-        wv[j] = *reinterpret_cast<const __nv_bfloat162*>(w + (long long)(warp * DW + j) * PJ_L);
+    if (tid == 0) {
+        mbar_expect_tx(bar, AQ_D * PJ_L * 2);
+        bulk_g2s(smem + L::OFF_W, kvb + ((long long)h * PJ_KVB_ROWS + rank * AQ_D) * PJ_L, AQ_D * PJ_L * 2, bar);
+    }
     for (int r0 = 0; r0 < n; r0 += PJ_ROWS) {
         const int nr = min(PJ_ROWS, n - r0);
-        for (int i = tid; i < PJ_ROWS * PJ_NOPE; i += PJ_THREADS) {
-            const int r = i / PJ_NOPE, d = i % PJ_NOPE;
-            qs[r][d] = r < nr ? q[(long long)(r0 + r) * q_row + h * PJ_QK + d] : 0.f;
+        for (int i = tid; i < PJ_ROWS * AQ_D; i += PJ_THREADS) {
+            const int r = i / AQ_D, d = i % AQ_D;
+            qs[d * PJ_ROWS + r] = r < nr ? q[(long long)(r0 + r) * q_row + h * PJ_QK + rank * AQ_D + d] : 0.f;
         }
         __syncthreads();
-        float acc[PJ_ROWS][2];
+        if (r0 == 0) mbar_wait(bar, 0, 41);  // bounded; a timeout is recorded and the sums run on
+        float acc[2][8];
 #pragma unroll
-        for (int r = 0; r < PJ_ROWS; ++r) acc[r][0] = acc[r][1] = 0.f;
+        for (int r = 0; r < 2; ++r)
 #pragma unroll
-        for (int j = 0; j < DW; ++j) {
-            const float2 f = __bfloat1622float2(wv[j]);
+            for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < AQ_D; ++d) {
+            const uint4 wq = *reinterpret_cast<const uint4*>(ws + d * PJ_L + 8 * cg);
+            const float2 x = *reinterpret_cast<const float2*>(qs + d * PJ_ROWS + 2 * rg);
+            const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wq);
 #pragma unroll
-            for (int r = 0; r < PJ_ROWS; ++r) {
-                const float x = qs[r][warp * DW + j];
-                acc[r][0] = fmaf(x, f.x, acc[r][0]);
-                acc[r][1] = fmaf(x, f.y, acc[r][1]);
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(w2[e]);
+                acc[0][2 * e] = fmaf(x.x, f.x, acc[0][2 * e]);
+                acc[0][2 * e + 1] = fmaf(x.x, f.y, acc[0][2 * e + 1]);
+                acc[1][2 * e] = fmaf(x.y, f.x, acc[1][2 * e]);
+                acc[1][2 * e + 1] = fmaf(x.y, f.y, acc[1][2 * e + 1]);
             }
         }
 #pragma unroll
-        for (int r = 0; r < PJ_ROWS; ++r) {
-            part[warp][r][2 * lane] = acc[r][0];
-            part[warp][r][2 * lane + 1] = acc[r][1];
+        for (int r = 0; r < 2; ++r) {
+            float4* pr = reinterpret_cast<float4*>(part + (2 * rg + r) * PJ_L + 8 * cg);
+            pr[0] = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+            pr[1] = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
         }
-        __syncthreads();
-        for (int i = tid; i < PJ_ROWS * 64; i += PJ_THREADS) {
-            const int r = i / 64, c = i % 64;
-            if (r >= nr) continue;
-            float s = part[0][r][c];
+        cluster_sync_all();  // every CTA's partials visible to the cluster
+        {
+            const int r = tid >> 5, c = (int)rank * 128 + 4 * (tid & 31);
+            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int k = 1; k < 8; ++k) s += part[k][r][c];
-            q_abs[(long long)(r0 + r) * o_row + h * (PJ_L + PJ_ROPE) + c0 + c] = __float2bfloat16_rn(s);
+            for (uint32_t k = 0; k < AQ_SPLIT; ++k) {
+                const float4 v = dsmem_ld_f32x4(dsmem_addr(part + r * PJ_L + c, k));
+                s.x += v.x;
+                s.y += v.y;
+                s.z += v.z;
+                s.w += v.w;
+            }
+            if (r < nr) {
+                __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&lo);
+                u.y = *reinterpret_cast<uint32_t*>(&hi);
+                *reinterpret_cast<uint2*>(q_abs + (long long)(r0 + r) * o_row + h * (PJ_L + PJ_ROPE) + c) = u;
+            }
         }
-        if (blockIdx.x == 0)  // the roped part rides along
+        if (rank == 0)  // the roped part rides along
             for (int i = tid; i < nr * PJ_ROPE; i += PJ_THREADS) {
                 const int r = i / PJ_ROPE, j = i % PJ_ROPE;
                 q_abs[(long long)(r0 + r) * o_row + h * (PJ_L + PJ_ROPE) + PJ_L + j] =
                     __float2bfloat16_rn(q[(long long)(r0 + r) * q_row + h * PJ_QK + PJ_NOPE + j]);
             }
-        __syncthreads();  // qs / part are reused by the next chunk
+        cluster_sync_all();  // remote reads done before partials are rewritten or the CTA exits
     }
 }
 
-// grid (256 / 32 v blocks, 64 heads). Warp w computes v = v0 + 4 w .. + 3: lane
-// l dots columns [8 l, 8 l + 8) and [256 + 8 l, 256 + 8 l + 8) of the weight
-// row with the context, then a fixed-order tree over the lanes.
-__global__ void __launch_bounds__(PJ_THREADS) mla_project_v_kernel(int n, const float* __restrict__ ctx,
-                                                                   long long c_row,
-                                                                   const __nv_bfloat16* __restrict__ kvb,
-                                                                   float* __restrict__ out, long long o_row) {
+// ---- project_v: PV_SPLIT CTAs per head, each over 64 of the 256 v ----
+constexpr int PV_SPLIT = 4, PV_V = PJ_V / PV_SPLIT;
+struct PvLayout {
+    static constexpr uint32_t OFF_W = 0;                              // [64][512] bf16
+    static constexpr uint32_t OFF_C = OFF_W + PV_V * PJ_L * 2;        // [8][512] fp32
+    static constexpr uint32_t OFF_BAR = OFF_C + PJ_ROWS * PJ_L * 4;
+    static constexpr uint32_t BYTES = OFF_BAR + 16;
+};
+
+// grid (PV_SPLIT, 64 heads). Warp w computes v = 64 k + 8 w .. + 7: lane l dots
+// columns [8 l, 8 l + 8) and [256 + 8 l, 256 + 8 l + 8) of those 8 weight rows
+// with each context row; the 8 lane-partials are
+// then summed across the warp by a fixed butterfly that halves the values
+// each lane carries at every step (9 shuffles for 8 outputs).
+__global__ void __launch_bounds__(PJ_THREADS, 2) mla_project_v_kernel(int n, const float* __restrict__ ctx,
+                                                                      long long c_row,
+                                                                      const __nv_bfloat16* __restrict__ kvb,
+                                                                      float* __restrict__ out, long long o_row) {
+    using L = PvLayout;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const __nv_bfloat16* ws = reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_W);
+    float* cs = reinterpret_cast<float*>(smem + L::OFF_C);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    const int h = blockIdx.y, k = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
-    __shared__ __align__(16) float cs[PJ_ROWS][PJ_L];
-    const int h = blockIdx.y, v0 = blockIdx.x * 32;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint4 wv[4][2];  // the warp's 4 weight rows, this lane's 2 x 8 columns
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const __nv_bfloat16* wr = kvb + ((long long)h * PJ_KVB_ROWS + PJ_NOPE + v0 + 4 * warp + k) * PJ_L;
-        wv[k][0] = *reinterpret_cast<const uint4*>(wr + 8 * lane);
-        wv[k][1] = *reinterpret_cast<const uint4*>(wr + 256 + 8 * lane);
+    if (tid == 0) {
+        mbar_expect_tx(bar, PV_V * PJ_L * 2);
+        bulk_g2s(smem + L::OFF_W, kvb + ((long long)h * PJ_KVB_ROWS + PJ_NOPE + k * PV_V) * PJ_L, PV_V * PJ_L * 2,
+                 bar);
     }
+    // the output this lane ends up holding: v index within the warp's 8
+    const int vi = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
     for (int r0 = 0; r0 < n; r0 += PJ_ROWS) {
         const int nr = min(PJ_ROWS, n - r0);
         for (int i = tid; i < PJ_ROWS * PJ_L / 4; i += PJ_THREADS) {
             const int r = i / (PJ_L / 4), c4 = i % (PJ_L / 4);
-            reinterpret_cast<float4*>(cs[r])[c4] =
+            reinterpret_cast<float4*>(cs)[i] =
                 r < nr ? *reinterpret_cast<const float4*>(ctx + (long long)(r0 + r) * c_row + h * PJ_L + 4 * c4)
                        : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         __syncthreads();
+        if (r0 == 0) mbar_wait(bar, 0, 42);  // bounded; a timeout is recorded
         for (int r = 0; r < nr; ++r) {
-            float x[16];
+            float s[8];
 #pragma unroll
+            for (int j = 0; j < 8; ++j) s[j] = 0.f;
+#pragma unroll 1
             for (int half = 0; half < 2; ++half) {
-                const float4 a = *reinterpret_cast<const float4*>(&cs[r][256 * half + 8 * lane]);
-                const float4 b = *reinterpret_cast<const float4*>(&cs[r][256 * half + 8 * lane + 4]);
-                x[8 * half + 0] = a.x;
-                x[8 * half + 1] = a.y;
-                x[8 * half + 2] = a.z;
-                x[8 * half + 3] = a.w;
-                x[8 * half + 4] = b.x;
-                x[8 * half + 5] = b.y;
-                x[8 * half + 6] = b.z;
-                x[8 * half + 7] = b.w;
-            }
+                const float4 a = *reinterpret_cast<const float4*>(cs + r * PJ_L + 256 * half + 8 * lane);
+                const float4 b = *reinterpret_cast<const float4*>(cs + r * PJ_L + 256 * half + 8 * lane + 4);
+                const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float s = 0.f;
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&wv[k][half]);
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 wq = *reinterpret_cast<const uint4*>(ws + (warp * 8 + j) * PJ_L + 256 * half + 8 * lane);
+                    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&wq);
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const float2 f = __bfloat1622float2(p[e]);
-                        s = fmaf(x[8 * half + 2 * e], f.x, s);
-                        s = fmaf(x[8 * half + 2 * e + 1], f.y, s);
+                        s[j] = fmaf(x[2 * e], f.x, s[j]);
+                        s[j] = fmaf(x[2 * e + 1], f.y, s[j]);
                     }
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
-                if (lane == 0) out[(long long)(r0 + r) * o_row + h * PJ_V + v0 + 4 * warp + k] = s;
             }
+            // butterfly: keep half, send half, at lane distances 16, 8, 4; then 2, 1
+            const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+            float t[4], u[2];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float keep = b16 ? s[4 + j] : s[j], send = b16 ? s[j] : s[4 + j];
+                t[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float keep = b8 ? t[2 + j] : t[j], send = b8 ? t[j] : t[2 + j];
+                u[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+            float v;
+            {
+                const float keep = b4 ? u[1] : u[0], send = b4 ? u[0] : u[1];
+                v = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            if ((lane & 3) == 0) out[(long long)(r0 + r) * o_row + h * PJ_V + k * PV_V + warp * 8 + vi] = v;
         }
-        __syncthreads();  // cs is reused by the next chunk
+        __syncthreads();  // cs is rewritten by the next chunk
     }
 }
 

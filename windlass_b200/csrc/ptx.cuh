@@ -202,6 +202,14 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank)
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
     return ra;
 }
+__device__ __forceinline__ float4 dsmem_ld_f32x4(uint32_t ra) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(ra)
+                 : "memory");
+    return v;
+}
 __device__ __forceinline__ uint32_t dsmem_atom_add(uint32_t ra, uint32_t v) {
     uint32_t old;
     asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(ra), "r"(v) : "memory");

@@ -106,6 +106,10 @@ int ensure_attrs() {
                                      wl::TOPKM_PART_SMEM));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::TOPKM_THR_SMEM));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_absorb_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::AqLayout::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_project_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::PvLayout::BYTES));
     int sms = 0;
     WL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     g_sm_count[dev] = sms;
@@ -956,9 +960,12 @@ int wl_mla_absorb_q(const wl_attn_cfg* cfg, int32_t n, const float* q, int64_t q
     if (n == 0) return WL_OK;
     if (!q || !kv_b || !q_abs || (reinterpret_cast<uintptr_t>(kv_b) & 3) ||
         (reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(q_abs) & 1) ||
-        q_row_stride < wl::PJ_H * wl::PJ_QK || q_abs_row_stride < wl::PJ_H * (wl::PJ_L + wl::PJ_ROPE))
+        q_row_stride < wl::PJ_H * wl::PJ_QK || q_abs_row_stride < wl::PJ_H * (wl::PJ_L + wl::PJ_ROPE) ||
+        !aligned16(kv_b) || (reinterpret_cast<uintptr_t>(q_abs) & 7) || (q_abs_row_stride & 3))
         return WL_ERR_ARG;
-    WL_CUDA_TRY(launch_pdl(wl::mla_absorb_q_kernel, dim3(wl::PJ_L / 64, wl::PJ_H), dim3(wl::PJ_THREADS), 0,
+    if (int e = ensure_attrs()) return e;
+    WL_CUDA_TRY(launch_pdl(wl::mla_absorb_q_kernel, dim3(wl::AQ_SPLIT, wl::PJ_H), dim3(wl::PJ_THREADS),
+                           wl::AqLayout::BYTES,
                            static_cast<cudaStream_t>(stream), (int)n, q, (long long)q_row_stride,
                            static_cast<const __nv_bfloat16*>(kv_b), static_cast<__nv_bfloat16*>(q_abs),
                            (long long)q_abs_row_stride));
@@ -971,10 +978,12 @@ int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_
     if (n < 0) return WL_ERR_ARG;
     if (n == 0) return WL_OK;
     if (!ctx || !kv_b || !out || !aligned16(kv_b) || !aligned16(ctx) || (ctx_row_stride & 3) ||
-        (reinterpret_cast<uintptr_t>(out) & 3) || ctx_row_stride < wl::PJ_H * wl::PJ_L ||
+        !aligned16(out) || (out_row_stride & 3) || ctx_row_stride < wl::PJ_H * wl::PJ_L ||
         out_row_stride < wl::PJ_H * wl::PJ_V)
         return WL_ERR_ARG;
-    WL_CUDA_TRY(launch_pdl(wl::mla_project_v_kernel, dim3(wl::PJ_V / 32, wl::PJ_H), dim3(wl::PJ_THREADS), 0,
+    if (int e = ensure_attrs()) return e;
+    WL_CUDA_TRY(launch_pdl(wl::mla_project_v_kernel, dim3(wl::PV_SPLIT, wl::PJ_H), dim3(wl::PJ_THREADS),
+                           wl::PvLayout::BYTES,
                            static_cast<cudaStream_t>(stream), (int)n, ctx, (long long)ctx_row_stride,
                            static_cast<const __nv_bfloat16*>(kv_b), out, (long long)out_row_stride));
     return WL_OK;
