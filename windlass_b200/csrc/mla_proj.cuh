@@ -71,7 +71,7 @@ __global__ void __cluster_dims__(AQ_SPLIT, 1, 1) __launch_bounds__(PJ_THREADS, 2
             qs[d * PJ_ROWS + r] = r < nr ? q[(long long)(r0 + r) * q_row + h * PJ_QK + rank * AQ_D + d] : 0.f;
         }
         __syncthreads();
-        if (r0 == 0) mbar_wait(bar, 0, 41);  // bounded; a timeout is recorded and the sums run on
+        if (r0 == 0) mbar_wait_fast(bar, 0, 41);  // bounded; a timeout is recorded and the sums run on
         float acc[2][8];
 #pragma unroll
         for (int r = 0; r < 2; ++r)
@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 2) mla_project_v_kernel(int n, con
                        : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         __syncthreads();
-        if (r0 == 0) mbar_wait(bar, 0, 42);  // bounded; a timeout is recorded
+        if (r0 == 0) mbar_wait_fast(bar, 0, 42);  // bounded; a timeout is recorded
         for (int r = 0; r < nr; ++r) {
             float s[8];
 #pragma unroll
