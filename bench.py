@@ -545,9 +545,9 @@ def side_configs(torch, A, _lib, device, stream):
 
 def around_kernels(torch, A, device, stream):
     """The kernels either side of the substep at config 4's decode batch (8
-    rows) and config 3's prefill chunk (4096 tokens): the absorption GEMVs
-    (weights rotated over 8 instances, 233 MB > L2, so they stream from HBM)
-    and the cache write. Each timed as a CUDA graph of back-to-back calls."""
+    rows) and config 3's prefill chunk (4096 tokens): the absorption GEMVs and
+    the indexer's query projection (weights rotated over 8 instances, larger
+    than L2 in total, so they stream from HBM) and the cache write. Each timed as a CUDA graph of back-to-back calls."""
     res = {}
     cfg = A.glm52_cfg(8192)
     g = torch.Generator(device=device)
@@ -578,6 +578,15 @@ def around_kernels(torch, A, device, stream):
     wb = 64 * 256 * 512 * 2
     res["project_v_b8"] = {"us": round(us, 2), "weight_bytes": wb, "achieved_gbs": round(wb / (us * 1e-6) / 1e9, 1)}
     del kvbs
+    # the indexer's query side at B = 8 (wq_b 16.8 MB bf16 + weights_proj 0.8 MB fp32, rotated over 8)
+    wqs = [(torch.randn(4096, 2048, device=device, generator=g) * 0.02).to(torch.bfloat16) for _ in range(n_w)]
+    wp = torch.randn(32, 6144, device=device, generator=g) * 0.02
+    qr, xh = torch.randn(B, 2048, device=device, generator=g), torch.randn(B, 6144, device=device, generator=g)
+    cq, sq = torch.rand(B, 32, device=device, generator=g), torch.rand(B, 32, device=device, generator=g)
+    us = graph_us([lambda w=w: A.indexer_query(cfg, qr, w, xh, wp, cq, sq) for w in wqs])
+    wb = 4096 * 2048 * 2 + 32 * 6144 * 4
+    res["indexer_query_b8"] = {"us": round(us, 2), "weight_bytes": wb, "achieved_gbs": round(wb / (us * 1e-6) / 1e9, 1)}
+    del wqs
     for name, n, T_max in (("cache_append_decode_b8", 8, 8192), ("cache_append_prefill_4096", 4096, 8192)):
         n_seq = 8 if n == 8 else 1
         keys = A.IndexKeys(torch.empty(n_seq, T_max, 128, dtype=torch.uint8, device=device),

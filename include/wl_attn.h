@@ -302,6 +302,23 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io,
  * (different streams, or different host threads) race and must not. */
 int wl_attn_decode_noalloc(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, void* stream);
 
+/* ---- the indexer's query side --------------------------------------------------
+ * For n query rows: q_idx[r] = RoPE(wq_b @ q_resid[r]) (RoPE on dims [0, 64)
+ * of each of the 32 heads, interleaved pairs in, halves out, with the row's
+ * table cos/sin [n, 32]) stored bf16 [n, 32, 128]; and w_idx[r][h] =
+ * (weights_proj @ x[r])[h] * 32^-0.5 stored fp32 [n, 32] — the inputs the
+ * scoring entry points take. q_resid: fp32 [n, 2048] (the shared q-LoRA
+ * residual); wq_b: bf16 [32*128, 2048]; x: fp32 [n, hidden] (the
+ * input_layernorm output; hidden a multiple of 1024); weights_proj: fp32
+ * [32, hidden]. Row strides in elements, multiples of 4; matrices 16-byte
+ * aligned. Replaces the query half of launch_indexer_query
+ * (glm_kernels.cuh:469-472: launch_matvec_bf16, rope_interleave_slice,
+ * indexer_head_weights). */
+int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, int64_t q_resid_row_stride,
+                     const void* wq_b, const float* x, int64_t x_row_stride, int32_t hidden,
+                     const float* weights_proj, const float* cos, const float* sin,
+                     void* q_idx, float* w_idx, void* stream);
+
 /* ---- the absorption around the attention ------------------------------------
  * kv_b = kv_b_proj, device bf16 [n_heads * (qk_nope 192 + v_head 256), kv_lora]
  * (per head: 192 W_UK rows, then 256 W_UV rows), 16-byte aligned.

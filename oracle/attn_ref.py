@@ -17,6 +17,9 @@ function citing the reference it follows (paths inside ssubbotin/windlass):
   mla_absorbed     src/glm_layer_runner.cuh:251-298 (absorbed form of
                    attn_block's s = q.K, drop -> -inf, softmax, p.V,
                    tools/ref_glm_chain.py:616-638)
+  indexer_query    tools/ref_glm_chain.py:489-497 (indexer_scores' q and w:
+                   wq_b @ q_resid, RoPE on the leading 64 of each head,
+                   weights_proj @ x * H^-0.5; glm_kernels.cuh:469-472)
   mla_absorb_q     src/glm_layer_runner.cuh:196-215 (q_nope through W_UK),
                    with the roped part appended: the attention's input row
   mla_project_v    src/glm_layer_runner.cuh:217-234 (ctx through W_UV)
@@ -146,6 +149,19 @@ def mla_sparse(q_abs, c_kv, k_rot, sel, scale, dtype=np.float64):
     T = c_kv.shape[0]
     keep = canonical(sel, T)
     return mla_absorbed(q_abs, c_kv[keep], k_rot[keep], None, scale, dtype)
+
+
+def indexer_query(q_resid, wq_b, x, weights_proj, cos, sin, H: int = 32, D: int = 128, R: int = 64):
+    """(q [n, H, D] post-RoPE, w [n, H]) for n query rows, float64: q = wq_b @ q_resid
+    reshaped per head with RoPE (interleaved in, halves out) on its leading R
+    dims; w = weights_proj @ x * H^-0.5 (ref_glm_chain.py:489-497)."""
+    q = np.asarray(q_resid, np.float64) @ np.asarray(wq_b, np.float64).T
+    q = q.reshape(q.shape[0], H, D)
+    c, s = np.asarray(cos, np.float64)[:, None, :], np.asarray(sin, np.float64)[:, None, :]
+    a, b = q[..., 0:R:2], q[..., 1:R:2]
+    q = np.concatenate([a * c - b * s, b * c + a * s, q[..., R:]], axis=-1)
+    w = np.asarray(x, np.float64) @ np.asarray(weights_proj, np.float64).T * H ** -0.5
+    return q, w
 
 
 def mla_absorb_q(q: np.ndarray, kv_b: np.ndarray, nope: int = 192, v_head: int = 256) -> np.ndarray:

@@ -17,6 +17,11 @@ Writes two files next to this script:
                    the first 512 of kv_a_proj_with_mqa, RoPE of the trailing
                    64) for 16 tokens at scattered positions, with the
                    projections' outputs the kernel takes as inputs.
+  query_ref.npz    the indexer's query side at GLM-5.2's dimensions: the
+                   reference's indexer_scores (its q and w) for 4 rows whose
+                   inputs (q_resid, x with hidden 1024, wq_b, weights_proj,
+                   RoPE rows) are regenerated from seed 20260806 by
+                   query_inputs() below; only the outputs are stored.
   chain_ref.npz    tools/ref_glm_chain.attn_block (the direct, non-absorbed
                    MLA form with the DSA indexer and IndexShare) run over
                    positions 0..T-1 of a two-layer group (layer 0 "full",
@@ -135,10 +140,40 @@ def cache_fixture(ref: str) -> dict:
                 ref_krot=R.rope_interleave(ckv[:, 512:], cos[pos], sin[pos]).astype(np.float32))
 
 
+def query_inputs() -> dict:
+    """Seeded inputs of query_ref.npz (also called by the tests)."""
+    rng = np.random.default_rng(20260806)
+    n, HID = 4, 1024
+    f32 = lambda *s, sd=1.0: (rng.standard_normal(s) * sd).astype(np.float32)  # noqa: E731
+    wq_b = f32(32 * 128, 2048, sd=0.02)
+    wq_b = ((wq_b.view(np.uint32) + 0x7FFF + ((wq_b.view(np.uint32) >> 16) & 1)) & 0xFFFF0000).view(np.float32)
+    ang = rng.uniform(0, 2 * np.pi, (n, 32))
+    return dict(q_resid=f32(n, 2048), x=f32(n, HID), wq_b=wq_b, weights_proj=f32(32, HID, sd=0.05),
+                cos=np.cos(ang).astype(np.float32), sin=np.sin(ang).astype(np.float32),
+                pos=np.array([0, 5, 100, 4095]))
+
+
+def query_fixture(ref: str) -> dict:
+    sys.path.insert(0, os.path.join(ref, "tools"))
+    import ref_glm_chain as R  # noqa: E402
+
+    q = query_inputs()
+    cfg = dict(index_heads=32, index_dim=128, qk_rope=64)
+    W = dict(ix_wq_b=q["wq_b"], ix_weights_proj=q["weights_proj"])
+    K = np.zeros((1, 128), np.float32)
+    outs_q, outs_w = [], []
+    for i in range(4):
+        # indexer_scores takes cos/sin tables indexed by pos: a one-row table per call
+        qq, ww, _ = R.indexer_scores(q["q_resid"][i], q["x"][i], K, W, cfg, 0, q["cos"][i:i + 1], q["sin"][i:i + 1])
+        outs_q.append(qq)
+        outs_w.append(ww)
+    return dict(ref_q=np.stack(outs_q).astype(np.float32), ref_w=np.stack(outs_w).astype(np.float32))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("WINDLASS_REF", ""), help="reference checkout")
-    ap.add_argument("--which", default="indexer,chain,cache", help="fixtures to write (comma-separated)")
+    ap.add_argument("--which", default="indexer,chain,cache,query", help="fixtures to write (comma-separated)")
     a = ap.parse_args()
     if not a.ref or not os.path.isdir(os.path.join(a.ref, "tools")):
         raise SystemExit("pass --ref <path to the reference checkout>")
@@ -150,6 +185,8 @@ def main() -> None:
         np.savez_compressed(os.path.join(HERE, "chain_ref.npz"), **chain_fixture(a.ref))
     if "cache" in which:
         np.savez_compressed(os.path.join(HERE, "cache_ref.npz"), **cache_fixture(a.ref))
+    if "query" in which:
+        np.savez_compressed(os.path.join(HERE, "query_ref.npz"), **query_fixture(a.ref))
     print("wrote", HERE)
 
 

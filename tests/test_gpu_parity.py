@@ -624,3 +624,34 @@ def test_absorb_attend_project_chain():
     ctx, _ = o.mla_absorbed(qa, inp["c_kv"], inp["k_rot"], None, inp["scale"])
     ref = o.mla_project_v(ctx, kvb)
     assert_ulp(ref, got, what="absorb -> attention -> project")
+
+
+# ---- the indexer's query side (wl_indexer_query) ------------------------------------------------
+
+def _query_case(q):
+    cfg = A.glm52_cfg(4096)
+    qi, wi = A.indexer_query(cfg, dev(q["q_resid"], torch.float32), dev(q["wq_b"], torch.bfloat16),
+                             dev(q["x"], torch.float32), dev(q["weights_proj"], torch.float32),
+                             dev(q["cos"], torch.float32), dev(q["sin"], torch.float32))
+    rq, rw = o.indexer_query(q["q_resid"], q["wq_b"], q["x"], q["weights_proj"], q["cos"], q["sin"])
+    assert_ulp(rq, cpu(qi.float()), tol=1.0, what="q_idx (bf16)")
+    assert np.abs(cpu(wi) - rw).max() <= 1e-5 * np.abs(rw).max()
+
+
+def test_indexer_query_golden_inputs():
+    import os
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    from make_golden import query_inputs
+    _query_case(query_inputs())
+
+
+@pytest.mark.parametrize("n", [1, 13])
+def test_indexer_query_glm_hidden(n):
+    rng = np.random.default_rng(300 + n)
+    ang = rng.uniform(0, 2 * np.pi, (n, 32))
+    _query_case(dict(q_resid=rng.standard_normal((n, 2048)).astype(np.float32),
+                     wq_b=o.bf16_round((rng.standard_normal((4096, 2048)) * 0.02).astype(np.float32)),
+                     x=rng.standard_normal((n, 6144)).astype(np.float32),
+                     weights_proj=(rng.standard_normal((32, 6144)) * 0.02).astype(np.float32),
+                     cos=np.cos(ang).astype(np.float32), sin=np.sin(ang).astype(np.float32)))

@@ -141,6 +141,23 @@ def test_cache_append_negative_control_layernorm_bias():
     assert rel(g["ref_key"], r["key_f32"]) > 1e-3
 
 
+# ---- pin 4: the indexer's query side (indexer_scores' q and w) ----
+
+def test_indexer_query_matches_reference_fixture():
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import query_inputs
+
+    q = query_inputs()
+    g = dict(np.load(os.path.join(GOLD, "query_ref.npz")))
+    rq, rw = o.indexer_query(q["q_resid"], q["wq_b"], q["x"], q["weights_proj"], q["cos"], q["sin"])
+    assert rel(g["ref_q"], rq) <= 1e-6
+    assert rel(g["ref_w"], rw) <= 1e-6
+    # negative control: RoPE on the trailing 64 dims instead of the leading 64
+    wrong = np.concatenate([rq[..., 64:], rq[..., :64]], -1)
+    assert rel(g["ref_q"], wrong) > 1e-2
+
+
 # ---- properties ----------------------------------------------------------------------
 
 def test_e4m3_quantisation_roundtrip():

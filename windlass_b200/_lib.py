@@ -110,6 +110,7 @@ SIGNATURES = {
     "wl_device_error": (C.c_int, [i32, C.POINTER(u32)]),
     "wl_attn_decode_noalloc": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(DecodeIO), vp]),
     "wl_cache_append": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(CacheAppendIO), vp]),
+    "wl_indexer_query": (C.c_int, [C.POINTER(AttnCfg), i32, vp, i64, vp, vp, i64, i32, vp, vp, vp, vp, vp, vp]),
     "wl_mla_absorb_q": (C.c_int, [C.POINTER(AttnCfg), i32, vp, i64, vp, vp, i64, vp]),
     "wl_mla_project_v": (C.c_int, [C.POINTER(AttnCfg), i32, vp, i64, vp, vp, i64, vp]),
 }

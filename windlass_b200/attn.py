@@ -182,6 +182,30 @@ def lse_merge(o_part: torch.Tensor, lse_part: torch.Tensor):
     return ctx, lse
 
 
+# ---- the indexer's query side ------------------------------------------------------------------
+
+def indexer_query(cfg: AttnCfg, q_resid: torch.Tensor, wq_b: torch.Tensor, x: torch.Tensor,
+                  weights_proj: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    """(q_idx bf16 [n, 32, 128], w_idx fp32 [n, 32]) from q_resid fp32 [n, 2048],
+    wq_b bf16 [4096, 2048], x fp32 [n, hidden], weights_proj fp32 [32, hidden] and
+    the rows' RoPE tables [n, 32] (``wl_indexer_query``; the query half of
+    launch_indexer_query, src/glm_kernels.cuh:469-472; numpy indexer_scores'
+    q and w, tools/ref_glm_chain.py:482-501)."""
+    for t, dt, nm in ((q_resid, torch.float32, "q_resid"), (wq_b, torch.bfloat16, "wq_b"),
+                      (x, torch.float32, "x"), (weights_proj, torch.float32, "weights_proj"),
+                      (cos, torch.float32, "cos"), (sin, torch.float32, "sin")):
+        _need(t, dt, nm)
+    q_resid, x = q_resid.contiguous(), x.contiguous()
+    wq_b, weights_proj, cos, sin = wq_b.contiguous(), weights_proj.contiguous(), cos.contiguous(), sin.contiguous()
+    n, hidden = x.shape
+    q_idx = torch.empty(n, IDX_H, IDX_D, dtype=torch.bfloat16, device=x.device)
+    w_idx = torch.empty(n, IDX_H, dtype=torch.float32, device=x.device)
+    check(lib().wl_indexer_query(C.byref(cfg), n, _ptr(q_resid), q_resid.stride(0), _ptr(wq_b), _ptr(x),
+                                 x.stride(0), hidden, _ptr(weights_proj), _ptr(cos), _ptr(sin), _ptr(q_idx),
+                                 _ptr(w_idx), _stream()), "wl_indexer_query")
+    return q_idx, w_idx
+
+
 # ---- the absorption around the attention ------------------------------------------------------
 
 def mla_absorb_q(cfg: AttnCfg, q: torch.Tensor, kv_b: torch.Tensor) -> torch.Tensor:

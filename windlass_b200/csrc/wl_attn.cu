@@ -21,6 +21,7 @@
 
 #include "../../include/wl_attn.h"
 #include "cache_append.cuh"
+#include "idx_query.cuh"
 #include "indexer.cuh"
 #include "mla_attn.cuh"
 #include "mla_attn64.cuh"
@@ -106,6 +107,8 @@ int ensure_attrs() {
                                      wl::TOPKM_PART_SMEM));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::TOPKM_THR_SMEM));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::idx_query_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::IQ_SMEM));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_absorb_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::AqLayout::BYTES));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_project_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -950,6 +953,32 @@ int wl_lse_merge(const float* o_part, const float* lse_part, int32_t n_rows, int
                  int32_t kv_lora, float* ctx, float* lse, void* stream) {
     return launch_merge(o_part, lse_part, n_rows, n_parts, row_stride, part_stride, lse_row_stride,
                         lse_part_stride, n_heads, kv_lora, ctx, lse, static_cast<cudaStream_t>(stream));
+}
+
+// ---- the indexer's query side ------------------------------------------------------------
+int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, int64_t q_resid_row_stride,
+                     const void* wq_b, const float* x, int64_t x_row_stride, int32_t hidden,
+                     const float* weights_proj, const float* cos, const float* sin, void* q_idx, float* w_idx,
+                     void* stream) {
+    if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
+    if (n < 0) return WL_ERR_ARG;
+    if (n == 0) return WL_OK;
+    if (!q_resid || !wq_b || !x || !weights_proj || !cos || !sin || !q_idx || !w_idx) return WL_ERR_ARG;
+    if (!aligned16(q_resid) || (q_resid_row_stride & 3) || q_resid_row_stride < wl::IQ_QL || !aligned16(wq_b) ||
+        !aligned16(x) || (x_row_stride & 3) || hidden <= 0 || (hidden % 1024) || x_row_stride < hidden ||
+        !aligned16(weights_proj) || (reinterpret_cast<uintptr_t>(q_idx) & 1) ||
+        (reinterpret_cast<uintptr_t>(w_idx) & 3))
+        return WL_ERR_ARG;
+    if (int e = ensure_attrs()) return e;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    WL_CUDA_TRY(launch_pdl(wl::idx_query_kernel, dim3(wl::IQ_H * wl::IQ_D / wl::IQ_DIMS), dim3(wl::IQ_THREADS),
+                           wl::IQ_SMEM, st, (int)n, q_resid, (long long)q_resid_row_stride,
+                           static_cast<const __nv_bfloat16*>(wq_b), cos, sin, static_cast<__nv_bfloat16*>(q_idx),
+                           (long long)wl::IQ_H * wl::IQ_D));
+    const float head_scale = (float)(1.0 / std::sqrt((double)wl::IQ_H));
+    WL_CUDA_TRY(launch_pdl(wl::idx_head_weights_kernel, dim3(wl::IQ_H), dim3(256), 0, st, (int)n, x,
+                           (long long)x_row_stride, weights_proj, (int)hidden, head_scale, w_idx, (long long)wl::IQ_H));
+    return WL_OK;
 }
 
 // ---- the absorption around the attention ---------------------------------------------
