@@ -202,6 +202,15 @@ size_t wl_attn_prefill_workspace_bytes(const wl_attn_cfg* cfg, int32_t n_q, int3
 int wl_attn_prefill(const wl_attn_cfg* cfg, const wl_attn_prefill_io* io,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* wl_attn_prefill with run_prefill_layer_major's IndexShare dispatch
+ * (glm_layer_runner.cuh:954-983): an owner layer publishes every row's
+ * selection (io->sel_out / sel_n_out, which must be set: row i is query
+ * position pos0 + i) into *share; a shared layer requires *share and attends
+ * each row over its own published row (or densely if share->dense). */
+int wl_attn_layer_prefill(const wl_attn_cfg* cfg, wl_attn_prefill_io* io,
+                          int32_t owner, uint32_t layer, wl_index_share* share,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- the individual hot-path kernels ------------------------------------- */
 
 /* a1+a2 fused: index[r][t] = sum_h w[r][h] * relu(idx_qk_scale * scale[t] *

@@ -432,6 +432,41 @@ def test_prefill_consumer_and_dense():
     assert torch.equal(den["ctx"], big["ctx"]), "k >= T: sparse prefill must equal dense bit for bit"
 
 
+def test_prefill_layer_group_index_share():
+    """run_prefill_layer_major's IndexShare over a chunk: the owner layer
+    publishes one selection per row; shared layers (other latent caches)
+    attend each row over its own published row; before any owner a shared
+    layer raises; dense mode attends every causal key."""
+    pos0, n_q = 200, 24
+    T = pos0 + n_q
+    cfg = A.glm52_cfg(T, index_topk=96)
+    share = A.IndexShare()
+    inp0, g0 = _prefill_inputs(pos0, n_q, 3)
+    with pytest.raises(RuntimeError, match="no published indices"):
+        A.run_prefill_attention(cfg, 1, False, share, g0["kv"], g0["q_abs"], pos0)
+    own = A.run_prefill_attention(cfg, 0, True, share, g0["kv"], g0["q_abs"], pos0, g0["keys"], g0["q_idx"],
+                                  g0["w_idx"])
+    assert share.producer == 0
+    sel, n = cpu(own["sel"]), cpu(own["sel_n"])
+    ref = A.attn_prefill(cfg, g0["kv"], g0["q_abs"], pos0, keys=g0["keys"], q_idx=g0["q_idx"], w_idx=g0["w_idx"])
+    assert np.array_equal(sel, cpu(ref["sel"])) and torch.equal(own["ctx"], ref["ctx"])
+    inp1 = o.make_inputs(T, 3, seq=1, n_q=n_q)
+    g1 = to_gpu(dict(inp1, q_abs=inp1["q_abs"][:, None], q_idx=inp1["q_idx"][:, None],
+                     w_idx=inp1["w_idx"][:, None]))
+    q1 = dev(inp1["q_abs"], torch.bfloat16)
+    con = A.run_prefill_attention(cfg, 1, False, share, g1["kv"], q1, pos0)
+    assert share.producer == 0
+    ctx = cpu(con["ctx"])
+    for i in (0, 5, n_q - 1):
+        L = pos0 + i + 1
+        rc, _ = o.mla_sparse(inp1["q_abs"][i], inp1["c_kv"][:L], inp1["k_rot"][:L], sel[i, :n[i]], 1 / 16)
+        assert_ulp(rc, ctx[i], what=f"shared layer row {i}")
+    den = A.run_prefill_attention(cfg, 7, False, A.IndexShare(dense=True), g1["kv"], q1, pos0)
+    i = n_q - 1
+    rc, _ = o.mla_absorbed(inp1["q_abs"][i], inp1["c_kv"][:T], inp1["k_rot"][:T], None, 1 / 16)
+    assert_ulp(rc, cpu(den["ctx"])[i], what="dense mode")
+
+
 def test_decode_long_context_multi_cta_topk():
     """T above the single-CTA top-k limit: the multi-CTA top-k's set must equal
     numpy's top-k of the GPU's own scores exactly, and the attention must match."""

@@ -91,6 +91,8 @@ SIGNATURES = {
                                        C.POINTER(IndexShareC), vp, C.c_size_t, vp]),
     "wl_attn_prefill_workspace_bytes": (C.c_size_t, [C.POINTER(AttnCfg), i32, i32]),
     "wl_attn_prefill": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(PrefillIO), vp, C.c_size_t, vp]),
+    "wl_attn_layer_prefill": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(PrefillIO), i32, u32,
+                                        C.POINTER(IndexShareC), vp, C.c_size_t, vp]),
     "wl_indexer_scores": (C.c_int, [C.POINTER(AttnCfg), C.POINTER(IndexCache), i32,
                                     C.POINTER(Rows), vp, vp, vp, i64, vp]),
     "wl_indexer_topk": (C.c_int, [vp, i64, C.POINTER(Rows), i32, i32, vp, vp, i64, vp, vp, C.c_size_t, vp]),

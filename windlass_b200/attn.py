@@ -459,6 +459,43 @@ def attn_prefill(cfg: AttnCfg, kv: LatentKV, q_abs: torch.Tensor, pos0: int, *,
     return dict(ctx=ctx, lse=lse, sel=sel_out, sel_n=sel_n_out)
 
 
+def run_prefill_attention(cfg: AttnCfg, layer: int, owner: bool, share: IndexShare, kv: LatentKV,
+                          q_abs: torch.Tensor, pos0: int, keys: IndexKeys | None = None,
+                          q_idx: torch.Tensor | None = None, w_idx: torch.Tensor | None = None) -> dict:
+    """The attention substep of one layer of run_prefill_layer_major
+    (glm_layer_runner.cuh:954-983) for a chunk of n_q rows after pos0, through
+    ``wl_attn_layer_prefill``: owners publish every row's selection, shared
+    layers attend each row over its own published row."""
+    n_q = q_abs.shape[0]
+    T = pos0 + n_q
+    kk = min(cfg.index_topk, T)
+    dev = q_abs.device
+    ctx = torch.empty(n_q, N_HEADS, KV_LORA, dtype=torch.float32, device=dev)
+    sel_out = sel_n_out = None
+    if owner:
+        sel_out = torch.full((n_q, kk), -1, dtype=torch.int32, device=dev)
+        sel_n_out = torch.empty(n_q, dtype=torch.int32, device=dev)
+    io = PrefillIO()
+    io.n_q, io.pos0 = n_q, pos0
+    io.latent = kv.c()
+    if keys is not None:
+        io.index = keys.c()
+    io.q_abs, io.q_idx, io.w_idx = _ptr(q_abs), _ptr(q_idx), _ptr(w_idx)
+    io.sel_out, io.sel_n_out = _ptr(sel_out), _ptr(sel_n_out)
+    io.sel_stride = sel_out.stride(0) if sel_out is not None else 0
+    io.ctx = _ptr(ctx)
+    nbytes = lib().wl_attn_prefill_workspace_bytes(C.byref(cfg), n_q, T)
+    ws = workspace(nbytes, dev)
+    st = lib().wl_attn_layer_prefill(C.byref(cfg), C.byref(io), int(owner), layer, C.byref(share.c),
+                                     _ptr(ws), ws.numel(), _stream())
+    if st == _lib.WL_ERR_NO_INDICES:
+        share.require(layer)  # raises with the reference's message
+    check(st, "wl_attn_layer_prefill")
+    if owner:
+        share._keep = (sel_out, sel_n_out)
+    return dict(ctx=ctx, sel=sel_out, sel_n=sel_n_out)
+
+
 def device_error(clear: bool = True) -> tuple[int, int]:
     """(status, raw word) of the library's device-side error word."""
     w = C.c_uint32(0)

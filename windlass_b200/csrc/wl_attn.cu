@@ -1287,6 +1287,35 @@ int wl_attn_prefill(const wl_attn_cfg* cfg, const wl_attn_prefill_io* io, void* 
                        true);
 }
 
+int wl_attn_layer_prefill(const wl_attn_cfg* cfg, wl_attn_prefill_io* io, int32_t owner, uint32_t layer,
+                          wl_index_share* share, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!io || !share) return WL_ERR_ARG;
+    if (owner) {
+        if (!io->sel_out || !io->sel_n_out) return WL_ERR_ARG;  // the published rows must outlive the call
+        io->mode = WL_MODE_OWNER;
+        if (int e = wl_attn_prefill(cfg, io, workspace, workspace_bytes, stream)) return e;
+        // Publish every row's raw selection, one row per query position (the
+        // per-row index buffers of run_prefill_layer_major,
+        // glm_layer_runner.cuh:763-770, 954-983).
+        const int64_t T = (int64_t)io->pos0 + io->n_q;
+        wl_index_share_publish(share, layer, io->sel_out, io->sel_n_out, io->sel_stride,
+                               (int32_t)(cfg->index_topk < T ? cfg->index_topk : T));
+        return WL_OK;
+    }
+    if (int e = wl_index_share_require(share, layer)) return e;
+    if (share->dense) {
+        io->mode = WL_MODE_DENSE;
+    } else {
+        if (!share->n_dev) return WL_ERR_ARG;  // prefill rows carry their own counts
+        io->mode = WL_MODE_CONSUMER;
+        io->sel_in = share->idx;
+        io->sel_n_in = share->n_dev;
+        io->sel_stride = share->stride;
+        io->sel_flags = WL_SEL_CANONICAL;
+    }
+    return wl_attn_prefill(cfg, io, workspace, workspace_bytes, stream);
+}
+
 // ---- sharded decode ----------------------------------------------------------------------------
 int wl_comm_unique_id(uint8_t id_out[128]) {
     if (!id_out) return WL_ERR_ARG;
