@@ -4,14 +4,14 @@
 Contract: ``python bench.py --gpus N --steps K --warmup W`` (N > 1 under
 torchrun, one rank per GPU) prints ONE JSON line on rank 0.
 
-Workload (``config.workload``): BASELINE config 4 — one decode token for each
+Workload (``config.workload``): benchmark config 4 — one decode token for each
 of 8 independent sequences, each with a 131072-key bf16 latent cache
 [T, 576] and fp8-e4m3 index keys [T, 128] + per-key scale, top-2048, as an
 indexer-owning layer. At N GPUs every cache is split into N contiguous key
 shards (strong scaling: the same total work). A step = one layer-step of the
 substep over all 8 sequences; the metric is microseconds per layer-step.
 The caches (1.35 GB) exceed L2 (126 MB) at every N <= 8, so every step reads
-HBM. Inputs are synthetic (seeded, BASELINE's distributions), generated on the
+HBM. Inputs are synthetic (seeded, the benchmark's distributions), generated on the
 device. ``--impl reference`` times the reference's algorithm on the host cores
 (the numpy port in oracle/, since the reference's own path is numpy).
 """
@@ -205,7 +205,7 @@ def run_reference(args, rank):
         "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic (seeded, BASELINE distributions)",
+        "data": "synthetic (seeded, benchmark distributions)",
         "config": {"workload": "cfg4: decode, 8 seq x T=131072, top-2048, owner layer",
                    "batch": 8, "T": 131072, "index_topk": 2048},
         "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": cores, "kind": "port",
@@ -364,7 +364,7 @@ def main():
             "metric": METRIC, "value": round(us, 2), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5), "higher_is_better": False,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded on device, BASELINE distributions)",
+            "data": "synthetic (seeded on device, benchmark distributions)",
             "config": {"workload": "cfg4: decode, 8 seq x T=131072, top-2048, owner layer",
                        "batch": B, "T": T, "index_topk": K, "parallelism": f"kv-seq shard x{world}" + ("" if comm is None else
                                                                   (" (NVLink peer exchange)" if comm.p2p else " (NCCL)")),
@@ -477,7 +477,7 @@ def kernel_breakdown(torch, A, _lib, cfg, data, steps, stream):
 
 
 def side_configs(torch, A, _lib, device, stream):
-    """Short measurements of BASELINE configs 1, 2 and 3 on this GPU."""
+    """Short measurements of benchmark configs 1, 2 and 3 on this GPU."""
     out = {}
     L = _lib.lib()
     # decode, batch 1: config 2 (T=32768) and config 1 (T=4096), owner + consumer;

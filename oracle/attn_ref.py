@@ -29,7 +29,7 @@ function citing the reference it follows (paths inside ssubbotin/windlass):
                    and the latent row of attn_block (rms_norm + rope_interleave,
                    ref_glm_chain.py:63-106, 576-581; glm_layer_runner.cuh:
                    544-570), in the kernel's fixed summation order
-  quantize_e4m3    BASELINE's fp8 index-key format (not in the reference):
+  quantize_e4m3    the benchmark's fp8 index-key format (not in the reference):
                    e4m3 (OCP "fn", round-to-nearest-even) with one fp32 scale
                    per key = amax / 448.
 
@@ -329,7 +329,7 @@ def cache_append(k_raw, k_norm_w, k_norm_b, kv_raw, kv_norm_w, cos, sin, ln_eps=
     return out
 
 
-# ---- seeded inputs ------------------------------------------------------------
+# ---- seeded inputs (benchmark configs) ------------------------------------------------------------
 
 def rope_interleave(x: np.ndarray, pos: np.ndarray, theta: float) -> np.ndarray:
     """Interleaved-in, halves-out RoPE (ref_glm_chain.py:85-106), float64 tables."""
@@ -342,7 +342,7 @@ def rope_interleave(x: np.ndarray, pos: np.ndarray, theta: float) -> np.ndarray:
 
 
 def make_inputs(T: int, config: int, seq: int = 0, n_q: int = 1, theta: float = 1e6) -> dict:
-    """Seeded synthetic inputs with BASELINE's shapes and distributions.
+    """Seeded synthetic inputs with the benchmark's shapes and distributions.
 
     seed = 20260801 + config + 1000 * seq. c_kv ~ N(0,1) RMS-normalised per
     row; k_rot ~ N(0,1) roped at positions 0..T-1; q_abs, q_idx ~ N(0,1); all

@@ -1,6 +1,6 @@
 """Parity of the sm_100a kernels (through the C ABI) with the oracle.
 
-Tolerances, from the reference's own gates and BASELINE:
+Tolerances, from the reference's own gates and the benchmark spec:
   * index scores: max |gpu - oracle| <= 1e-5 * max|oracle| (the reference's
     fp32 indexer gate, src/test_glm_indexer.cu:167);
   * selection: bit-exact sets wherever the oracle's score is farther than that
@@ -395,7 +395,7 @@ def test_prefill_rows_vs_oracle(pos0, n_q, k):
 
 
 def test_prefill_config3_full_size_properties():
-    """BASELINE config 3 (4096 rows on a 4096-token prefix, top-2048) at full
+    """benchmark config 3 (4096 rows on a 4096-token prefix, top-2048) at full
     size: counts, causality, canonical lists; spot rows against the oracle."""
     pos0, n_q = 4096, 4096
     inp, g = _prefill_inputs(pos0, n_q, 3)
