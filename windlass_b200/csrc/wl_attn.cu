@@ -976,7 +976,8 @@ int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, in
                            static_cast<const __nv_bfloat16*>(wq_b), cos, sin, static_cast<__nv_bfloat16*>(q_idx),
                            (long long)wl::IQ_H * wl::IQ_D));
     const float head_scale = (float)(1.0 / std::sqrt((double)wl::IQ_H));
-    WL_CUDA_TRY(launch_pdl(wl::idx_head_weights_kernel, dim3(wl::IQ_H), dim3(256), 0, st, (int)n, x,
+    if (n > 65535) return WL_ERR_ARG;
+    WL_CUDA_TRY(launch_pdl(wl::idx_head_weights_kernel, dim3(wl::IQ_H, n), dim3(256), 0, st, (int)n, x,
                            (long long)x_row_stride, weights_proj, (int)hidden, head_scale, w_idx, (long long)wl::IQ_H));
     return WL_OK;
 }
