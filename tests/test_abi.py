@@ -155,3 +155,55 @@ def test_workspace_sizes_scale_with_batch_and_T():
     s = lib().wl_attn_sharded_workspace_bytes(C.byref(cfg), 4096, 8, 8)
     assert s > lib().wl_attn_workspace_bytes(C.byref(cfg), 4096, 8)
     assert lib().wl_attn_prefill_workspace_bytes(C.byref(cfg), 4096, 8192) >= 4096 * 8192 * 4
+
+
+# ---- argument checks of the entry points around the substep (no launch happens) ----
+
+def test_cache_append_argument_checks():
+    cfg = _cfg()
+    io = _lib.CacheAppendIO()
+    io.n = 0
+    assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_OK  # nothing to do
+    io.n = 4
+    assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG  # no pos / tables
+    io.pos, io.cos, io.sin = 0x1000, 0x2000, 0x3000
+    assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG  # neither part given
+    io.k_raw = 0x4008  # misaligned, and no cache / norm weights
+    assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG
+    io.n = -1
+    assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG
+    bad = _cfg()
+    bad.kv_lora = 256
+    assert lib().wl_cache_append(C.byref(bad), C.byref(io), None) == _lib.WL_ERR_UNSUPPORTED
+
+
+def test_projection_argument_checks():
+    cfg = _cfg()
+    L = lib()
+    assert L.wl_mla_absorb_q(C.byref(cfg), 0, None, 0, None, None, 0, None) == _lib.WL_OK
+    assert L.wl_mla_absorb_q(C.byref(cfg), 2, None, 64 * 256, 0x1000, 0x2000, 64 * 576, None) == _lib.WL_ERR_ARG
+    assert L.wl_mla_absorb_q(C.byref(cfg), 2, 0x1000, 100, 0x1000, 0x2000, 64 * 576, None) == _lib.WL_ERR_ARG
+    assert L.wl_mla_project_v(C.byref(cfg), 0, None, 0, None, None, 0, None) == _lib.WL_OK
+    assert L.wl_mla_project_v(C.byref(cfg), 1, 0x1000, 64 * 512, 0x2008, 0x3000, 64 * 256, None) == _lib.WL_ERR_ARG
+    assert L.wl_mla_project_v(C.byref(cfg), -1, 0x1000, 64 * 512, 0x2000, 0x3000, 64 * 256, None) == _lib.WL_ERR_ARG
+    q = dict(q_resid=0x1000, wq_b=0x2000, x=0x3000, wp=0x4000, cos=0x5000, sin=0x6000, qi=0x7000, wi=0x8000)
+    args = lambda hidden, n=1: (C.byref(cfg), n, q["q_resid"], 2048, q["wq_b"], q["x"], hidden, hidden,  # noqa: E731
+                                q["wp"], q["cos"], q["sin"], q["qi"], q["wi"], None)
+    assert L.wl_indexer_query(*args(1000)) == _lib.WL_ERR_ARG  # hidden not a multiple of 1024
+    assert L.wl_indexer_query(*args(6144, n=0)) == _lib.WL_OK
+    assert L.wl_indexer_query(C.byref(cfg), 1, None, 2048, 0x2000, 0x3000, 6144, 6144, 0x4000, 0x5000, 0x6000,
+                              0x7000, 0x8000, None) == _lib.WL_ERR_ARG
+
+
+def test_layer_prefill_requires_a_published_share():
+    from windlass_b200._lib import PrefillIO
+    cfg = _cfg()
+    s = IndexShareC()
+    lib().wl_index_share_reset(C.byref(s))
+    io = PrefillIO()
+    io.n_q, io.pos0 = 4, 100
+    assert lib().wl_attn_layer_prefill(C.byref(cfg), C.byref(io), 0, 3, C.byref(s), None, 0, None) \
+        == _lib.WL_ERR_NO_INDICES
+    # an owner must name the buffers it publishes
+    assert lib().wl_attn_layer_prefill(C.byref(cfg), C.byref(io), 1, 3, C.byref(s), None, 0, None) \
+        == _lib.WL_ERR_ARG
