@@ -207,3 +207,44 @@ def test_layer_prefill_requires_a_published_share():
     # an owner must name the buffers it publishes
     assert lib().wl_attn_layer_prefill(C.byref(cfg), C.byref(io), 1, 3, C.byref(s), None, 0, None) \
         == _lib.WL_ERR_ARG
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """The boundary is a C ABI: include/wl_attn.h compiles as C99, and a C
+    program links against libwl_attn.so and runs its host-only calls."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "probe.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include <string.h>
+#include "wl_attn.h"
+int main(void) {
+    wl_attn_cfg cfg;
+    wl_attn_cfg_glm52(&cfg, 4096);
+    if (cfg.n_heads != 64 || cfg.kv_lora != 512 || cfg.index_topk != 2048) return 1;
+    if (strcmp(wl_strerror(WL_OK), "unknown status") == 0) return 2;
+    wl_index_share s;
+    memset(&s, 0, sizeof s);
+    wl_index_share_reset(&s);
+    if (wl_index_share_require(&s, 3) != WL_ERR_NO_INDICES) return 3;
+    wl_index_share_publish(&s, 0, (const int32_t*)0x100, NULL, 8, 8);
+    if (wl_index_share_require(&s, 3) != WL_OK || s.producer != 0) return 4;
+    wl_cache_append_io a;
+    memset(&a, 0, sizeof a);
+    a.n = 1;
+    if (wl_cache_append(&cfg, &a, NULL) != WL_ERR_ARG) return 5;
+    if (wl_abi_version() != WL_ABI_VERSION) return 6;
+    printf("ok\n");
+    return 0;
+}
+""")
+    exe = tmp_path / "probe"
+    libdir = os.path.join(ROOT, "windlass_b200")
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src), "-L", libdir,
+                    "-l:libwl_attn.so", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0 and out.stdout.strip() == "ok", (out.returncode, out.stdout, out.stderr)
