@@ -4,6 +4,7 @@ beyond a final line; the inputs are the bench's seeded synthetic ones.
 
     python -m windlass_b200.profile_case --case decode --batch 1 --T 32768 --iters 3
     python -m windlass_b200.profile_case --case prefill --pos0 1024 --n_q 1024 --iters 2
+    python -m windlass_b200.profile_case --case around --batch 8 --iters 3
 """
 from __future__ import annotations
 
@@ -18,7 +19,7 @@ if ROOT not in sys.path:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["decode", "consumer", "prefill"], default="decode")
+    ap.add_argument("--case", choices=["decode", "consumer", "prefill", "around"], default="decode")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--T", type=int, default=32768)
     ap.add_argument("--pos0", type=int, default=1024)
@@ -34,7 +35,32 @@ def main() -> None:
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    if a.case == "prefill":
+    if a.case == "around":
+        # the entry points either side of the substep, at a decode batch
+        cfg = A.glm52_cfg(8192)
+        g = torch.Generator(device=dev)
+        g.manual_seed(11)
+        B = a.batch
+        kvb = (torch.randn(64 * 448, 512, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        wq = (torch.randn(4096, 2048, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        wp = torch.randn(32, 6144, device=dev, generator=g) * 0.02
+        q, ctx = torch.randn(B, 64, 256, device=dev, generator=g), torch.randn(B, 64, 512, device=dev, generator=g)
+        qr, xh = torch.randn(B, 2048, device=dev, generator=g), torch.randn(B, 6144, device=dev, generator=g)
+        cs, sn = torch.rand(B, 32, device=dev, generator=g), torch.rand(B, 32, device=dev, generator=g)
+        keys = A.IndexKeys(torch.zeros(B, 8192, 128, dtype=torch.uint8, device=dev),
+                           torch.zeros(B, 8192, dtype=torch.float32, device=dev))
+        kv = A.LatentKV.packed(torch.zeros(B, 8192, 576, dtype=torch.bfloat16, device=dev))
+        pos = torch.full((B,), 8191, dtype=torch.int32, device=dev)
+        seq = torch.arange(B, dtype=torch.int32, device=dev)
+        ones = torch.ones(512, dtype=torch.bfloat16, device=dev)
+        for _ in range(a.iters):
+            A.indexer_query(cfg, qr, wq, xh, wp, cs, sn)
+            A.cache_append(cfg, pos, cs, sn, keys=keys, k_raw=torch.randn(B, 128, device=dev, generator=g),
+                           k_norm_w=ones[:128], k_norm_b=torch.zeros_like(ones[:128]), kv=kv,
+                           kv_raw=torch.randn(B, 576, device=dev, generator=g), kv_norm_w=ones, seq=seq)
+            A.mla_absorb_q(cfg, q, kvb)
+            A.mla_project_v(cfg, ctx, kvb)
+    elif a.case == "prefill":
         T = a.pos0 + a.n_q
         cfg = A.glm52_cfg(T)
         d = make_device_inputs(torch, 1, T, 0, 20260803, dev, n_q=a.n_q)
