@@ -19,11 +19,11 @@ namespace wl {
 
 constexpr int IQ_H = 32, IQ_D = 128, IQ_ROT = 64, IQ_QL = 2048;
 constexpr int IQ_ROWS = 8;        // query rows per chunk
-constexpr int IQ_DIMS = 16;       // output dims per CTA, one per warp
+constexpr int IQ_DIMS = 8;        // output dims per CTA, one per warp
 constexpr int IQ_THREADS = 32 * IQ_DIMS;
 constexpr uint32_t IQ_SMEM = IQ_ROWS * IQ_QL * 4 + IQ_ROWS * IQ_DIMS * 4;  // q_resid rows + dot products
 
-// grid (32 * 128 / 16). Warp w owns output dim o = 16 b + w with its weight
+// grid (32 * 128 / IQ_DIMS). Warp w owns output dim o = IQ_DIMS b + w with its weight
 // row in registers (lane l: columns 8 l + 256 j, j < 8); per query row the
 // lane partials are summed by a xor butterfly into shared memory, then the
 // CTA applies RoPE to the pairs (o, o + 1) with o % 128 < 64 and stores bf16.
