@@ -141,6 +141,21 @@ def test_cache_append_negative_control_layernorm_bias():
     assert rel(g["ref_key"], r["key_f32"]) > 1e-3
 
 
+def test_cache_append_zero_key_gets_unit_scale():
+    """A key whose LayerNorm output is all zero (zero weight, zero bias) is
+    stored as e4m3 zeros with scale 1 (the format's amax = 0 rule)."""
+    rng = np.random.default_rng(3)
+    r = o.cache_append(rng.standard_normal((2, 128)).astype(np.float32), np.zeros(128, np.float32),
+                       np.zeros(128, np.float32), rng.standard_normal((2, 576)).astype(np.float32),
+                       np.ones(512, np.float32), np.ones((2, 32), np.float32), np.zeros((2, 32), np.float32))
+    assert np.all(r["idx_bits"] == 0) and np.all(r["idx_scale"] == 1.0)
+    # RoPE at angle 0 (cos 1, sin 0) only moves the pairs into the halves layout
+    x = rng.standard_normal((2, 576)).astype(np.float32)
+    r = o.cache_append(np.zeros((2, 128), np.float32), np.ones(128, np.float32), np.zeros(128, np.float32), x,
+                       np.ones(512, np.float32), np.ones((2, 32), np.float32), np.zeros((2, 32), np.float32))
+    assert np.array_equal(r["k_rot_f32"], np.concatenate([x[:, 512::2], x[:, 513::2]], -1))
+
+
 # ---- pin 4: the indexer's query side (indexer_scores' q and w) ----
 
 def test_indexer_query_matches_reference_fixture():
