@@ -149,58 +149,84 @@ def elapsed_ms(torch, fn, steps, stream):
 
 
 # ---- the reference arm (host cores) --------------------------------------------------------------
-def cpu_sample_inputs(T, seed):
-    from oracle import attn_ref as o
-    return o.make_inputs(T, 4, seq=seed)
-
-
-def cpu_step(inp, k):
-    """One sequence of the workload through the reference's algorithm (numpy,
-    fp32 like tools/ref_glm_chain.py)."""
-    from oracle import attn_ref as o
-    return o.decode_step(inp, k, dtype=np.float32)
-
-
-def cpu_threads() -> int:
+def host_threads() -> int:
+    """Host cores this process may use (the same at every N: torch.distributed.run
+    sets OMP_NUM_THREADS=1 for its ranks, which is not the reference's setting)."""
     try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else 1
+        return len(os.sched_getaffinity(0))
     except Exception:
         return os.cpu_count() or 1
 
 
-def time_cpu(budget_s: float, max_steps: int | None = None):
-    """Time whole sequences of the workload on the host until the budget is spent."""
-    inp = cpu_sample_inputs(CFG4["T"], 0)
-    cpu_step(inp, CFG4["k"])  # warm
+def cpu_sample_inputs(T, batch, pool=None):
+    from oracle import attn_ref as o
+    gen = lambda s: o.make_inputs(T, 4, seq=s)  # noqa: E731
+    return list(pool.map(gen, range(batch))) if pool is not None else [gen(s) for s in range(batch)]
+
+
+def cpu_step(inps, k, pool):
+    """One layer-step of the workload through the reference's algorithm (numpy,
+    fp32 like tools/ref_glm_chain.py): every sequence of the batch, the
+    sequences spread over a thread pool (numpy releases the GIL in its
+    kernels; each worker's BLAS gets an equal share of the cores)."""
+    from oracle import attn_ref as o
+    return list(pool.map(lambda inp: o.decode_step(inp, k, dtype=np.float32), inps))
+
+
+class CpuArm:
+    """The reference's CPU path for config 4 with every host core in use."""
+
+    def __init__(self, batch):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from threadpoolctl import threadpool_limits
+        self.cores = host_threads()
+        self.workers = max(1, min(batch, self.cores))
+        self.limits = threadpool_limits(max(1, self.cores // self.workers))
+        self.pool = ThreadPoolExecutor(self.workers)
+        self.inps = cpu_sample_inputs(CFG4["T"], batch, self.pool)
+
+    def step(self):
+        cpu_step(self.inps, CFG4["k"], self.pool)
+
+    def close(self):
+        self.pool.shutdown()
+        self.limits.restore_original_limits()
+
+    def describe(self, steps):
+        return (f"{steps} steps x all {len(self.inps)} sequences (T=131072, top-2048) through oracle/attn_ref.py "
+                f"(numpy fp32), {self.workers} sequences in parallel x {max(1, self.cores // self.workers)} "
+                f"BLAS threads on {self.cores} host cores")
+
+
+def time_cpu(budget_s: float):
+    """Whole layer-steps (all 8 sequences) of the workload on the host until the budget is spent."""
+    arm = CpuArm(CFG4["batch"])
+    arm.step()  # warm
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_step(inp, CFG4["k"])
+        arm.step()
         n += 1
         el = time.perf_counter() - t0
-        if el >= budget_s or (max_steps and n >= max_steps):
+        if el >= budget_s:
             break
-    per_seq_us = el / n * 1e6
-    return per_seq_us * CFG4["batch"], n
+    arm.close()
+    return el / n * 1e6, n, arm
 
 
 def run_reference(args, rank):
     if rank != 0:
         return
-    # every step: one whole sequence (a bounded sample of the 8-sequence step), x8
-    inp = cpu_sample_inputs(CFG4["T"], 0)
+    arm = CpuArm(CFG4["batch"])
     for _ in range(max(args.warmup, 1)):
-        cpu_step(inp, CFG4["k"])
+        arm.step()
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        cpu_step(inp, CFG4["k"])
+        arm.step()
         times.append(time.perf_counter() - t0)
-    us = statistics.mean(times) * 1e6 * CFG4["batch"]
-    cores = cpu_threads()
-    sample = (f"1 of the 8 sequences (T=131072, top-2048) per step through oracle/attn_ref.py "
-              f"(numpy fp32), scaled x8; {args.steps} steps")
+    arm.close()
+    us = statistics.mean(times) * 1e6
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "us/layer",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3),
@@ -208,10 +234,124 @@ def run_reference(args, rank):
         "data": "synthetic (seeded, benchmark distributions)",
         "config": {"workload": "cfg4: decode, 8 seq x T=131072, top-2048, owner layer",
                    "batch": 8, "T": 131072, "index_topk": 2048},
-        "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": cores, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/layer", "cores": arm.cores, "kind": "port",
+                         "sample": arm.describe(args.steps)},
         "e2e": {"value": round(us, 1), "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+
+# ---- diagnostics run beside the timed region --------------------------------------------------
+PHASES_P2P = ["indexer", "local_topk", "cand_exchange", "global_topk", "attention", "reduce_scatter",
+              "all_gather", "unpack"]
+PHASES_NCCL = ["indexer", "local_topk", "cand_exchange", "global_topk", "attention", "local_merge",
+               "all_gather", "merge"]
+PHASES_1GPU = ["indexer", "topk", "attention", "merge"]
+
+
+def phase_breakdown(torch, L, step, device, names, reps=20):
+    """Per-phase device time of one layer-step (median over graph replays), from
+    the library's global-timer stamps at its phase boundaries. The stamp
+    launches break the overlap between phases, so the phases sum to a little
+    more than the unstamped step."""
+    buf = torch.zeros(64, dtype=torch.int64, device=device)
+    L.wl_diag_phase_stamps(buf.data_ptr(), 64)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        n = L.wl_diag_phase_count()
+    finally:
+        L.wl_diag_phase_stamps(None, 0)
+    rows = []
+    for _ in range(reps + 2):
+        g.replay()
+        torch.cuda.synchronize()
+        t = buf[:n].cpu().numpy().astype(np.float64)
+        rows.append(np.diff(t) * 1e-3)
+    d = np.median(np.array(rows[2:]), axis=0)
+    names = names if len(names) == len(d) else [f"phase{i}" for i in range(len(d))]
+    return {k: round(float(v), 2) for k, v in zip(names, d)}
+
+
+def single_layer_us(torch, step, reps=20):
+    """One eager call of the entry point, alone (synchronised on both sides):
+    launch latency included, no graph."""
+    ts = []
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3)
+    return round(float(np.median(ts)), 2)
+
+
+def check_parity(torch, dist, A, _lib, cfg, data, sel, sel_n, ctx, lse, rank, world, seqs=(0, 1)):
+    """The step's own outputs against the oracle on the same inputs: every rank's
+    shard of sequences `seqs` is gathered to rank 0, which recomputes them on
+    the host (oracle/attn_ref.py) and, at N > 1, on one GPU through
+    wl_attn_decode. Returns (ok, summary) on rank 0, (True, None) elsewhere."""
+    from oracle import attn_ref as o
+    K = CFG4["k"]
+    tol_rel = 1e-5  # the indexer's score tolerance (the reference's fp32 gate)
+    res = {"checked": True, "seqs": list(seqs), "max_ulp": 0.0, "max_ulp_oracle_sel": 0.0, "max_lse_err": 0.0,
+           "sel_mismatch": 0, "sel_in_gap": 0}
+    if world > 1:
+        res.update(single_gpu_sel_equal=True, max_ulp_vs_single_gpu=0.0)
+    sel_c, n_c, ctx_c, lse_c = (t.cpu().numpy() for t in (sel, sel_n, ctx, lse))
+    for s in seqs:
+        parts = [data["kv_raw"][s].contiguous(), data["keys"].keys[s].contiguous(), data["keys"].scale[s].contiguous()]
+        if world > 1:
+            full = []
+            for t in parts:
+                lst = [torch.empty_like(t) for _ in range(world)]
+                dist.all_gather(lst, t)
+                full.append(torch.cat(lst, 0))
+            parts = full
+        if rank != 0:
+            continue
+        kv, bits, scale = parts
+        inp = dict(c_kv=kv[:, :512].float().cpu().numpy(), k_rot=kv[:, 512:].float().cpu().numpy(),
+                   q_abs=data["q_abs"][s].float().cpu().numpy(), q_idx=data["q_idx"][s].float().cpu().numpy(),
+                   w_idx=data["w_idx"][s].cpu().numpy(), idx_bits=bits.cpu().numpy(),
+                   idx_scale=scale.cpu().numpy(), scale=1.0 / 16.0)
+        g_sel = sel_c[s, :int(n_c[s])]
+        ref_index = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+        ref_sel = o.indexer_topk(ref_index, K)
+        thr = np.sort(ref_index)[::-1][K - 1]
+        tol = tol_rel * np.abs(ref_index).max()
+        diff = set(ref_sel.tolist()) ^ set(g_sel.tolist())
+        far = [t for t in diff if abs(ref_index[t] - thr) > tol]
+        canonical = len(g_sel) == K and bool(np.all(np.diff(g_sel) > 0))
+        res["sel_mismatch"] += len(far) + (0 if canonical else 1)
+        res["sel_in_gap"] += len(diff) - len(far)
+        rc, rl = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], g_sel, 1 / 16)
+        res["max_ulp"] = max(res["max_ulp"], o.bf16_ulp_error(rc, ctx_c[s]))
+        res["max_lse_err"] = max(res["max_lse_err"], float(np.abs(lse_c[s] - rl).max()))
+        fc, _ = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], np.sort(ref_sel), 1 / 16)
+        res["max_ulp_oracle_sel"] = max(res["max_ulp_oracle_sel"], o.bf16_ulp_error(fc, ctx_c[s]))
+        if world > 1:
+            one = A.attn_decode(A.glm52_cfg(kv.shape[0]), A.LatentKV.packed(kv[None]), data["q_abs"][s:s + 1],
+                                keys=A.IndexKeys(bits[None], scale[None]), q_idx=data["q_idx"][s:s + 1],
+                                w_idx=data["w_idx"][s:s + 1])
+            torch.cuda.synchronize()
+            s1 = one["sel"].cpu().numpy()[0]
+            res["single_gpu_sel_equal"] &= bool(np.array_equal(s1, g_sel))
+            res["max_ulp_vs_single_gpu"] = max(res["max_ulp_vs_single_gpu"],
+                                               o.bf16_ulp_error(one["ctx"].cpu().numpy()[0], ctx_c[s]))
+    if rank != 0:
+        return True, None
+    for k in ("max_ulp", "max_ulp_oracle_sel", "max_lse_err", "max_ulp_vs_single_gpu"):
+        if k in res:
+            res[k] = round(float(res[k]), 4)
+    ok = (res["sel_mismatch"] == 0 and res["max_ulp"] <= 2.0 and res["max_lse_err"] < 1e-3
+          and res["max_ulp_oracle_sel"] <= 2.0 and res.get("single_gpu_sel_equal", True)
+          and res.get("max_ulp_vs_single_gpu", 0.0) <= 2.0)
+    res["ok"] = bool(ok)
+    return ok, res
 
 
 # ---- our arm ------------------------------------------------------------------------------------
@@ -340,6 +480,26 @@ def main():
     h2d = sum(h.numel() * h.element_size() for h in h_q)
     d2h = h_ctx.numel() * 4 + h_sel.numel() * 4
 
+    # ---- outside the timed regions: phase breakdown, un-graphed latency, self-check ----
+    names = (PHASES_P2P if comm.p2p else PHASES_NCCL) if comm is not None else PHASES_1GPU
+    phases = phase_breakdown(torch, L, step, device, names)
+    if world > 1:
+        pv = torch.tensor(list(phases.values()), device=device)
+        dist.all_reduce(pv, op=dist.ReduceOp.MAX)
+        phases = {k: round(float(v), 2) for k, v in zip(phases, pv.tolist())}
+    single_us = single_layer_us(torch, step)
+    if world > 1:
+        su = torch.tensor([single_us], device=device)
+        dist.all_reduce(su, op=dist.ReduceOp.MAX)
+        single_us = round(su.item(), 2)
+    step()
+    torch.cuda.synchronize()
+    par_ok, parity = check_parity(torch, dist, A, _lib, cfg, data, sel, sel_n, ctx, lse, rank, world)
+    if world > 1:
+        okt = torch.tensor([1 if par_ok else 0], device=device)
+        dist.broadcast(okt, 0)
+        par_ok = bool(okt.item())
+
     # ---- per-kernel breakdown through the individual entry points (roofline) ----
     roof = None
     breakdown = None
@@ -356,10 +516,9 @@ def main():
     if rank == 0:
         cpu = None
         if world == 1:
-            cpu_us, n = time_cpu(args.cpu_seconds)
-            cpu = {"value": round(cpu_us, 1), "unit": "us/layer", "cores": cpu_threads(), "kind": "port",
-                   "sample": f"{n} x 1 of the 8 sequences (T=131072, top-2048) through oracle/attn_ref.py "
-                             f"(numpy fp32), scaled x8"}
+            cpu_us, n, arm = time_cpu(args.cpu_seconds)
+            cpu = {"value": round(cpu_us, 1), "unit": "us/layer", "cores": arm.cores, "kind": "port",
+                   "sample": arm.describe(n)}
         line = {
             "metric": METRIC, "value": round(us, 2), "unit": "us/layer", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5), "higher_is_better": False,
@@ -376,6 +535,9 @@ def main():
             "clocks": clk,
             "roofline": roof,
             "kernels_us": breakdown,
+            "phases_us": phases,
+            "single_layer_us": single_us,
+            "parity": parity,
             "cpu_baseline": cpu,
             "extras": extras,
         }
@@ -389,7 +551,9 @@ def main():
         dist.barrier()
         sys.stdout.flush()
         sys.stderr.flush()
-        os._exit(0)
+        os._exit(0 if par_ok else 1)
+    if not par_ok:
+        sys.exit(1)
 
 
 def load_peaks():
@@ -477,12 +641,16 @@ def kernel_breakdown(torch, A, _lib, cfg, data, steps, stream):
 
 
 def side_configs(torch, A, _lib, device, stream):
-    """Short measurements of benchmark configs 1, 2 and 3 on this GPU."""
+    """Short measurements of benchmark configs 0, 1, 2 (decode, batch 1) and 3 (prefill) on this GPU."""
     out = {}
     L = _lib.lib()
     # decode, batch 1: config 2 (T=32768) and config 1 (T=4096), owner + consumer;
     # enough cache instances that each step reads HBM (> 2x L2 in total).
-    for name, T in (("cfg2_decode_32k", 32768), ("cfg1_decode_4k", 4096)):
+    peaks = load_peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    src = "fallback" if peaks.get("fallback") else "measured"
+    qbytes = 64 * 576 * 2 + 32 * 128 * 2 + 32 * 4 + 64 * 512 * 4 + 64 * 4  # queries in, ctx + lse out
+    for name, T in (("cfg2_decode_32k", 32768), ("cfg1_decode_4k", 4096), ("cfg0_decode_1k", 1024)):
         per = T * (1152 + 132)
         n_inst = max(2, int(np.ceil(300e6 / per)))
         cfg = A.glm52_cfg(T)
@@ -515,10 +683,16 @@ def side_configs(torch, A, _lib, device, stream):
             reps = 20
             ms = elapsed_ms(torch, lambda i: g.replay(), reps, stream)
             us = ms / (reps * n_inst) * 1e3
-            algo = (T * 132 if mode == 0 else 0) + min(2048, T) * 1152
-            res["owner" if mode == 0 else "consumer"] = {"us_per_layer": round(us, 2),
-                                                         "algo_bytes": algo,
-                                                         "achieved_gbs": round(algo / (us * 1e-6) / 1e9, 1)}
+            algo = (T * 132 if mode == 0 else 0) + min(2048, T) * 1152 + qbytes
+            gbs = algo / (us * 1e-6) / 1e9
+            ent = {"us_per_layer": round(us, 2), "algo_bytes": algo, "tokens_per_s": round(1e6 / us, 1),
+                   "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                "frac": round(gbs / hbm, 4), "peak_source": src}}
+            f0 = fns[0]
+            ent["single_layer_us"] = single_layer_us(torch, f0)
+            ent["phases_us"] = phase_breakdown(torch, L, f0, device,
+                                               PHASES_1GPU if mode == 0 else PHASES_1GPU[2:])
+            res["owner" if mode == 0 else "consumer"] = ent
         out[name] = res
         del insts, ios
         torch.cuda.empty_cache()
@@ -535,8 +709,12 @@ def side_configs(torch, A, _lib, device, stream):
     ms = elapsed_ms(torch, fn, 5, stream) / 5
     idx_flops = 2 * 32 * 128 * sum(pos0 + 1 + i for i in range(n_q))
     att_flops = n_q * 2048 * 64 * (2 * 576 + 2 * 512)
-    out["cfg3_prefill"] = {"ms": round(ms, 3), "tflops": round((idx_flops + att_flops) / (ms * 1e-3) / 1e12, 1),
-                           "idx_gflop": round(idx_flops / 1e9, 1), "attn_gflop": round(att_flops / 1e9, 1)}
+    tf = (idx_flops + att_flops) / (ms * 1e-3) / 1e12
+    pk = peaks.get("bf16_tflops", 1590.0)
+    out["cfg3_prefill"] = {"ms": round(ms, 3), "tflops": round(tf, 1),
+                           "idx_gflop": round(idx_flops / 1e9, 1), "attn_gflop": round(att_flops / 1e9, 1),
+                           "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk, "unit": "TFLOP/s",
+                                        "frac": round(tf / pk, 4), "peak_source": src + " bf16 burst"}}
     del d
     torch.cuda.empty_cache()
     out["around"] = around_kernels(torch, A, device, stream)

@@ -247,11 +247,13 @@ int wl_sel_normalize(const int32_t* sel_in, int64_t in_stride,
 
 /* a7: sparse absorbed-MLA attention over canonical lists (NULL = every key),
  * restricted to the key window [win_lo, win_hi) whose first key is cache row 0,
- * split into CTAs of `split_keys` selected keys (multiple of 128; 0 = the whole
+ * split into CTAs of `split_keys` selected keys (multiple of 64; 0 = the whole
  * list in one CTA). Writes per split the normalised partial output and its
  * log-sum-exp: o_part[(r*max_splits + s)*n_heads*kv_lora ...],
- * lse_part[(r*max_splits + s)*n_heads ...]. Replaces mla_decode_absorbed
- * (glm_layer_runner.cuh:251-298) with its mask (glm_kernels.cuh:526-545). */
+ * lse_part[(r*max_splits + s)*n_heads ...]. A split with no keys writes lse =
+ * -inf only and leaves its o untouched (wl_lse_merge never reads it).
+ * Replaces mla_decode_absorbed (glm_layer_runner.cuh:251-298) with its mask
+ * (glm_kernels.cuh:526-545). */
 int wl_mla_sparse_attn(const wl_attn_cfg* cfg, const wl_latent_cache* cache,
                        int32_t T, const wl_rows* rows, const void* q_abs,
                        const int32_t* sel, int64_t sel_stride,
@@ -273,14 +275,17 @@ int wl_lse_merge(const float* o_part, const float* lse_part, int32_t n_rows,
  * Rank r holds keys [t0, t0 + io->T) of every cache. Each rank scores and
  * selects locally; an all-gather of the (score, global index) candidates
  * gives every rank the exact single-GPU selection, each rank attends over its
- * part of it, and a second all-gather merges the (o, lse) partials. Every
- * rank returns the full ctx/lse and (owner) the global selection. No reference
- * counterpart: the reference is single-GPU (README.md:88).
+ * part of it, and the (o, lse) partials are combined: over peer memory as a
+ * reduce-scatter by heads (each rank merges 64/N heads of every row) and an
+ * all-gather of the merged slices; over NCCL as an all-gather of the partials
+ * and a merge on every rank. Every rank returns the full ctx/lse and (owner)
+ * the global selection. No reference counterpart: the reference is
+ * single-GPU (README.md:88).
  * The all-gathers run over NVLink peer memory (each rank writes into every
  * rank's exchange region; wl_comm_create maps them, collectively, through CUDA
- * IPC), or over NCCL when that is unavailable, disabled (WL_NO_P2P=1) or a call
- * exceeds the regions' capacity (32 rows, index_topk 4096). Creation and
- * destruction are collective. */
+ * IPC; N must divide 64), or over NCCL when that is unavailable, disabled
+ * (WL_NO_P2P=1) or a call exceeds the regions' capacity (32 rows,
+ * index_topk 4096). Creation and destruction are collective. */
 typedef struct wl_comm wl_comm;
 int wl_comm_unique_id(uint8_t id_out[128]);
 int wl_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank,
@@ -363,7 +368,8 @@ int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_
  * cos/sin [n][rope_dim/2] (the caller's table, as in the reference).
  * Replaces launch_indexer_key (glm_kernels.cuh:432-448) and the latent row
  * write of run_attention (glm_layer_runner.cuh:544-570). Rows outside
- * [0, cfg->T_max) set the device error word and are skipped. The caches'
+ * [0, cfg->T_max), and sequences outside [0, n_seq), set the device error
+ * word and are skipped. The caches'
  * pointers are written through (their `const` is the readers' view). */
 typedef struct wl_cache_append_io {
     int32_t n;                  /* tokens                                      */
@@ -380,6 +386,8 @@ typedef struct wl_cache_append_io {
     const void*  kv_norm_w;     /* device bf16 [kv_lora] kv_a_layernorm weight */
     float        rms_eps;       /* 1e-6 (LORA_NORM_EPS)                        */
     wl_latent_cache latent;
+    int32_t n_seq;              /* sequences the caches hold: every seq[i] must
+                                   lie in [0, n_seq); 1 when seq is NULL        */
 } wl_cache_append_io;
 
 int wl_cache_append(const wl_attn_cfg* cfg, const wl_cache_append_io* io, void* stream);
@@ -390,6 +398,38 @@ int wl_cache_append(const wl_attn_cfg* cfg, const wl_cache_append_io* io, void* 
  * Synchronises the device. `clear` resets it to 0. Returns the WL_ERR_* code
  * (WL_OK when clean); *detail (may be NULL) receives the raw word. */
 int wl_device_error(int32_t clear, uint32_t* detail);
+
+/* Limit of every bounded device-side wait of this library on the current
+ * device, in SM clock cycles (about 1 s by default; <= 0 restores the
+ * default). Waits that run past it set the device error word (read by
+ * wl_device_error as WL_ERR_TIMEOUT) and unwind; tests shorten it to make a
+ * wait run out without hanging anything. */
+int wl_diag_set_wait_limit(int64_t cycles);
+
+/* Phase timeline of wl_attn_decode and wl_attn_decode_sharded. With a device
+ * buffer set, every later call (or graph replay of one captured meanwhile)
+ * writes the global timer (ns) into dev_buf[i] at its i-th phase boundary, up
+ * to `cap` stamps in all; wl_diag_phase_count returns how many were issued
+ * since the buffer was set. NULL turns stamping off. Boundaries of
+ * wl_attn_decode: start | indexer | top-k | attention | merge (owner; a
+ * consumer has no indexer or top-k stamps). Of wl_attn_decode_sharded over
+ * peer memory: start | indexer | local top-k | candidate exchange | global
+ * top-k | attention | (o, lse) reduce-scatter | all-gather | unpack; over
+ * NCCL: start | indexer | local top-k | candidate exchange | global top-k |
+ * attention | local merge | all-gather | merge. Stamping adds one tiny launch per
+ * boundary and breaks the overlap between phases: a diagnostic, not a
+ * measurement of the unstamped step. Not thread-safe across concurrent calls. */
+int wl_diag_phase_stamps(uint64_t* dev_buf, int32_t cap);
+int32_t wl_diag_phase_count(void);
+
+/* The final (o, lse) merge of the sharded decode, run over a caller-provided
+ * region in the peer-exchange wire format (8-byte words {payload, epoch}; part
+ * s of row r at word s*slot_words + r*(64*512+64), its lse 64*512 words
+ * further) with the epoch read from *epoch_ctr (device). Test hook for the
+ * exchange's consumer: words whose epoch never matches make its bounded waits
+ * run out. */
+int wl_diag_merge_exchange(const void* region, int64_t slot_words, const uint32_t* epoch_ctr, int32_t n_rows,
+                           int32_t n_parts, float* ctx, float* lse, void* stream);
 
 /* sizeof of each public struct, for binding checks: fills up to n entries in
  * the order cfg, latent_cache, index_cache, rows, index_share, decode_io,

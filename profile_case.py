@@ -2,9 +2,9 @@
 profilers (ncu launch lists and per-kernel captures). No timing, no output
 beyond a final line; the inputs are the bench's seeded synthetic ones.
 
-    python -m windlass_b200.profile_case --case decode --batch 1 --T 32768 --iters 3
-    python -m windlass_b200.profile_case --case prefill --pos0 1024 --n_q 1024 --iters 2
-    python -m windlass_b200.profile_case --case around --batch 8 --iters 3
+    python profile_case.py --case decode --batch 1 --T 32768 --iters 3
+    python profile_case.py --case prefill --pos0 1024 --n_q 1024 --iters 2
+    python profile_case.py --case around --batch 8 --iters 3
 """
 from __future__ import annotations
 
@@ -12,7 +12,7 @@ import argparse
 import os
 import sys
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 

@@ -168,6 +168,12 @@ def test_cache_append_argument_checks():
     assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG  # no pos / tables
     io.pos, io.cos, io.sin = 0x1000, 0x2000, 0x3000
     assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG  # neither part given
+    io.k_raw = 0x4000
+    io.n_seq = 0  # the caches must hold at least one sequence
+    assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG
+    io.seq, io.n_seq = None, 2  # without a sequence list there is exactly one
+    assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG
+    io.n_seq = 1
     io.k_raw = 0x4008  # misaligned, and no cache / norm weights
     assert lib().wl_cache_append(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_ARG
     io.n = -1
@@ -248,3 +254,27 @@ int main(void) {
                     "-l:libwl_attn.so", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0 and out.stdout.strip() == "ok", (out.returncode, out.stdout, out.stderr)
+
+
+def test_noalloc_rejections_happen_before_any_device_work():
+    """wl_attn_decode_noalloc refuses, with WL_ERR_UNSUPPORTED, the two modes
+    that would need scratch beyond its fixed array (an owner layer's indexer
+    and top-k; normalising a non-canonical list), and batches past its
+    maximum with WL_ERR_WORKSPACE — all before touching the GPU."""
+    cfg = _cfg()
+    io = _lib.DecodeIO()
+    io.batch, io.T = 1, 100
+    io.q_abs, io.ctx = 0x1000, 0x2000
+    io.mode = _lib.WL_MODE_OWNER
+    io.q_idx, io.w_idx = 0x3000, 0x4000
+    io.index.keys, io.index.scale = 0x5000, 0x6000
+    L = lib()
+    assert L.wl_attn_decode_noalloc(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_UNSUPPORTED
+    io.mode = _lib.WL_MODE_CONSUMER
+    io.sel_in, io.sel_n, io.sel_stride, io.sel_flags = 0x7000, 10, 10, 0
+    assert L.wl_attn_decode_noalloc(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_UNSUPPORTED
+    io.sel_flags = _lib.WL_SEL_CANONICAL
+    io.batch = 5
+    assert L.wl_attn_decode_noalloc(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_WORKSPACE
+    io.sel_in = None  # a consumer with nothing to consume
+    assert L.wl_attn_decode_noalloc(C.byref(cfg), C.byref(io), None) == _lib.WL_ERR_NO_INDICES

@@ -334,6 +334,50 @@ def test_batched_decode_eight_sequences():
         assert_sel_close(sel, ref_index, 2048, IDX_TOL * np.abs(ref_index).max())
 
 
+def test_config4_full_size_owner_step():
+    """Benchmark config 4 exactly as bench.py runs it: 8 sequences x 131072
+    keys, top-2048, an owner layer through wl_attn_decode (indexer with the
+    fused row histogram, then the 8-CTA cluster top-k, split-K attention and
+    merge). Every sequence: selection canonical and within the score-gap
+    tolerance of the oracle's, ctx within 2 bf16 ulp of the oracle over the
+    GPU's selection; two sequences also end to end (index scores, the
+    oracle's own selection, lse)."""
+    T, B = 131072, 8
+    inps = [o.make_inputs(T, 4, seq=s) for s in range(B)]
+    kv = torch.empty(B, T, 576, dtype=torch.bfloat16, device="cuda")
+    bits = torch.empty(B, T, 128, dtype=torch.uint8, device="cuda")
+    scale = torch.empty(B, T, dtype=torch.float32, device="cuda")
+    for s, inp in enumerate(inps):
+        kv[s, :, :512] = dev(inp["c_kv"], torch.bfloat16)
+        kv[s, :, 512:] = dev(inp["k_rot"], torch.bfloat16)
+        bits[s] = dev(inp["idx_bits"], torch.uint8)
+        scale[s] = dev(inp["idx_scale"], torch.float32)
+    q_abs = dev(np.stack([i["q_abs"] for i in inps]), torch.bfloat16)
+    q_idx = dev(np.stack([i["q_idx"] for i in inps]), torch.bfloat16)
+    w_idx = dev(np.stack([i["w_idx"] for i in inps]), torch.float32)
+    cfg = A.glm52_cfg(T)
+    index_out = torch.empty(B, T, dtype=torch.float32, device="cuda")
+    out = A.attn_decode(cfg, A.LatentKV.packed(kv), q_abs, keys=A.IndexKeys(bits, scale), q_idx=q_idx,
+                        w_idx=w_idx, index_out=index_out)
+    torch.cuda.synchronize()
+    sel_all, ctx_all, lse_all = cpu(out["sel"]), cpu(out["ctx"]), cpu(out["lse"])
+    assert np.all(cpu(out["sel_n"]) == 2048)
+    for s, inp in enumerate(inps):
+        sel = sel_all[s]
+        canonical_ok(sel, 2048, T)
+        ref_index = o.indexer_scores(inp["q_idx"], o.dequant_e4m3(inp["idx_bits"], inp["idx_scale"]), inp["w_idx"])
+        assert_sel_close(sel, ref_index, 2048, IDX_TOL * np.abs(ref_index).max())
+        rc, rl = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], sel, 1 / 16)
+        assert_ulp(rc, ctx_all[s], what=f"seq {s} ctx")
+        assert np.abs(lse_all[s] - rl).max() < 1e-3
+        if s < 2:
+            gi = cpu(index_out[s])
+            assert np.abs(gi - ref_index).max() <= IDX_TOL * np.abs(ref_index).max()
+            assert np.array_equal(sel, np.sort(o.indexer_topk(gi, 2048)))  # exact on its own scores
+            full = o.decode_step(inp, 2048)
+            assert_ulp(full["ctx"], ctx_all[s], what=f"seq {s} ctx vs the oracle's selection")
+
+
 def test_layer_group_index_share():
     """Owner layer publishes; three shared layers reuse the selection unchanged;
     a shared layer before any owner raises (glm_layer_runner.cuh:485-517)."""
@@ -610,6 +654,24 @@ def test_cache_append_row_out_of_range_sets_error_and_skips():
     assert np.array_equal(kbits[0, pos[ok]], ref["idx_bits"][ok])
     assert np.array_equal(lat[0, pos[ok], :512], ref["c_kv"][ok])
     assert np.all(kbits[0, 255] == 0x5A) and np.all(lat[0, 255] == 3.0)
+
+
+def test_cache_append_sequence_out_of_range_sets_error_and_skips():
+    """A token whose sequence lies past the caches' n_seq is flagged and skipped,
+    like a bad row; the other tokens are written."""
+    T_max, n_seq = 256, 2
+    pos = np.array([3, 9, 7])
+    seq = np.array([0, 2, 1])  # sequence 2 does not exist
+    got, ref = _append_case(3, T_max, pos, seq=seq, n_seq=n_seq, seed=11)
+    st, word = A.device_error(clear=True)
+    assert st == _lib.WL_ERR_DEVICE
+    kbits, kscale, lat = got
+    for i in (0, 2):
+        assert np.array_equal(kbits[seq[i], pos[i]], ref["idx_bits"][i])
+        assert np.array_equal(lat[seq[i], pos[i], :512], ref["c_kv"][i])
+    untouched = np.ones((n_seq, T_max), bool)
+    untouched[seq[[0, 2]], pos[[0, 2]]] = False
+    assert np.all(kbits[untouched] == 0x5A) and np.all(lat[untouched] == 3.0)
 
 
 # ---- the absorption around the attention (wl_mla_absorb_q / wl_mla_project_v) ----------------

@@ -81,3 +81,36 @@ def test_noalloc_rejects_batches_beyond_its_fixed_scratch():
     io, keep = A.decode_io(cfg, kv, q_abs, mode=_lib.WL_MODE_DENSE)
     st = _lib.lib().wl_attn_decode_noalloc(C.byref(cfg), C.byref(io), torch.cuda.current_stream().cuda_stream)
     assert st == _lib.WL_ERR_WORKSPACE
+
+
+def test_noalloc_without_lse_and_with_device_counts():
+    """Two more shapes of a call: no lse output (the attention's merge then
+    writes its lse into the fixed scratch) and a consumer whose per-sequence
+    counts come from device memory (ragged lists of one stride)."""
+    A.device_error(clear=True)
+    T = 3000
+    inps = [o.make_inputs(T, 1, seq=10 + s) for s in range(4)]
+    kv, q_abs = _gpu(inps)
+    cfg = A.glm52_cfg(T)
+    rng = np.random.default_rng(17)
+    counts = [2048, 700, 1, 1999]
+    sel = np.full((4, 2048), -1, np.int32)
+    for b, n in enumerate(counts):
+        sel[b, :n] = np.sort(rng.choice(T, n, replace=False))
+    sel_t = torch.from_numpy(sel).cuda()
+    n_t = torch.tensor(counts, dtype=torch.int32, device="cuda")
+    kw = dict(mode=_lib.WL_MODE_CONSUMER, sel_in=sel_t, sel_n_in=n_t, canonical=True)
+    ref = A.attn_decode(cfg, kv, q_abs, **kw)
+    got = _noalloc(cfg, kv, q_abs, **kw)
+    _same(ref, got)
+    # the same call with io.lse = NULL: ctx is unchanged
+    io, keep = A.decode_io(cfg, kv, q_abs, **kw)
+    io.lse = None
+    _lib.check(_lib.lib().wl_attn_decode_noalloc(C.byref(cfg), C.byref(io), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert torch.equal(keep["ctx"], got["ctx"])
+    for b, n in enumerate(counts):
+        rc, _ = o.mla_absorbed(inps[b]["q_abs"], inps[b]["c_kv"], inps[b]["k_rot"], sel[b, :n], 1 / 16)
+        assert o.bf16_ulp_error(rc, keep["ctx"].cpu().numpy()[b]) <= ULP_TOL
+    st, word = A.device_error(clear=True)
+    assert st == _lib.WL_OK, f"device error word 0x{word:08x}"

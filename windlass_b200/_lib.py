@@ -71,7 +71,8 @@ class Shard(C.Structure):
 class CacheAppendIO(C.Structure):
     _fields_ = [("n", i32), ("pos", vp), ("seq", vp), ("cos", vp), ("sin", vp), ("k_raw", vp),
                 ("k_norm_w", vp), ("k_norm_b", vp), ("ln_eps", f32), ("index", IndexCache),
-                ("kv_raw", vp), ("kv_norm_w", vp), ("rms_eps", f32), ("latent", LatentCache)]
+                ("kv_raw", vp), ("kv_norm_w", vp), ("rms_eps", f32), ("latent", LatentCache),
+                ("n_seq", i32)]
 
 
 STRUCTS = [AttnCfg, LatentCache, IndexCache, Rows, IndexShareC, DecodeIO, PrefillIO, Shard, CacheAppendIO]
@@ -115,6 +116,10 @@ SIGNATURES = {
     "wl_indexer_query": (C.c_int, [C.POINTER(AttnCfg), i32, vp, i64, vp, vp, i64, i32, vp, vp, vp, vp, vp, vp]),
     "wl_mla_absorb_q": (C.c_int, [C.POINTER(AttnCfg), i32, vp, i64, vp, vp, i64, vp]),
     "wl_mla_project_v": (C.c_int, [C.POINTER(AttnCfg), i32, vp, i64, vp, vp, i64, vp]),
+    "wl_diag_set_wait_limit": (C.c_int, [i64]),
+    "wl_diag_phase_stamps": (C.c_int, [vp, i32]),
+    "wl_diag_phase_count": (i32, []),
+    "wl_diag_merge_exchange": (C.c_int, [vp, i64, vp, i32, i32, vp, vp, vp]),
 }
 
 _lib = None

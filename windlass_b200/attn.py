@@ -280,6 +280,13 @@ def cache_append(cfg: AttnCfg, pos: torch.Tensor, cos: torch.Tensor, sin: torch.
         io.kv_raw, io.kv_norm_w = (t.data_ptr() for t in hold[-2:])
         io.rms_eps = rms_eps
         io.latent = kv.c()
+    # sequences the given caches hold: the library skips (and flags) any seq[i] outside them
+    counts = []
+    if k_raw is not None:
+        counts.append(keys.keys.shape[0] if keys.keys.dim() == 3 else 1)
+    if kv_raw is not None:
+        counts.append(kv.c_kv.shape[0] if kv.c_kv.dim() == 3 else 1)
+    io.n_seq = min(counts) if seq is not None else 1
     check(lib().wl_cache_append(C.byref(cfg), C.byref(io), _stream()), "wl_cache_append")
 
 

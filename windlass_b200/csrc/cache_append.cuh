@@ -33,6 +33,7 @@ struct AppendParams {
     int n;                      // tokens
     const int* pos;             // [n] cache row of each token
     const int* seq;             // [n] sequence of each token, or null (all 0)
+    int n_seq;                  // sequences the caches hold (seq[i] must be below it)
     int T_max;                  // rows each sequence's caches hold
     const float* cos;           // [n][32] the token's RoPE table row
     const float* sin;
@@ -73,7 +74,7 @@ __global__ void __launch_bounds__(32 * CA_WARPS) cache_append_kernel(AppendParam
     if (tok >= p.n) return;
     const int row = p.pos[tok];
     const int sq = p.seq ? p.seq[tok] : 0;
-    if (row < 0 || row >= p.T_max || sq < 0) {
+    if (row < 0 || row >= p.T_max || sq < 0 || sq >= p.n_seq) {
         if (lane == 0) set_error(ERRC_BOUNDS, 40);
         return;
     }

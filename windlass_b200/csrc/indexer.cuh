@@ -136,39 +136,6 @@ struct IdxStreamParams {
     CUtensorMap tm_keys;
 };
 
-#ifdef WL_TRACE
-__device__ long long* g_trace;
-#define WL_TRB(slot)                                                                                    \
-    do {                                                                                                \
-        if (g_trace && threadIdx.x == 0) {                                                              \
-            unsigned long long t_;                                                                      \
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
-            g_trace[512 + 2 * (blockIdx.y * gridDim.x + blockIdx.x) + (slot)] = (long long)t_;          \
-        }                                                                                               \
-    } while (0)
-#define WL_TRP(slot)                                                                                    \
-    do {                                                                                                \
-        if (g_trace && blockIdx.x == 0 && blockIdx.y == 0) {                                            \
-            unsigned long long t_;                                                                      \
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                      \
-            g_trace[900 + (slot)] = (long long)t_;                                                      \
-        }                                                                                               \
-    } while (0)
-#define WL_TR(slot, i)                                                                                  \
-    do {                                                                                                \
-        if (g_trace && blockIdx.x == 0 && blockIdx.y == 0 && (i) < 64) g_trace[(i) * 8 + (slot)] = clock64(); \
-    } while (0)
-#else
-#define WL_TR(slot, i) \
-    do {               \
-    } while (0)
-#define WL_TRB(slot) \
-    do {             \
-    } while (0)
-#define WL_TRP(slot) \
-    do {             \
-    } while (0)
-#endif
 
 // grid (CTAs per group, row groups): a CTA takes R consecutive rows (one key
 // cache) and a contiguous range of `tiles_per_cta` tiles of their keys.
@@ -177,8 +144,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
     indexer_stream_kernel(IdxParams p, const __grid_constant__ IdxStreamParams sp, unsigned* hist, int tiles_per_cta) {
     using L = IdxStream<R>;
     constexpr int NT = L::THREADS, NACC = L::NACC;
-    WL_KT_BEGIN(0);
-    WL_TRB(0);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* k8 = smem + L::OFF_K8;
@@ -236,7 +201,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
     tc_fence_before();
     __syncthreads();  // barriers initialised, TMEM address published
     tc_fence_after();
-    if (tid == 0) WL_TRP(0);
     pdl_wait();  // everything above overlaps the previous kernel; global data below
     pdl_trigger();
     const uint32_t tmem = *tmem_slot;
@@ -295,7 +259,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
         *reinterpret_cast<uint32_t*>(sQ + rl * 128u + ((((byte >> 4) ^ rl) & 7u) << 4) + (byte & 15u)) = lo4;
         if (lane == 0) sW[hr] = j < nrows ? wv[k2] / s_h : 0.f;
     }
-    if (tid == 32) WL_TRP(1);
     if (!producer) {
         fence_proxy_async_smem();  // the query tiles are read by the tensor cores
         asm volatile("bar.sync 1, %0;" ::"n"(NT - 32) : "memory");
@@ -307,8 +270,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
             const int s = i % IDX_NS;
             if (i >= IDX_NS && !mbar_wait(empty + s, (uint32_t)(i / IDX_NS - 1) & 1u, 10)) break;
             if (lane == 0) {
-                WL_TR(0, i);
-                if (i == 0) WL_TRP(2);
                 const int t0 = (tb + i) * IDX_TILE;
                 mbar_expect_tx(full + s, L::K8_TILE);
                 tma_load3d(k8 + s * L::K8_TILE, &sp.tm_keys, 0, t0, seq, full + s);
@@ -324,9 +285,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
             if (i >= NACC && !mbar_wait(acc_empty + a, (uint32_t)(i / NACC - 1) & 1u, 12)) break;
             tc_fence_after();
             if (lane == 0) {
-                WL_TR(3, i);
-                if (i == 0) WL_TRP(3);
-                if (i == n - 1) WL_TRP(4);
                 const uint32_t sA = smem_u32(k8 + s * L::K8_TILE);
                 const uint32_t d = tmem + (uint32_t)(a * L::QROWS);
 #pragma unroll
@@ -337,7 +295,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
                 }
                 mma_commit(acc_full + a);
                 mma_commit(empty + s);  // keys consumed
-                WL_TR(4, i);
             }
             __syncwarp();
         }
@@ -361,7 +318,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
             const float sc_raw = sc_next;
             sc_next = load_scale(i + L::EPI_GROUPS);
             if (!mbar_wait(acc_full + a, (uint32_t)(i / NACC) & 1u, 15)) break;
-            if (key == 0) WL_TR(5, i);
             tc_fence_after();
             const float sc = sc_raw * p.qk_scale;
 #pragma unroll 1
@@ -380,14 +336,10 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
             }
             tc_fence_before();
             mbar_arrive(acc_empty + a);
-            if (key == 0) WL_TR(6, i);
-            if (key == 0 && i == n - 1) WL_TRP(5);
         }
     }
     tc_fence_before();
-    if (tid == 0) WL_TRP(6);
     __syncthreads();
-    if (tid == 0) WL_TRP(7);
     if (hrow) {  // this CTA's counts into the row's histogram: nonzero bins only
         for (int b4 = tid; b4 < TOPK_HIST_BINS / 4; b4 += NT) {
             const uint4 c = reinterpret_cast<const uint4*>(sHist)[b4];
@@ -401,9 +353,6 @@ __global__ void __launch_bounds__(IdxStream<R>::THREADS, IDX_CTAS_PER_SM)
         tc_fence_after();
         tmem_dealloc(tmem, L::TMEM_COLS);
     }
-    WL_KT_END(0);
-    WL_TRB(1);
-    if (tid == 0) WL_TRP(8);
 }
 
 }  // namespace wl

@@ -17,7 +17,7 @@
 
 namespace wl {
 
-constexpr int AT_TILE = 128;  // split-K ranges are multiples of this many keys
+constexpr int AT_TILE = 64;  // split-K ranges are multiples of this many keys (one tile)
 constexpr int AT_H = 64;
 constexpr int AT_D = 576;
 constexpr int AT_DV = 512;
@@ -37,6 +37,8 @@ struct AttnParams {
     int sel_n;
     long long win_lo, win_hi;
     int split_keys;  // 0: one CTA covers the whole list
+    int dyn_split;   // 1: split_keys ignored; the window's entries spread evenly over the
+                     //    max_splits CTAs of the row, in multiples of 64 keys
     int max_splits;
     float* o_part;
     float* lse_part;
@@ -64,7 +66,6 @@ struct MergeParams {
 // Up to 32 parts: lane s holds part s's lse; all parts' columns load at once.
 template <bool LL>
 __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
-    WL_KT_BEGIN(3);
     pdl_wait();
     pdl_trigger();
     const int h = blockIdx.x, q = blockIdx.y, r = blockIdx.z, lane = threadIdx.x;
@@ -135,7 +136,6 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
     *reinterpret_cast<float4*>(p.ctx + (long long)r * p.ctx_row_stride + (long long)h * p.dv + c) = acc;
     if (q == 0 && lane == 0 && p.lse)
         p.lse[(long long)r * p.lse_out_row_stride + h] = (W > 0.f) ? M + logf(W) : -INFINITY;
-    WL_KT_END(3);
 }
 
 }  // namespace wl

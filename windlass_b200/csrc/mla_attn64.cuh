@@ -36,17 +36,6 @@
 
 namespace wl {
 
-#ifdef WL_TRACE
-__device__ long long* g_trace_pf;
-#define WL_TPF(slot, i)                                                                              \
-    do {                                                                                             \
-        if (g_trace_pf && blockIdx.y == 100 && blockIdx.x == 0 && (i) < 64) g_trace_pf[(i) * 8 + (slot)] = clock64();  \
-    } while (0)
-#else
-#define WL_TPF(slot, i) \
-    do {                \
-    } while (0)
-#endif
 
 constexpr int PF_TILE = 64;       // keys per tile
 constexpr int PF_NBUF = 3;        // key tiles in shared memory
@@ -122,7 +111,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid == 0) WL_TPF(7, 0);
     const int r = blockIdx.y, split = blockIdx.x;
     const int seq = r / p.rows_per_seq;
     const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
@@ -170,7 +158,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     int cb, ce;
     {
         const int e0 = misc[0], e1 = max(misc[1], misc[0]);
-        if (p.split_keys > 0) {
+        if (p.dyn_split) {
+            // the entries this rank's window holds, evenly over the row's CTAs
+            const int per = (((e1 - e0) + p.max_splits - 1) / p.max_splits + PF_TILE - 1) / PF_TILE * PF_TILE;
+            cb = min(e0 + split * per, e1);
+            ce = min(cb + per, e1);
+        } else if (p.split_keys > 0) {
             cb = e0 + split * p.split_keys;
             ce = min(cb + p.split_keys, e1);
         } else {
@@ -184,8 +177,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     float* ctx = p.o_part + ((long long)r * p.max_splits + split) * (AT_H * AT_DV);
     float* lse_out = p.lse_part + ((long long)r * p.max_splits + split) * AT_H;
     if (n_keys <= 0) {
-        for (int i = tid; i < AT_H * AT_DV / 4; i += PF_THREADS)
-            reinterpret_cast<float4*>(ctx)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        // An empty split: lse = -inf marks it; its o is never read (the merge
+        // skips parts of weight zero), so it is not written.
         if (tid < AT_H) lse_out[tid] = -INFINITY;
         return;
     }
@@ -213,7 +206,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tid == 0) WL_TPF(7, 4);
     const uint32_t tmem = *tmem_slot;
     const __nv_bfloat16* ckv = p.c_kv + (long long)seq * p.ckv_seq;
     const __nv_bfloat16* krt = p.k_rot + (long long)seq * p.krot_seq;
@@ -261,11 +253,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                 cp_async16(tile + (uint32_t)c * L::CHUNK + sw128_off(j, seg), src, row < 0 ? 0u : 16u);
             }
             cp_async_commit();
-            if (g == 0) WL_TPF(0, i);
             cp_async_wait_all();
             fence_proxy_async_smem();
             mbar_arrive(kfull + b);
-            if (g == 0) WL_TPF(1, i);
             asm volatile("bar.sync 2, %0;" ::"n"(PF_GATHER) : "memory");  // rows_sh[b] is rewritten PF_NBUF tiles on
         }
     } else if (warp == PF_MMA_WARP) {
@@ -277,7 +267,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             if (i >= 2 && !mbar_wait_fast(sfree + s, (uint32_t)((i >> 1) - 1) & 1u, 33)) return false;
             tc_fence_after();
             if (lane == 0) {
-                WL_TPF(2, i);
                 const uint32_t tile = sK + (uint32_t)b * L::TILE;
                 const uint32_t d = tmem + (16u << 16) + (uint32_t)(s * PF_TILE);
 #pragma unroll 1
@@ -298,7 +287,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             if (!mbar_wait_fast(pready, (uint32_t)i & 1u, 34)) return false;
             tc_fence_after();
             if (lane == 0) {
-                WL_TPF(3, i);
                 const uint32_t tile = sK + (uint32_t)b * L::TILE;
 #pragma unroll
                 for (int ks = 0; ks < PF_TILE / 16; ++ks) {
@@ -357,7 +345,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             const int s = i & 1;
             const int nv = min(PF_TILE, n_keys - i * PF_TILE);
             if (!(ok = mbar_wait_fast(sfull + s, (uint32_t)(i >> 1) & 1u, 35))) break;
-            if (tid == 0) WL_TPF(4, i);
             tc_fence_after();
             float sv[32];
             tmem_ld16x2_32<32>(tmem + lane_s + (uint32_t)(s * PF_TILE), sv);
@@ -376,7 +363,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
             // P of the previous tile must be consumed (and O complete) first
             if (i >= 1 && !(ok = mbar_wait_fast(pvdone, (uint32_t)(i - 1) & 1u, 36))) break;
-            if (tid == 0) WL_TPF(5, i);
             tc_fence_after();
             float sum = 0.f;
             const uint32_t prow = sP + (uint32_t)h * 128u;
@@ -413,7 +399,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             fence_proxy_async_smem();  // P is read by the tensor cores
             tc_fence_before();
             mbar_arrive(pready);
-            if (tid == 0) WL_TPF(6, i);
         }
         // ---- 1 / l and lse per head, for the epilogue warps ----
         if (!hi_half) {
@@ -471,15 +456,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             }
         }
     }
-    if (tid == 0) WL_TPF(7, 1);
     tc_fence_before();
     __syncthreads();
-    if (tid == 0) WL_TPF(7, 2);
     if (warp == PF_MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, L::TMEM_COLS);
     }
-    if (tid == 0) WL_TPF(7, 3);
 }
 
 }  // namespace wl

@@ -26,7 +26,7 @@
 namespace wl {
 
 constexpr int P2P_MAX_RANKS = 8;
-constexpr int XCH_CAND = 0, XCH_PART = 1, XCH_TYPES = 2;
+constexpr int XCH_CAND = 0, XCH_PART = 1, XCH_GATH = 2, XCH_TYPES = 3;
 constexpr long long P2P_OFF_CAND = 0;
 
 struct P2PArgs {
@@ -56,11 +56,11 @@ __device__ __forceinline__ uint64_t ll_load1_raw(const uint64_t* src) {
 __device__ __forceinline__ uint32_t ll_wait1(const uint64_t* src, uint32_t epoch, uint64_t first, unsigned site) {
     uint64_t x = first;
     if ((uint32_t)(x >> 32) == epoch) return (uint32_t)x;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), lim = g_wait_cycles;
     while (true) {
         x = ll_load1_raw(src);
         if ((uint32_t)(x >> 32) == epoch) return (uint32_t)x;
-        if (clock64() - t0 > WL_WAIT_CYCLES) {
+        if (clock64() - t0 > lim) {
             set_error(ERRC_TIMEOUT, site);
             return 0u;
         }

@@ -3,7 +3,7 @@
 // and the shared-memory matrix descriptors tcgen05.mma reads.
 //
 // Every wait in this library is bounded: a wait that runs past
-// WL_WAIT_CYCLES sets the device error word and returns false, and the caller
+// g_wait_cycles sets the device error word and returns false, and the caller
 // unwinds (waits for its own copies, frees TMEM, returns). Nothing here traps.
 #pragma once
 #include <cstdint>
@@ -14,8 +14,11 @@
 
 namespace wl {
 
-// ~1 s at the B200's 1.9 GHz SM clock.
-constexpr long long WL_WAIT_CYCLES = 2000000000LL;
+// Limit of every bounded wait, in SM clock cycles: ~1 s at the B200's 1.9 GHz
+// SM clock. A device variable (not a constant) so that a test can shorten it
+// through wl_diag_set_wait_limit and watch a wait run out.
+constexpr long long WL_WAIT_CYCLES_DEFAULT = 2000000000LL;
+__device__ long long g_wait_cycles = WL_WAIT_CYCLES_DEFAULT;
 
 // Device error word (one per device per loaded library). First error wins.
 // Layout: code << 24 | site << 16 | (blockIdx.x & 0xffff).
@@ -74,9 +77,9 @@ __device__ __forceinline__ bool mbar_try_wait_nohint(uint64_t* bar, uint32_t par
 }
 __device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, unsigned site) {
     if (mbar_try_wait_nohint(bar, parity)) return true;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), lim = g_wait_cycles;
     while (!mbar_try_wait_nohint(bar, parity)) {
-        if (clock64() - t0 > WL_WAIT_CYCLES) {
+        if (clock64() - t0 > lim) {
             set_error(ERRC_TIMEOUT, site);
             return false;
         }
@@ -86,9 +89,9 @@ __device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, u
 // Bounded wait for phase `parity` of `bar`. false = timed out (error recorded).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned site) {
     if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
+    const long long t0 = clock64(), lim = g_wait_cycles;
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > WL_WAIT_CYCLES) {
+        if (clock64() - t0 > lim) {
             set_error(ERRC_TIMEOUT, site);
             return false;
         }
@@ -239,29 +242,6 @@ __device__ __forceinline__ void cluster_sync_all() {
 // kernel may touch, and only then pdl_trigger() — so that, transitively, every
 // grid before its predecessor has completed once a dependent starts. Both are
 // no-ops for a kernel launched without the attribute.
-#ifdef WL_TRACE
-// Per-kernel first-start / last-end global timestamps (trace builds only).
-__device__ unsigned long long* g_ktrace;
-__device__ __forceinline__ unsigned long long gtimer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ long long* g_trace_attn;
-#define WL_TA(slot)                                                                                        \
-    do {                                                                                                   \
-        if (g_trace_attn && threadIdx.x == 0 && blockIdx.y == 0 && blockIdx.x < 16)                        \
-            g_trace_attn[blockIdx.x * 16 + (slot)] = clock64();                                           \
-    } while (0)
-#define WL_KT_BEGIN(k) \
-    do { if (g_ktrace && threadIdx.x == 0) atomicMin(g_ktrace + 2 * (k), gtimer()); } while (0)
-#define WL_KT_END(k) \
-    do { if (g_ktrace && threadIdx.x == 0) atomicMax(g_ktrace + 2 * (k) + 1, gtimer()); } while (0)
-#else
-#define WL_TA(slot) do {} while (0)
-#define WL_KT_BEGIN(k) do {} while (0)
-#define WL_KT_END(k) do {} while (0)
-#endif
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -534,24 +534,6 @@ constexpr int TOPKC_CL = 8;
 constexpr int TOPKC_THREADS = 1024;
 constexpr int TOPKC_GCAP = 4096;  // keys of the crossing bin CTA 0 gathers (else the distributed refinement)
 
-#ifdef WL_TRACE
-__device__ long long* g_trace_topk;
-#define WL_TRK(slot)                                                                                  \
-    do {                                                                                              \
-        if (g_trace_topk && blockIdx.y == 0 && threadIdx.x == 0) g_trace_topk[blockIdx.x * 16 + (slot)] = clock64(); \
-    } while (0)
-#define WL_TRR(slot)                                                                   \
-    do {                                                                               \
-        if (g_trace_topk && blockIdx.x == 0 && threadIdx.x == 0) g_trace_topk[128 + (slot)] = clock64(); \
-    } while (0)
-#else
-#define WL_TRR(slot) \
-    do {             \
-    } while (0)
-#define WL_TRK(slot) \
-    do {             \
-    } while (0)
-#endif
 
 // Block-wide search from the top over bins held by threads: thread t owns the
 // consecutive bins [t * PERB, (t + 1) * PERB) with counts c[0..PERB) (higher t
@@ -605,7 +587,6 @@ __device__ __forceinline__ void block_find_from_top(const uint32_t (&c)[PERB], u
 template <int PER>
 __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS, 1)
     topk_cluster_kernel(TopkMParams p, int vec4, CandOut co) {
-    WL_KT_BEGIN(1);
     pdl_wait();
     pdl_trigger();
     static_assert(PER % 4 == 0 && PER <= 32, "PER: whole float4s, one bit each in a 32-bit mask");
@@ -624,7 +605,6 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     const int kk = min(p.k, len);
     int* out = p.out + (long long)r * p.out_stride;
     const int lo = (int)rank * TOPKC_THREADS * PER, hi = min(len, lo + TOPKC_THREADS * PER);
-    WL_TRK(0);
     if (rank == 0 && tid == 0 && p.n_out) p.n_out[r] = kk > 0 ? kk : 0;
     if (rank == 0) cand_pad(co, r, max(kk, 0), tid, TOPKC_THREADS);
     if (kk <= 0) return;  // uniform over the cluster
@@ -666,7 +646,6 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     // Every CTA of the cluster has started and CTA 0's counters are zero
     // before any remote access (the wait follows level 1).
     cluster_arrive();
-    WL_TRK(1);
     // ---- level 1: the bin b1 of the indexer's histogram holding the k-th key ----
     uint32_t b1, above1, bcount;
     {
@@ -676,7 +655,6 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     uint32_t u[PER];
 #pragma unroll
     for (int j = 0; j < PER; ++j) u[j] = ordered_key(f[j]);
-    WL_TRK(2);
     // One pass over the keys: those in bins above b1 are selected outright, those
     // in b1 are the candidates; every later step walks the candidate bits only.
     uint32_t mabove = 0, mcand = 0;
@@ -712,9 +690,7 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
             const int j = __ffs(m) - 1;
             if (slot < (uint32_t)TOPKC_GCAP) dsmem_st_v2(gc0 + slot * 8u, u[j], (uint32_t)(i0 + j));
         }
-        WL_TRK(3);
         cluster_sync_all();  // the candidates and counts are in CTA 0
-        WL_TRK(4);
         if (rank == 0) {
             // ---- levels 2, 3 (10 + 9 bits) over the gathered keys ----
             const uint32_t n = min(gctl[0], (uint32_t)TOPKC_GCAP);
@@ -761,9 +737,7 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
                 dsmem_st_v4(dsmem_addr(res, (uint32_t)tid), thr, remaining, gb, eb);
             }
         }
-        WL_TRK(5);
         cluster_sync_all();  // every CTA's thr, need and output bases written; no remote access after this
-        WL_TRK(6);
         const uint32_t thr = res[0], need = res[1];
         uint32_t mgt = mabove, meq = 0;
         for (uint32_t m = mcand; m; m &= m - 1) {
@@ -794,8 +768,6 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
                 }
             }
         }
-        WL_TRK(12);
-        WL_KT_END(1);
         return;
     }
     // ---- levels 2, 3 over the cluster: bin `tid` of each pass summed over the CTAs ----
@@ -809,9 +781,7 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
             const uint32_t x = u[__ffs(m) - 1];  // dynamic index: local memory only for this rare walk
             if ((x & mask_hi) == prefix) atomicAdd(&h[(x >> shift) & (nb - 1)], 1u);
         }
-        WL_TRK(3 + 3 * pass);
         cluster_sync_all();  // every CTA's histogram complete and visible
-        WL_TRK(4 + 3 * pass);
         uint32_t c1[1] = {0u};
         if (tid < (int)nb) {
 #pragma unroll
@@ -822,7 +792,6 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
         prefix |= b << shift;
         mask_hi |= (nb - 1) << shift;
         remaining -= above;
-        WL_TRK(5 + 3 * pass);
     }
     const uint32_t thr = prefix, need = remaining;
     // ---- ordered emission ----
@@ -839,9 +808,7 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
         tot[0] = total & 0xffffu;
         tot[1] = total >> 16;
     }
-    WL_TRK(9);
     cluster_sync_all();  // totals visible; also orders every remote histogram read before exit
-    WL_TRK(10);
     uint32_t gt_b = 0, eq_b = 0;
     for (uint32_t c = 0; c < rank; ++c) {
         gt_b += dsmem_ld_u32(&tot[0], c);
@@ -868,10 +835,7 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
             }
         }
     }
-    WL_TRK(11);
     cluster_wait();  // no CTA leaves while another may still read its totals
-    WL_TRK(12);
-    WL_KT_END(1);
 }
 
 // ---- single-CTA top-k with the row in registers --------------------------------------
@@ -888,7 +852,6 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
 template <int PER, bool LL>
 __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p, int vec4, CandOut co) {
     static_assert(PER % 4 == 0 && PER <= 32, "PER: whole float4s, one bit each in a 32-bit mask");
-    WL_TRR(0);
     pdl_wait();
     pdl_trigger();
     __shared__ uint32_t hist[2048];
@@ -967,7 +930,6 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
 #pragma unroll
         for (int j = 0; j < PER; ++j) u[j] = ordered_key(f[j]);
     }
-    WL_TRR(1);
     // ---- the row's key range: levels bin the offset d = key - lo ----
     uint32_t lo = 0xffffffffu, hi = 0u;
 #pragma unroll
@@ -1010,9 +972,7 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
     uint32_t b1, above1;
     {
         uint32_t c2[2] = {hist[2 * tid], hist[2 * tid + 1]};
-        WL_TRR(2);
         block_find_from_top<2>(c2, (uint32_t)kk, scan_sh, &b1, &above1);
-        WL_TRR(3);
     }
     // ---- levels 2 and 3 over the crossing bin's keys ----
     uint32_t prefix = b1 << s1, mask_hi = s1 >= 32 ? 0u : (0xffffffffu << s1), remaining = (uint32_t)kk - above1;
@@ -1037,7 +997,6 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
         mask_hi |= (nb - 1u) << shift;
         remaining -= above;
         shift_hi = shift;
-        WL_TRR(4 + 3 * pass);
     }
     prefix += lo;  // back from the offset to the key
     const uint32_t thr = prefix, need = remaining;
@@ -1051,7 +1010,6 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
     }
     uint32_t total;
     const uint32_t ex = block_excl_scan(((uint32_t)__popc(meq) << 16) | (uint32_t)__popc(mgt), scan_sh, &total);
-    WL_TRR(5);
     uint32_t gt_b = ex & 0xffffu, eq_b = ex >> 16;
     for (uint32_t m = mgt | meq; m; m &= m - 1) {
         const int j = __ffs(m) - 1;
@@ -1072,7 +1030,6 @@ __global__ void __launch_bounds__(TOPK_THREADS, 1) topk_reg_kernel(TopkParams p,
             }
         }
     }
-    WL_TRR(6);
 }
 
 // ---- normalisation of an arbitrary index list ---------------------------------

@@ -28,32 +28,33 @@
 #include "mla_proj.cuh"
 #include "p2p.cuh"
 #include "topk.cuh"
+#include "xmerge.cuh"
 
 namespace {
 
-#ifdef WL_TRACE
-// Phase timeline of one host call (trace builds only): a one-thread kernel
-// stamps the global timer at each phase boundary (works inside CUDA graphs).
+// Phase timeline of the sharded decode (diagnostics, off by default): when a
+// caller has set a stamp buffer with wl_diag_phase_stamps, a one-thread kernel
+// writes the global timer at each phase boundary of wl_attn_decode_sharded.
+// It works inside CUDA graphs (the buffer pointer is baked into the captured
+// launches). The extra launches break the programmatic overlap between the
+// phases, so a stamped step runs somewhat slower than an unstamped one.
 __global__ void phase_stamp_kernel(unsigned long long* buf, int i) {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     buf[i] = t;
 }
+std::mutex g_ph_mu;
 unsigned long long* g_ph_buf = nullptr;
-int g_ph_n = -1;  // -1: off
-#define WL_PHASE(st)                                                                 \
-    do {                                                                             \
-        if (g_ph_n >= 0 && g_ph_n < 32 && g_ph_buf) {                                \
-            phase_stamp_kernel<<<1, 1, 0, st>>>(g_ph_buf, g_ph_n++);                \
-        }                                                                            \
-    } while (0)
-#else
-#define WL_PHASE(st) \
-    do {             \
-    } while (0)
-#endif
+int g_ph_cap = 0;
+int g_ph_n = 0;
+void phase_stamp(cudaStream_t st) {
+    std::lock_guard<std::mutex> lk(g_ph_mu);
+    if (!g_ph_buf || g_ph_n >= g_ph_cap) return;
+    phase_stamp_kernel<<<1, 1, 0, st>>>(g_ph_buf, g_ph_n++);
+}
+#define WL_PHASE(st) phase_stamp(st)
 
-constexpr int kMaxSplits = 16;   // split-K CTAs per decode row
+constexpr int kMaxSplits = 32;   // split-K CTAs per decode row (the merge takes up to 32 parts)
 constexpr int kMaxDevices = 64;
 
 #define WL_CUDA_TRY(expr)                                           \
@@ -231,11 +232,16 @@ int rows_ok(const wl_rows* r, int32_t T) {
     return WL_OK;
 }
 
-// Keys per split so that at most kMaxSplits CTAs cover n entries.
-int split_keys_for(long long n) {
-    long long per = ceil_div(n > 0 ? n : 1, kMaxSplits);
-    per = ceil_div(per, wl::AT_TILE) * wl::AT_TILE;
-    return (int)(per < wl::AT_TILE ? wl::AT_TILE : per);
+// Split-K CTAs per decode row: about one wave of CTAs over all rows (the
+// attention is latency-bound at decode batches), at most `cap`, and no more
+// than one per 64-key tile of the longest list. The kernel spreads each row's
+// entries (inside its key window) evenly over these CTAs.
+int splits_for(int32_t rows, long long n_max, int cap) {
+    long long s = sm_count() / (rows > 0 ? rows : 1);
+    s = s < 1 ? 1 : s;
+    s = s > cap ? cap : s;
+    const long long tiles = ceil_div(n_max > 0 ? n_max : 1, wl::AT_TILE);
+    return (int)(s > tiles ? tiles : s);
 }
 
 // ---- kernel launchers ----------------------------------------------------------
@@ -505,14 +511,14 @@ int launch_normalize(const int32_t* in, int64_t in_stride, const int32_t* n_in_d
 int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int64_t len_T,
                 const wl_rows* rows, const void* q_abs, const int32_t* sel, int64_t sel_stride,
                 const int32_t* sel_n_dev, int32_t sel_n, int64_t win_lo, int64_t win_hi, int32_t split_keys,
-                float* o_part, float* lse_part, int32_t max_splits, cudaStream_t st, bool many_rows = false) {
+                float* o_part, float* lse_part, int32_t max_splits, cudaStream_t st, bool dyn_split = false) {
     if (!c || !c->c_kv || !c->k_rot || !q_abs || !o_part || !lse_part) return WL_ERR_ARG;
     if (!aligned16(c->c_kv) || !aligned16(c->k_rot) || !aligned16(q_abs)) return WL_ERR_ARG;
     if ((c->c_kv_row_stride & 7) || (c->k_rot_row_stride & 7) || (c->c_kv_seq_stride & 7) ||
         (c->k_rot_seq_stride & 7))
         return WL_ERR_ARG;
     if (split_keys < 0 || (split_keys % wl::AT_TILE) || max_splits <= 0) return WL_ERR_ARG;
-    if (split_keys == 0 && max_splits != 1) return WL_ERR_ARG;
+    if (split_keys == 0 && max_splits != 1 && !dyn_split) return WL_ERR_ARG;
     if (rows->n_rows > 65535 || max_splits > 65535) return WL_ERR_ARG;
     wl::AttnParams p{};
     p.c_kv = static_cast<const __nv_bfloat16*>(c->c_kv);
@@ -535,13 +541,13 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     p.win_lo = win_lo;
     p.win_hi = win_hi;
     p.split_keys = split_keys;
+    p.dyn_split = dyn_split ? 1 : 0;
     p.max_splits = max_splits;
     p.o_part = o_part;
     p.lse_part = lse_part;
     p.scale_log2 = cfg->softmax_scale * 1.4426950408889634f;
     // Heads as M = 64, gather / QK / softmax / P.V pipelined over 64-key tiles;
     // grid (splits, rows), each CTA one (o, lse) partial.
-    (void)many_rows;
     wl::PfParams pp{};
     if (int e = encode_q_map(&pp.tm_q, q_abs, rows->n_rows)) return e;
     pp.o_tma = aligned16(o_part) && encode_o_map(&pp.tm_o, o_part, (int64_t)rows->n_rows * max_splits) == WL_OK;
@@ -698,9 +704,10 @@ __global__ void candidates_to_rows_kernel(const float* s_all, const int* i_all, 
 // region layout; larger calls use the NCCL exchange.
 constexpr int kP2PMaxRows = 32;
 constexpr int kP2PMaxK = 4096;
-// Slots hold the wire format: 8 bytes per 4-byte payload word.
-constexpr long long kP2PCandSlot = (long long)kP2PMaxRows * kP2PMaxK * 2 * 8;                    // scores, indices
-constexpr long long kP2PPartSlot = (long long)kP2PMaxRows * (wl::AT_H * wl::AT_DV + wl::AT_H) * 8;  // (o, lse) rows
+// Slots hold the wire format: 8 bytes per 4-byte payload word. Region layout:
+// [candidate slots: N x kP2PCandSlot][PART slots: N x xslot][GATH slots: N x xslot],
+// xslot = the (o, lse) words of kP2PMaxRows rows x 64/N heads (xmerge.cuh).
+constexpr long long kP2PCandSlot = (long long)kP2PMaxRows * kP2PMaxK * 2 * 8;  // scores, indices
 
 struct wl_comm {
     ncclComm_t comm;
@@ -715,8 +722,13 @@ struct wl_comm {
 
 namespace {
 
+long long p2p_xslot(int nranks) {
+    const long long w = (long long)kP2PMaxRows * (wl::AT_H / nranks) * (wl::AT_DV + 1);
+    return (w * 8 + 255) / 256 * 256;
+}
 long long p2p_off_part(int nranks) { return wl::P2P_OFF_CAND + nranks * kP2PCandSlot; }
-size_t p2p_region_bytes(int nranks) { return (size_t)(p2p_off_part(nranks) + 2LL * nranks * kP2PPartSlot); }
+long long p2p_off_gath(int nranks) { return p2p_off_part(nranks) + nranks * p2p_xslot(nranks); }
+size_t p2p_region_bytes(int nranks) { return (size_t)(p2p_off_gath(nranks) + nranks * p2p_xslot(nranks)); }
 
 bool p2p_allowed() {
     static const bool on = [] {
@@ -742,7 +754,7 @@ void p2p_release(wl_comm* c) {
 // peer exchange off everywhere (the outcome is all-reduced).
 void p2p_setup(wl_comm* c) {
     const int N = c->nranks;
-    if (N < 2 || N > wl::P2P_MAX_RANKS || !p2p_allowed()) return;
+    if (N < 2 || N > wl::P2P_MAX_RANKS || (wl::AT_H % N) || !p2p_allowed()) return;
     int ok = 1;
     cudaIpcMemHandle_t mine{};
     if (cudaMalloc(&c->region, p2p_region_bytes(N)) != cudaSuccess ||
@@ -967,7 +979,7 @@ int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, in
     if (!aligned16(q_resid) || (q_resid_row_stride & 3) || q_resid_row_stride < wl::IQ_QL || !aligned16(wq_b) ||
         !aligned16(x) || (x_row_stride & 3) || hidden <= 0 || (hidden % 1024) || x_row_stride < hidden ||
         !aligned16(weights_proj) || (reinterpret_cast<uintptr_t>(q_idx) & 1) ||
-        (reinterpret_cast<uintptr_t>(w_idx) & 3))
+        (reinterpret_cast<uintptr_t>(w_idx) & 3) || n > 65535)
         return WL_ERR_ARG;
     if (int e = ensure_attrs()) return e;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -976,7 +988,6 @@ int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, in
                            static_cast<const __nv_bfloat16*>(wq_b), cos, sin, static_cast<__nv_bfloat16*>(q_idx),
                            (long long)wl::IQ_H * wl::IQ_D));
     const float head_scale = (float)(1.0 / std::sqrt((double)wl::IQ_H));
-    if (n > 65535) return WL_ERR_ARG;
     WL_CUDA_TRY(launch_pdl(wl::idx_head_weights_kernel, dim3(wl::IQ_H, n), dim3(256), 0, st, (int)n, x,
                            (long long)x_row_stride, weights_proj, (int)hidden, head_scale, w_idx, (long long)wl::IQ_H));
     return WL_OK;
@@ -1025,10 +1036,12 @@ int wl_cache_append(const wl_attn_cfg* cfg, const wl_cache_append_io* io, void* 
     if (!io || io->n < 0) return WL_ERR_ARG;
     if (io->n == 0) return WL_OK;
     if (!io->pos || !io->cos || !io->sin || (!io->k_raw && !io->kv_raw)) return WL_ERR_ARG;
+    if (io->n_seq < 1 || (!io->seq && io->n_seq != 1)) return WL_ERR_ARG;
     wl::AppendParams p{};
     p.n = io->n;
     p.pos = io->pos;
     p.seq = io->seq;
+    p.n_seq = io->n_seq;
     p.T_max = cfg->T_max;
     p.cos = io->cos;
     p.sin = io->sin;
@@ -1080,23 +1093,36 @@ size_t wl_attn_workspace_bytes(const wl_attn_cfg* cfg, int32_t T_max, int32_t ba
     return carve_decode(nullptr, cfg, T_max, batch, 1).bytes;
 }
 
-static int decode_local(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, const DecodeWs& w,
-                        int64_t t0, int64_t T_global, float* ctx, float* lse, const int32_t* sel,
-                        const int32_t* cnt, int32_t sel_n, int64_t stride, long long n_max, cudaStream_t st,
-                        int64_t ctx_row_stride = 0, int64_t lse_row_stride = 0) {
-    // Attention over the selection restricted to this cache's window [t0, t0+T),
-    // then the merge of its split-K partials.
+// Attention over the selection restricted to this cache's window [t0, t0+T)
+// into split-K partials (at most `cap` per row; the workspace holds
+// kMaxSplits), returning the split count.
+static int decode_attn(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, const DecodeWs& w, int64_t t0,
+                       int64_t T_global, const int32_t* sel, const int32_t* cnt, int32_t sel_n, int64_t stride,
+                       long long n_max, cudaStream_t st, int cap, int32_t* nsplit_out) {
     const int32_t B = io->batch;
     const wl_rows rows{B, 1, (int32_t)T_global, 0};
     if (n_max <= 0) n_max = 1;
-    const int32_t split = split_keys_for(n_max);
-    const int32_t nsplit = (int32_t)ceil_div(n_max, split);
-    if (int e = launch_attn(cfg, &io->latent, io->T, T_global, &rows, io->q_abs, sel, stride, cnt, sel_n, t0,
-                            t0 + io->T, split, w.o_part, w.lse_part, nsplit, st))
-        return e;
-    return launch_merge(w.o_part, w.lse_part, B, nsplit, (int64_t)nsplit * wl::AT_H * wl::AT_DV,
-                        (int64_t)wl::AT_H * wl::AT_DV, (int64_t)nsplit * wl::AT_H, wl::AT_H, wl::AT_H,
-                        wl::AT_DV, ctx, lse, st, ctx_row_stride, lse_row_stride);
+    const int32_t nsplit = splits_for(B, n_max, cap);
+    *nsplit_out = nsplit;
+    return launch_attn(cfg, &io->latent, io->T, T_global, &rows, io->q_abs, sel, stride, cnt, sel_n, t0,
+                       t0 + io->T, 0, w.o_part, w.lse_part, nsplit, st, true);
+}
+
+static int decode_local(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, const DecodeWs& w,
+                        int64_t t0, int64_t T_global, float* ctx, float* lse, const int32_t* sel,
+                        const int32_t* cnt, int32_t sel_n, int64_t stride, long long n_max, cudaStream_t st,
+                        int64_t ctx_row_stride = 0, int64_t lse_row_stride = 0, int cap = kMaxSplits) {
+    // Attention over the selection restricted to this cache's window [t0, t0+T),
+    // then the merge of its split-K partials.
+    const int32_t B = io->batch;
+    int32_t nsplit = 1;
+    if (int e = decode_attn(cfg, io, w, t0, T_global, sel, cnt, sel_n, stride, n_max, st, cap, &nsplit)) return e;
+    WL_PHASE(st);
+    const int em = launch_merge(w.o_part, w.lse_part, B, nsplit, (int64_t)nsplit * wl::AT_H * wl::AT_DV,
+                                (int64_t)wl::AT_H * wl::AT_DV, (int64_t)nsplit * wl::AT_H, wl::AT_H, wl::AT_H,
+                                wl::AT_DV, ctx, lse, st, ctx_row_stride, lse_row_stride);
+    WL_PHASE(st);
+    return em;
 }
 
 // Selection for decode: returns the list/count/stride the attention consumes.
@@ -1112,6 +1138,7 @@ static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, co
         if (int e = launch_indexer(cfg, &io->index, T, &rows, io->q_idx, io->w_idx, index, istride, st,
                                    fuse ? w.topk.hist : nullptr))
             return e;
+        WL_PHASE(st);
         const int32_t kk = cfg->index_topk < T ? cfg->index_topk : T;
         int32_t* out = io->sel_out ? io->sel_out : w.sel;
         const int64_t ostride = io->sel_out ? io->sel_stride : kk;
@@ -1120,6 +1147,7 @@ static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, co
         if (int e = launch_topk(index, istride, &rows, T, cfg->index_topk, nullptr, out, ostride, n_out, st, &w.topk,
                                 fuse))
             return e;
+        WL_PHASE(st);
         *sel = out;
         *cnt = n_out;
         *stride = ostride;
@@ -1155,6 +1183,7 @@ int wl_attn_decode(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, void* wo
     if (int e = ensure_attrs()) return e;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const DecodeWs w = carve_decode(align_base(workspace), cfg, io->T, io->batch, 1);
+    WL_PHASE(st);  // stamps: start | indexer | top-k (owner) | attention | merge
     const int32_t* sel = nullptr;
     const int32_t* cnt = nullptr;
     int64_t stride = 0;
@@ -1284,8 +1313,7 @@ int wl_attn_prefill(const wl_attn_cfg* cfg, const wl_attn_prefill_io* io, void* 
         return WL_ERR_ARG;
     }
     float* lse = io->lse ? io->lse : w_lse;
-    return launch_attn(cfg, &io->latent, T, T, &rows, io->q_abs, sel, stride, cnt, 0, 0, T, 0, io->ctx, lse, 1, st,
-                       true);
+    return launch_attn(cfg, &io->latent, T, T, &rows, io->q_abs, sel, stride, cnt, 0, 0, T, 0, io->ctx, lse, 1, st);
 }
 
 int wl_attn_layer_prefill(const wl_attn_cfg* cfg, wl_attn_prefill_io* io, int32_t owner, uint32_t layer,
@@ -1387,6 +1415,12 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     // global top-k can read the candidate slots as segmented rows).
     const bool p2p = comm->p2p && B <= kP2PMaxRows && k <= kP2PMaxK && (k % 32) == 0 &&
                      (int64_t)N * k <= kTopkRegMax;
+    // Phase stamps (diagnostics): start | indexer | local top-k | candidate
+    // exchange | global top-k | attention | (o, lse) reduce-scatter | all-gather
+    // | unpack (peer exchange); the NCCL exchange stamps start | indexer |
+    // local top-k | candidate exchange | global top-k | attention | local merge
+    // | all-gather | merge. A consumer layer has no indexer, top-k or
+    // candidate stamps.
     WL_PHASE(st);
 
     const int32_t* gsel = nullptr;
@@ -1410,7 +1444,6 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st, &w.topk, fuse,
                                 cand_direct ? &co : nullptr))
             return e;
-        WL_PHASE(st);
         if (!cand_direct) {
             gather_candidates_kernel<<<dim3((unsigned)ceil_div(k, 256), B), 256, 0, st>>>(
                 index, T, w.sel, kl, w.cnt, k, t0, w.cand_score, w.cand_idx);
@@ -1456,7 +1489,6 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
                     return e;
             }
         }
-        WL_PHASE(st);
         if (io->index_out) {
             // Local scores into the caller's buffer (this rank's window).
             for (int32_t b = 0; b < B; ++b)
@@ -1484,8 +1516,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
             gstride = Tg;
         }
     }
-    // Local partial over this rank's window, merged over its splits straight
-    // into the exchange layout [row][64 * 512 + 64].
+    // Attention over this rank's part of the global list (its window of keys).
     long long n_max = Tg;
     int32_t sel_n = 0;
     if (io->mode == WL_MODE_OWNER) n_max = kg;
@@ -1493,24 +1524,41 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         n_max = (gcnt || !(io->sel_flags & WL_SEL_CANONICAL)) ? gstride : io->sel_n;
         sel_n = io->sel_n;
     }
+    if (p2p) {
+        // Split-K partials, then the (o, lse) reduce-scatter over heads and the
+        // all-gather of the merged slices (xmerge.cuh).
+        int32_t nsplit = 1;
+        if (int e = decode_attn(cfg, io, w, t0, Tg, gsel, gcnt, sel_n, gstride, n_max, st, kMaxSplits, &nsplit))
+            return e;
+        WL_PHASE(st);
+        wl::XMergeParams xp{};
+        xp.a = p2p_args(comm);
+        xp.B = B;
+        xp.hs = wl::AT_H / N;
+        xp.nsplit = nsplit;
+        xp.o_part = w.o_part;
+        xp.lse_part = w.lse_part;
+        xp.part_off = p2p_off_part(N);
+        xp.part_slot = p2p_xslot(N);
+        xp.gath_off = p2p_off_gath(N);
+        xp.gath_slot = p2p_xslot(N);
+        xp.ctx = io->ctx;
+        xp.lse = io->lse;
+        WL_CUDA_TRY(launch_pdl(wl::xscatter_kernel, dim3(wl::AT_H, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
+        WL_PHASE(st);
+        WL_CUDA_TRY(launch_pdl(wl::xgather_kernel, dim3(xp.hs, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
+        WL_PHASE(st);
+        WL_CUDA_TRY(launch_pdl(wl::xunpack_kernel, dim3(wl::AT_H, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
+        WL_PHASE(st);
+        return WL_OK;
+    }
+    // NCCL: local partial merged over its splits straight into the exchange
+    // layout [row][64 * 512 + 64], all-gathered, then merged over the ranks.
     if (int e = decode_local(cfg, io, w, t0, Tg, w.part_send, w.part_send + wl::AT_H * wl::AT_DV, gsel, gcnt, sel_n,
                              gstride, n_max, st, rowsz, rowsz))
         return e;
     const size_t per = (size_t)B * rowsz;
     float* lse = io->lse ? io->lse : w.lse_tmp;
-    if (p2p) {
-        WL_PHASE(st);
-        if (int e = launch_put(comm, wl::XCH_PART, w.part_send, per * 4, p2p_off_part(N), kP2PPartSlot,
-                               (long long)N * kP2PPartSlot, st))
-            return e;
-        WL_PHASE(st);
-        const wl::P2PRecv rp = p2p_recv(comm, wl::XCH_PART, p2p_off_part(N), kP2PPartSlot, (long long)N * kP2PPartSlot);
-        const int em = launch_merge(nullptr, nullptr, B, N, rowsz, rp.slot_words, rowsz, rp.slot_words, wl::AT_H,
-                                    wl::AT_DV, io->ctx, lse, st, 0, 0, &rp, wl::AT_H * wl::AT_DV);
-        WL_PHASE(st);
-        return em;
-    }
-    WL_PHASE(st);
     if (ncclAllGather(w.part_send, w.part_recv, per, ncclFloat32, comm->comm, st) != ncclSuccess) return WL_ERR_NCCL;
     WL_PHASE(st);
     // part_recv: [rank][row][64*512 + 64]
@@ -1520,47 +1568,6 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     return em;
 }
 
-#ifdef WL_TRACE
-// One candidate-type put of `bytes` from `src` (exchange microbenchmarks).
-int wl_trace_put(wl_comm* c, const void* src, size_t bytes, void* stream) {
-    if (!c || !c->p2p) return WL_ERR_ARG;
-    return launch_put(c, wl::XCH_CAND, src, bytes, wl::P2P_OFF_CAND, kP2PCandSlot, 0, static_cast<cudaStream_t>(stream));
-}
-void wl_phase_begin() {
-    if (!g_ph_buf) cudaMalloc(&g_ph_buf, 32 * sizeof(unsigned long long));
-    g_ph_n = 0;
-}
-// Microseconds between consecutive stamps of the last stamped call (or graph
-// replay); returns their count. Stops stamping.
-int wl_phase_read(float* us, int max_n) {
-    const int n = g_ph_n;
-    g_ph_n = -1;
-    if (n <= 1 || !g_ph_buf) return 0;
-    unsigned long long h[32];
-    cudaDeviceSynchronize();
-    cudaMemcpy(h, g_ph_buf, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
-    int m = 0;
-    for (int i = 1; i < n && m < max_n; ++i) us[m++] = (float)((h[i] - h[i - 1]) * 1e-3);
-    return m;
-}
-int wl_pftrace_set(long long* buf) {
-    return cudaMemcpyToSymbol(wl::g_trace_pf, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
-}
-int wl_atrace_set(long long* buf) {
-    return cudaMemcpyToSymbol(wl::g_trace_attn, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
-}
-int wl_ktrace_set(unsigned long long* buf) {
-    return cudaMemcpyToSymbol(wl::g_ktrace, &buf, sizeof(buf)) == cudaSuccess ? WL_OK : WL_ERR_CUDA;
-}
-int wl_trace_set(long long* buf) {
-    long long* b2 = buf ? buf + 1024 : nullptr;
-    return cudaMemcpyToSymbol(wl::g_trace, &buf, sizeof(buf)) == cudaSuccess &&
-                   cudaMemcpyToSymbol(wl::g_trace_topk, &b2, sizeof(b2)) == cudaSuccess
-               ? WL_OK
-               : WL_ERR_CUDA;
-}
-#endif
-
 // ---- decode attention without any allocation ------------------------------------------
 // For callers that cannot allocate device memory at all (for example code that
 // runs where cudaMalloc is not allowed, or an embedding runtime that owns every
@@ -1568,8 +1575,9 @@ int wl_trace_set(long long* buf) {
 // the decode attention live in this fixed array instead of a caller workspace.
 // Every GPU that loads the library holds it until the process exits.
 constexpr int kNoAllocMaxRows = 4;
-constexpr size_t kNoAllocPartFloats = (size_t)kNoAllocMaxRows * kMaxSplits * wl::AT_H * wl::AT_DV;
-constexpr size_t kNoAllocLseFloats = (size_t)kNoAllocMaxRows * kMaxSplits * wl::AT_H;
+constexpr int kNoAllocMaxSplits = 16;
+constexpr size_t kNoAllocPartFloats = (size_t)kNoAllocMaxRows * kNoAllocMaxSplits * wl::AT_H * wl::AT_DV;
+constexpr size_t kNoAllocLseFloats = (size_t)kNoAllocMaxRows * kNoAllocMaxSplits * wl::AT_H;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocPartFloats + kNoAllocLseFloats +
                                                          (size_t)kNoAllocMaxRows * wl::AT_H];
 static std::mutex g_noalloc_mu;
@@ -1600,8 +1608,9 @@ int wl_attn_decode_noalloc(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         }
         base = g_noalloc_ptr[dev];
     }
-    // Every partial slot the attention kernel may touch is written by it
-    // (empty splits write zeros and -inf), so nothing needs clearing.
+    // Nothing needs clearing: the attention kernel writes the lse of every
+    // split slot it may use (-inf for an empty split), and the merge reads the
+    // o of non-empty splits only, which the same call has written.
     DecodeWs w{};
     w.o_part = base;
     w.lse_part = base + kNoAllocPartFloats;
@@ -1618,10 +1627,40 @@ int wl_attn_decode_noalloc(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     }
     float* lse = io->lse ? io->lse : w.lse_tmp;
     return decode_local(cfg, io, w, 0, io->T, io->ctx, lse, sel, io->sel_n_in, sel_n, stride, n_max,
-                        static_cast<cudaStream_t>(stream));
+                        static_cast<cudaStream_t>(stream), 0, 0, kNoAllocMaxSplits);
 }
 
 // ---- diagnostics ---------------------------------------------------------------------------
+int wl_diag_set_wait_limit(int64_t cycles) {
+    const long long v = cycles > 0 ? (long long)cycles : wl::WL_WAIT_CYCLES_DEFAULT;
+    WL_CUDA_TRY(cudaMemcpyToSymbol(wl::g_wait_cycles, &v, sizeof(v)));
+    return WL_OK;
+}
+
+int wl_diag_phase_stamps(uint64_t* dev_buf, int32_t cap) {
+    if (dev_buf && cap <= 0) return WL_ERR_ARG;
+    std::lock_guard<std::mutex> lk(g_ph_mu);
+    g_ph_buf = reinterpret_cast<unsigned long long*>(dev_buf);
+    g_ph_cap = dev_buf ? cap : 0;
+    g_ph_n = 0;
+    return WL_OK;
+}
+
+int32_t wl_diag_phase_count(void) {
+    std::lock_guard<std::mutex> lk(g_ph_mu);
+    return g_ph_n;
+}
+
+int wl_diag_merge_exchange(const void* region, int64_t slot_words, const uint32_t* epoch_ctr, int32_t n_rows,
+                           int32_t n_parts, float* ctx, float* lse, void* stream) {
+    if (!region || !epoch_ctr || !ctx || slot_words <= 0 || !aligned16(region)) return WL_ERR_ARG;
+    const int64_t rowsz = wl::AT_H * wl::AT_DV + wl::AT_H;
+    if (slot_words < (int64_t)n_rows * rowsz) return WL_ERR_ARG;
+    const wl::P2PRecv rp{static_cast<const uint64_t*>(region), slot_words, 0, epoch_ctr};
+    return launch_merge(nullptr, nullptr, n_rows, n_parts, rowsz, slot_words, rowsz, slot_words, wl::AT_H,
+                        wl::AT_DV, ctx, lse, static_cast<cudaStream_t>(stream), 0, 0, &rp, wl::AT_H * wl::AT_DV);
+}
+
 int wl_device_error(int32_t clear, uint32_t* detail) {
     WL_CUDA_TRY(cudaDeviceSynchronize());
     unsigned w = 0;
