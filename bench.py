@@ -718,7 +718,26 @@ def side_configs(torch, A, _lib, device, stream):
     del d
     torch.cuda.empty_cache()
     out["around"] = around_kernels(torch, A, device, stream)
+    out["reference_gpu_kernels"] = reference_gpu_kernels()
     return out
+
+
+def reference_gpu_kernels():
+    """The reference's own CUDA kernels for the same block (indexer scores,
+    combine, one-CTA top-k, index mask, mla_decode_absorbed; bf16 keys, fp32
+    latent cache), compiled unmodified for sm_100a into oracle/_ref by
+    oracle/build_ref.sh and timed there with CUDA events, batch 1. The GPU row
+    to compare configs 0-2 with; absent when the binary was not built."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_kernels_bench")
+    if not os.path.exists(exe):
+        return {"unavailable": "oracle/_ref/ref_kernels_bench not built (needs the reference sources)"}
+    try:
+        r = subprocess.run([exe, "10"], capture_output=True, text=True, timeout=300)
+        rows = [json.loads(x) for x in r.stdout.splitlines() if x.startswith("{")]
+        return {"source": "reference src/glm_kernels.cuh + src/glm_layer_runner.cuh, unmodified, sm_100a",
+                "rows": rows, "rc": r.returncode}
+    except Exception as ex:  # reported, not hidden
+        return {"unavailable": f"{type(ex).__name__}: {ex}"}
 
 
 def around_kernels(torch, A, device, stream):

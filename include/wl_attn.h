@@ -338,7 +338,8 @@ int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, in
  * (per head: 192 W_UK rows, then 256 W_UV rows), 16-byte aligned.
  *
  * wl_mla_absorb_q: for n query rows, q fp32 [n][n_heads][256] (qk_nope 192 |
- * roped qk_rope 64; row stride q_row_stride floats) ->
+ * roped qk_rope 64; 16-byte aligned, row stride q_row_stride floats, a
+ * multiple of 4) ->
  *   q_abs[r][h][c]       = sum_{d<192} q[r][h][d] * kv_b[h*448 + d][c]   (c < 512)
  *   q_abs[r][h][512 + j] = q[r][h][192 + j]                              (j < 64)
  * in bf16 (row stride q_abs_row_stride elements): the absorbed query the
@@ -348,7 +349,12 @@ int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, in
  * wl_mla_project_v: ctx fp32 [n][n_heads][512] (row stride ctx_row_stride
  * floats, a multiple of 4) -> out[r][h][v] = sum_c ctx[r][h][c] *
  * kv_b[h*448 + 192 + v][c], fp32 [n][n_heads][256] (row stride out_row_stride).
- * Replaces mla_project_v (glm_layer_runner.cuh:217-234). fp32 accumulation. */
+ * Replaces mla_project_v (glm_layer_runner.cuh:217-234). fp32 accumulation.
+ *
+ * Both run on the tensor cores: the bf16 weight slice is the MMA's A operand
+ * and each fp32 activation enters as three bf16 terms (hi + mid + lo, 24
+ * significant bits), so the products accumulate in fp32 as exactly as the
+ * reference's fp32 FMA loop (wl_indexer_query's projection likewise). */
 int wl_mla_absorb_q(const wl_attn_cfg* cfg, int32_t n, const float* q, int64_t q_row_stride,
                     const void* kv_b, void* q_abs, int64_t q_abs_row_stride, void* stream);
 int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_t ctx_row_stride,

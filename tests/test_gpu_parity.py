@@ -680,7 +680,7 @@ def _kv_b(rng):
     return o.bf16_round((rng.standard_normal((64 * 448, 512)) * 0.05).astype(np.float32))
 
 
-@pytest.mark.parametrize("n", [1, 8, 13])
+@pytest.mark.parametrize("n", [1, 8, 13, 40])
 def test_absorb_q_vs_oracle(n):
     """fp32 accumulation, bf16 output: within one bf16 ulp of the output scale
     (the rounding of the stored value), the roped part copied exactly."""
@@ -693,7 +693,7 @@ def test_absorb_q_vs_oracle(n):
     assert np.array_equal(got[..., 512:], o.bf16_round(q[..., 192:]))
 
 
-@pytest.mark.parametrize("n", [1, 8, 13])
+@pytest.mark.parametrize("n", [1, 8, 13, 40])
 def test_project_v_vs_oracle(n):
     rng = np.random.default_rng(200 + n)
     ctx = rng.standard_normal((n, 64, 512)).astype(np.float32)
@@ -743,7 +743,7 @@ def test_indexer_query_golden_inputs():
     _query_case(query_inputs())
 
 
-@pytest.mark.parametrize("n", [1, 13])
+@pytest.mark.parametrize("n", [1, 13, 40])
 def test_indexer_query_glm_hidden(n):
     rng = np.random.default_rng(300 + n)
     ang = rng.uniform(0, 2 * np.pi, (n, 32))

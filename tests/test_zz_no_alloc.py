@@ -110,7 +110,7 @@ def test_noalloc_without_lse_and_with_device_counts():
     torch.cuda.synchronize()
     assert torch.equal(keep["ctx"], got["ctx"])
     for b, n in enumerate(counts):
-        rc, _ = o.mla_absorbed(inps[b]["q_abs"], inps[b]["c_kv"], inps[b]["k_rot"], sel[b, :n], 1 / 16)
+        rc, _ = o.mla_sparse(inps[b]["q_abs"], inps[b]["c_kv"], inps[b]["k_rot"], sel[b, :n], 1 / 16)
         assert o.bf16_ulp_error(rc, keep["ctx"].cpu().numpy()[b]) <= ULP_TOL
     st, word = A.device_error(clear=True)
     assert st == _lib.WL_OK, f"device error word 0x{word:08x}"

@@ -25,10 +25,10 @@
 #include "indexer.cuh"
 #include "mla_attn.cuh"
 #include "mla_attn64.cuh"
-#include "mla_proj.cuh"
 #include "p2p.cuh"
 #include "topk.cuh"
 #include "xmerge.cuh"
+#include "gemv_tc.cuh"
 
 namespace {
 
@@ -108,12 +108,12 @@ int ensure_attrs() {
                                      wl::TOPKM_PART_SMEM));
     WL_CUDA_TRY(cudaFuncSetAttribute(wl::topk_threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      wl::TOPKM_THR_SMEM));
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::idx_query_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     wl::IQ_SMEM));
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_absorb_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     wl::AqLayout::BYTES));
-    WL_CUDA_TRY(cudaFuncSetAttribute(wl::mla_project_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     wl::PvLayout::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::gemv_tc_kernel<wl::GV_IDXQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::GvShape<wl::GV_IDXQ>::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::gemv_tc_kernel<wl::GV_PROJV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::GvShape<wl::GV_PROJV>::BYTES));
+    WL_CUDA_TRY(cudaFuncSetAttribute(wl::gemv_tc_kernel<wl::GV_ABSQ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     wl::GvShape<wl::GV_ABSQ>::BYTES));
     int sms = 0;
     WL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     g_sm_count[dev] = sms;
@@ -183,6 +183,55 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     cfg.attrs = at;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// A bf16 matrix [outer][inner] (row stride `row_elems`) as a 2D tensor map with
+// {box_inner, box_outer} boxes, 128B swizzle (box_inner = 64: 128-byte rows).
+int encode_bf16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_elems,
+                   uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn enc = encode_tiled_fn();
+    if (!enc) return WL_ERR_CUDA;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_elems * 2};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::fprintf(stderr, "wl_attn: cuTensorMapEncodeTiled (weights) failed (%d)\n", (int)r);
+        return WL_ERR_CUDA;
+    }
+    return WL_OK;
+}
+
+// One of the tensor-core weight products (gemv_tc.cuh), programmatic launch;
+// the query projection as 4-CTA clusters along K.
+template <int MODE>
+int launch_gemv(const wl::GvParams& p, dim3 grid, cudaStream_t st) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(wl::GV_THREADS);
+    cfg.dynamicSmemBytes = wl::GvShape<MODE>::BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (MODE == wl::GV_IDXQ) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = wl::GV_CL;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    WL_CUDA_TRY(cudaLaunchKernelEx(&cfg, wl::gemv_tc_kernel<MODE>, p));
+    return WL_OK;
 }
 
 // Zeroes n_rows fused top-k histograms (HB + 1 words each) in the launch chain.
@@ -983,10 +1032,16 @@ int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, in
         return WL_ERR_ARG;
     if (int e = ensure_attrs()) return e;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    WL_CUDA_TRY(launch_pdl(wl::idx_query_kernel, dim3(wl::IQ_H * wl::IQ_D / wl::IQ_DIMS), dim3(wl::IQ_THREADS),
-                           wl::IQ_SMEM, st, (int)n, q_resid, (long long)q_resid_row_stride,
-                           static_cast<const __nv_bfloat16*>(wq_b), cos, sin, static_cast<__nv_bfloat16*>(q_idx),
-                           (long long)wl::IQ_H * wl::IQ_D));
+    wl::GvParams gp{};
+    if (int e = encode_bf16_2d(&gp.tm_w, wq_b, wl::IQ_QL, wl::IQ_H * wl::IQ_D, wl::IQ_QL, 64, wl::GV_M)) return e;
+    gp.n = n;
+    gp.x = q_resid;
+    gp.x_row = q_resid_row_stride;
+    gp.out = q_idx;
+    gp.out_row = (long long)wl::IQ_H * wl::IQ_D;
+    gp.cos = cos;
+    gp.sin = sin;
+    if (int e = launch_gemv<wl::GV_IDXQ>(gp, dim3(wl::GV_CL, wl::IQ_H * wl::IQ_D / wl::GV_M), st)) return e;
     const float head_scale = (float)(1.0 / std::sqrt((double)wl::IQ_H));
     WL_CUDA_TRY(launch_pdl(wl::idx_head_weights_kernel, dim3(wl::IQ_H, n), dim3(256), 0, st, (int)n, x,
                            (long long)x_row_stride, weights_proj, (int)hidden, head_scale, w_idx, (long long)wl::IQ_H));
@@ -999,18 +1054,22 @@ int wl_mla_absorb_q(const wl_attn_cfg* cfg, int32_t n, const float* q, int64_t q
     if (!cfg_supported(cfg)) return cfg ? WL_ERR_UNSUPPORTED : WL_ERR_ARG;
     if (n < 0) return WL_ERR_ARG;
     if (n == 0) return WL_OK;
-    if (!q || !kv_b || !q_abs || (reinterpret_cast<uintptr_t>(kv_b) & 3) ||
-        (reinterpret_cast<uintptr_t>(q) & 3) || (reinterpret_cast<uintptr_t>(q_abs) & 1) ||
+    if (!q || !kv_b || !q_abs || (reinterpret_cast<uintptr_t>(kv_b) & 3) || !aligned16(q) || (q_row_stride & 3) ||
+        (reinterpret_cast<uintptr_t>(q_abs) & 1) ||
         q_row_stride < wl::PJ_H * wl::PJ_QK || q_abs_row_stride < wl::PJ_H * (wl::PJ_L + wl::PJ_ROPE) ||
         !aligned16(kv_b) || (reinterpret_cast<uintptr_t>(q_abs) & 7) || (q_abs_row_stride & 3))
         return WL_ERR_ARG;
     if (int e = ensure_attrs()) return e;
-    WL_CUDA_TRY(launch_pdl(wl::mla_absorb_q_kernel, dim3(wl::AQ_SPLIT, wl::PJ_H), dim3(wl::PJ_THREADS),
-                           wl::AqLayout::BYTES,
-                           static_cast<cudaStream_t>(stream), (int)n, q, (long long)q_row_stride,
-                           static_cast<const __nv_bfloat16*>(kv_b), static_cast<__nv_bfloat16*>(q_abs),
-                           (long long)q_abs_row_stride));
-    return WL_OK;
+    wl::GvParams gp{};
+    if (int e = encode_bf16_2d(&gp.tm_w, kv_b, wl::PJ_L, (uint64_t)wl::PJ_H * wl::PJ_KVB_ROWS, wl::PJ_L, 64,
+                               wl::PJ_NOPE))
+        return e;
+    gp.n = n;
+    gp.x = q;
+    gp.x_row = q_row_stride;
+    gp.out = q_abs;
+    gp.out_row = q_abs_row_stride;
+    return launch_gemv<wl::GV_ABSQ>(gp, dim3(wl::PJ_L / wl::GV_M, wl::PJ_H), static_cast<cudaStream_t>(stream));
 }
 
 int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_t ctx_row_stride,
@@ -1023,11 +1082,16 @@ int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_
         out_row_stride < wl::PJ_H * wl::PJ_V)
         return WL_ERR_ARG;
     if (int e = ensure_attrs()) return e;
-    WL_CUDA_TRY(launch_pdl(wl::mla_project_v_kernel, dim3(wl::PV_SPLIT, wl::PJ_H), dim3(wl::PJ_THREADS),
-                           wl::PvLayout::BYTES,
-                           static_cast<cudaStream_t>(stream), (int)n, ctx, (long long)ctx_row_stride,
-                           static_cast<const __nv_bfloat16*>(kv_b), out, (long long)out_row_stride));
-    return WL_OK;
+    wl::GvParams gp{};
+    if (int e = encode_bf16_2d(&gp.tm_w, kv_b, wl::PJ_L, (uint64_t)wl::PJ_H * wl::PJ_KVB_ROWS, wl::PJ_L, 64,
+                               wl::GV_M))
+        return e;
+    gp.n = n;
+    gp.x = ctx;
+    gp.x_row = ctx_row_stride;
+    gp.out = out;
+    gp.out_row = out_row_stride;
+    return launch_gemv<wl::GV_PROJV>(gp, dim3(wl::PJ_V / wl::GV_M, wl::PJ_H), static_cast<cudaStream_t>(stream));
 }
 
 // ---- the cache write path -------------------------------------------------------------
