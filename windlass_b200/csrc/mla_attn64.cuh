@@ -116,6 +116,30 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const long long lraw = (long long)p.len0 + (long long)(r % p.rows_per_seq) * p.len_step;
     const long long len = lraw < p.len_T ? lraw : p.len_T;
     const int* list = p.sel ? p.sel + (long long)r * p.sel_stride : nullptr;
+    // Set-up that touches no global memory runs before the wait on the
+    // previous kernel (under programmatic launch it overlaps that kernel's
+    // tail): the barriers and the tensor memory (see pdl_wait in ptx.cuh for
+    // why allocating here cannot deadlock).
+    if (tid == 0) {
+        for (int b = 0; b < PF_NBUF; ++b) {
+            mbar_init(kfull + b, PF_GATHER);  // the gather threads
+            mbar_init(kfree + b, 1);          // the P.V commit
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(sfull + b, 1);    // the QK commit
+            mbar_init(sfree + b, 128);  // the softmax threads
+        }
+        mbar_init(pready, 128);
+        mbar_init(pvdone, 1);
+        mbar_init(qload, 1);
+        mbar_init(qtmem, 128);  // the softmax threads, once the query is in tensor memory
+        fence_mbar_init();
+    }
+    if (warp == PF_MMA_WARP) tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
     pdl_wait();
     pdl_trigger();
     // Entry range [e0, e1) of the list (or key range) inside the key window
@@ -180,33 +204,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         // An empty split: lse = -inf marks it; its o is never read (the merge
         // skips parts of weight zero), so it is not written.
         if (tid < AT_H) lse_out[tid] = -INFINITY;
+        if (warp == PF_MMA_WARP) {
+            tc_fence_after();
+            tmem_dealloc(tmem, L::TMEM_COLS);
+        }
         return;
     }
     const int n_tiles = (n_keys + PF_TILE - 1) / PF_TILE;
 
     if (tid == 0) {
-        for (int b = 0; b < PF_NBUF; ++b) {
-            mbar_init(kfull + b, PF_GATHER);  // the gather threads
-            mbar_init(kfree + b, 1);          // the P.V commit
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(sfull + b, 1);    // the QK commit
-            mbar_init(sfree + b, 128);  // the softmax threads
-        }
-        mbar_init(pready, 128);
-        mbar_init(pvdone, 1);
-        mbar_init(qload, 1);
-        mbar_init(qtmem, 128);  // the softmax threads, once the query is in tensor memory
-        fence_mbar_init();
         // the row's absorbed query [64][576]: 9 TMA boxes into the staging tile
         mbar_expect_tx(qload, AT_CHUNKS * L::CHUNK);
         for (int c = 0; c < AT_CHUNKS; ++c) tma_load2d(sQstage + (uint32_t)c * L::CHUNK, &pp.tm_q, c * 64, r * AT_H, qload);
     }
-    if (warp == PF_MMA_WARP) tmem_alloc(tmem_slot, L::TMEM_COLS);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
     const __nv_bfloat16* ckv = p.c_kv + (long long)seq * p.ckv_seq;
     const __nv_bfloat16* krt = p.k_rot + (long long)seq * p.krot_seq;
 
@@ -452,7 +462,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                 for (int k = 0; k < AT_DV / 32; ++k)
                     tma_store2d(&pp.tm_o, 32 * k, row0, sK + (uint32_t)k * (AT_H * 128));
                 asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // written before the CTA retires
+                // the staging buffer must stay until the copies have read it; the
+                // writes themselves complete with the grid
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             }
         }
     }

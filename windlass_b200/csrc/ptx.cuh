@@ -242,6 +242,11 @@ __device__ __forceinline__ void cluster_sync_all() {
 // kernel may touch, and only then pdl_trigger() — so that, transitively, every
 // grid before its predecessor has completed once a dependent starts. Both are
 // no-ops for a kernel launched without the attribute.
+// Tensor memory: every kernel of this library that allocates tensor memory
+// does so before its pdl_trigger(). A dependent launches only once every CTA
+// of its predecessor has triggered, so by then each of those CTAs holds its
+// columns; an early dependent CTA that allocates can only wait for a
+// predecessor CTA to finish and free them, never the other way round.
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
