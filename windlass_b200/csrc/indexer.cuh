@@ -48,7 +48,7 @@ __device__ __forceinline__ int rows_len(int r, int rows_per_seq, int len0, int l
 //   warp 0      TMA producer: the rows' bf16 queries (bulk copy during setup),
 //               then each tile's fp8 keys as one 128 x 128-byte box with 128B
 //               swizzle (a tensor-map load; rows past the cache end read as
-//               zero) into ring stage i % IDX_NS (160 KB of keys in flight)
+//               zero) into ring stage i % IDX_NS (128 KB of keys in flight)
 //   warp 1      MMA issuer:   tcgen05.mma kind::f8f6f4 straight on the fp8 keys
 //               (M = 128 keys, K = 32 per instruction), one chain of 4 per
 //               tile: N = 64 R = each row's hi and lo e4m3 query terms
@@ -70,7 +70,7 @@ __device__ __forceinline__ int rows_len(int r, int rows_per_seq, int len0, int l
 // CTA counts into shared memory and adds its nonzero bins to the row's global
 // histogram at the end (warp-aggregating global atomics with __match_any_sync
 // measured slower).
-constexpr int IDX_NS = 10;   // TMA stages of fp8 keys
+constexpr int IDX_NS = 8;    // TMA stages of fp8 keys
 constexpr int IDX_CTAS_PER_SM = 1;
 constexpr int TOPK_HIST_BITS = 13;
 constexpr int TOPK_HIST_BINS = 1 << TOPK_HIST_BITS;

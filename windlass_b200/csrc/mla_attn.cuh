@@ -87,13 +87,16 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
     const float inv = W > 0.f ? 1.f / W : 0.f;
     const long long oi = (long long)r * p.row_stride + (long long)h * p.dv + c;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    // Parts in groups of 8: all loads of a group are issued before any use.
-    for (int s0 = 0; s0 < p.n_parts; s0 += 8) {
-        float4 v[8];
-        float wv[8];
-        uint64_t raw[8][4];
+    // Parts in groups of G (16 plain, 8 in the exchange format): all loads of a
+    // group are issued before any use, so a row of up to 16 splits costs one
+    // round of L2 latency.
+    constexpr int G = LL ? 8 : 16;
+    for (int s0 = 0; s0 < p.n_parts; s0 += G) {
+        float4 v[G];
+        float wv[G];
+        uint64_t raw[LL ? G : 1][4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < G; ++j) {
             const int s = s0 + j;
             wv[j] = __shfl_sync(0xffffffffu, wl, s & 31) * inv;
             const bool use = s < p.n_parts && wv[j] != 0.f;  // empty parts are never read
@@ -116,7 +119,7 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
         }
         if constexpr (LL) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < G; ++j) {
                 if (wv[j] == 0.f) continue;
                 const uint64_t* w = lb + oi + (long long)(s0 + j) * p.part_stride;
                 v[j] = make_float4(__uint_as_float(ll_wait1(w, epoch, raw[j][0], 21)),
@@ -126,7 +129,7 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
             }
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < G; ++j) {
             acc.x = fmaf(wv[j], v[j].x, acc.x);
             acc.y = fmaf(wv[j], v[j].y, acc.y);
             acc.z = fmaf(wv[j], v[j].z, acc.z);

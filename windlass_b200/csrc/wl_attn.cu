@@ -285,7 +285,17 @@ int rows_ok(const wl_rows* r, int32_t T) {
 // attention is latency-bound at decode batches), at most `cap`, and no more
 // than one per 64-key tile of the longest list. The kernel spreads each row's
 // entries (inside its key window) evenly over these CTAs.
+// WL_ATTN_SPLITS=n in the environment caps it further (a tuning knob).
+int splits_env_cap() {
+    static const int v = [] {
+        const char* e = std::getenv("WL_ATTN_SPLITS");
+        const int n = e ? std::atoi(e) : 0;
+        return n > 0 ? n : 1 << 30;
+    }();
+    return v;
+}
 int splits_for(int32_t rows, long long n_max, int cap) {
+    if (cap > splits_env_cap()) cap = splits_env_cap();
     long long s = sm_count() / (rows > 0 ? rows : 1);
     s = s < 1 ? 1 : s;
     s = s > cap ? cap : s;
