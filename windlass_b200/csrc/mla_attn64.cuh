@@ -142,6 +142,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const uint32_t tmem = *tmem_slot;
     pdl_wait();
     pdl_trigger();
+    if (tid == 0) {
+        // the row's absorbed query [64][576]: 9 TMA boxes into the staging tile,
+        // issued before the split's range is known (it overlaps that search)
+        mbar_expect_tx(qload, AT_CHUNKS * L::CHUNK);
+        for (int c = 0; c < AT_CHUNKS; ++c) tma_load2d(sQstage + (uint32_t)c * L::CHUNK, &pp.tm_q, c * 64, r * AT_H, qload);
+    }
     // Entry range [e0, e1) of the list (or key range) inside the key window
     // [win_lo, win_hi) — a 32-ary lower-bound search on the ascending list by
     // warps 0 and 1 when the window cuts the row — then this CTA's split of it.
@@ -204,6 +210,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         // An empty split: lse = -inf marks it; its o is never read (the merge
         // skips parts of weight zero), so it is not written.
         if (tid < AT_H) lse_out[tid] = -INFINITY;
+        if (tid == 0) mbar_wait_fast(qload, 0, 39);  // the query copy lands before the CTA leaves
         if (warp == PF_MMA_WARP) {
             tc_fence_after();
             tmem_dealloc(tmem, L::TMEM_COLS);
@@ -211,12 +218,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         return;
     }
     const int n_tiles = (n_keys + PF_TILE - 1) / PF_TILE;
-
-    if (tid == 0) {
-        // the row's absorbed query [64][576]: 9 TMA boxes into the staging tile
-        mbar_expect_tx(qload, AT_CHUNKS * L::CHUNK);
-        for (int c = 0; c < AT_CHUNKS; ++c) tma_load2d(sQstage + (uint32_t)c * L::CHUNK, &pp.tm_q, c * 64, r * AT_H, qload);
-    }
     const __nv_bfloat16* ckv = p.c_kv + (long long)seq * p.ckv_seq;
     const __nv_bfloat16* krt = p.k_rot + (long long)seq * p.krot_seq;
 
