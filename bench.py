@@ -711,7 +711,10 @@ def side_configs(torch, A, _lib, device, stream):
     att_flops = n_q * 2048 * 64 * (2 * 576 + 2 * 512)
     tf = (idx_flops + att_flops) / (ms * 1e-3) / 1e12
     pk = peaks.get("bf16_tflops", 1590.0)
+    gather = n_q * 2048 * 1152  # bytes of latent rows the attention gathers (mostly L2 hits)
     out["cfg3_prefill"] = {"ms": round(ms, 3), "tflops": round(tf, 1),
+                           "attn_gather_bytes": gather,
+                           "attn_gather_gbs": round(gather / (ms * 1e-3) / 1e9, 1),
                            "idx_gflop": round(idx_flops / 1e9, 1), "attn_gflop": round(att_flops / 1e9, 1),
                            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": pk, "unit": "TFLOP/s",
                                         "frac": round(tf / pk, 4), "peak_source": src + " bf16 burst"}}
