@@ -354,7 +354,10 @@ int wl_indexer_query(const wl_attn_cfg* cfg, int32_t n, const float* q_resid, in
  * Both run on the tensor cores: the bf16 weight slice is the MMA's A operand
  * and each fp32 activation enters as three bf16 terms (hi + mid + lo, 24
  * significant bits), so the products accumulate in fp32 as exactly as the
- * reference's fp32 FMA loop (wl_indexer_query's projection likewise). */
+ * reference's fp32 FMA loop (wl_indexer_query's projection likewise).
+ * Under programmatic launch the weights (kv_b, wq_b) are fetched before the
+ * wait on the previous kernel: a kernel that writes them must not signal an
+ * early launch of its dependents (ordinary kernels do not). */
 int wl_mla_absorb_q(const wl_attn_cfg* cfg, int32_t n, const float* q, int64_t q_row_stride,
                     const void* kv_b, void* q_abs, int64_t q_abs_row_stride, void* stream);
 int wl_mla_project_v(const wl_attn_cfg* cfg, int32_t n, const float* ctx, int64_t ctx_row_stride,
@@ -436,6 +439,19 @@ int32_t wl_diag_phase_count(void);
  * run out. */
 int wl_diag_merge_exchange(const void* region, int64_t slot_words, const uint32_t* epoch_ctr, int32_t n_rows,
                            int32_t n_parts, float* ctx, float* lse, void* stream);
+
+/* The sharded decode's peer-memory (o, lse) combination (reduce-scatter by
+ * heads, then all-gather) for `nranks` ranks emulated on the current GPU:
+ * every stage runs for every emulated rank before the next stage starts, so
+ * no wait depends on a kernel still to come. o_part [nranks][batch][nsplit]
+ * [64][512] and lse_part [nranks][batch][nsplit][64] are each rank's split
+ * partials; ctx [nranks][batch][64][512] and lse [nranks][batch][64] receive
+ * every rank's result (all equal). `regions`: zeroed device memory of
+ * wl_diag_xmerge_bytes(nranks) bytes (every rank's exchange region and
+ * counters), 16-byte aligned. A test hook for the exchange's layout. */
+size_t wl_diag_xmerge_bytes(int32_t nranks);
+int wl_diag_xmerge(int32_t nranks, int32_t batch, int32_t nsplit, const float* o_part, const float* lse_part,
+                   void* regions, size_t regions_bytes, float* ctx, float* lse, void* stream);
 
 /* sizeof of each public struct, for binding checks: fills up to n entries in
  * the order cfg, latent_cache, index_cache, rows, index_share, decode_io,

@@ -94,3 +94,46 @@ def test_a_wait_that_runs_out_reports_timeout_and_the_gpu_stays_usable():
     assert A.device_error(clear=True)[0] == _lib.WL_OK
     rc, _ = o.mla_sparse(inp["q_abs"], inp["c_kv"], inp["k_rot"], out["sel"].cpu().numpy()[0], 1 / 16)
     assert o.bf16_ulp_error(rc, out["ctx"].cpu().numpy()[0]) <= 2.0
+
+
+@pytest.mark.parametrize("nranks", [2, 4, 8])
+def test_sharded_exchange_layout_on_one_gpu(nranks):
+    """The sharded decode's peer-memory combination of (o, lse) partials —
+    reduce-scatter by heads, then all-gather — with `nranks` ranks emulated on
+    one GPU (every stage runs for all ranks before the next one, so nothing
+    waits on a kernel still to come): every rank must end with the merge of
+    all ranks' split partials, equal to the merge kernel's on the same parts."""
+    A.device_error(clear=True)
+    L = _lib.lib()
+    B, S = 3, 4
+    rng = np.random.default_rng(nranks)
+    o = rng.standard_normal((nranks, B, S, 64, 512)).astype(np.float32)
+    lse = rng.uniform(-4, 4, (nranks, B, S, 64)).astype(np.float32)
+    lse[0, 1, 2, 7] = -np.inf  # an empty split
+    lse[:, 2, :, 9] = -np.inf  # a head with no keys anywhere
+    lse[1 % nranks, 0, :, :] = -np.inf  # a rank whose window held none of row 0
+    nb = L.wl_diag_xmerge_bytes(nranks)
+    regions = torch.zeros(nb // 8 + 1, dtype=torch.int64, device="cuda")
+    o_t, l_t = torch.from_numpy(o).cuda(), torch.from_numpy(lse).cuda()
+    ctx = torch.full((nranks, B, 64, 512), 7.0, device="cuda")
+    lo = torch.full((nranks, B, 64), 7.0, device="cuda")
+    _lib.check(L.wl_diag_set_wait_limit(20_000_000))  # ~10 ms: a layout error times out quickly
+    try:
+        for call in range(2):  # the second call runs on the first call's slots (next epoch)
+            _lib.check(L.wl_diag_xmerge(nranks, B, S, o_t.data_ptr(), l_t.data_ptr(), regions.data_ptr(), nb,
+                                        ctx.data_ptr(), lo.data_ptr(), torch.cuda.current_stream().cuda_stream))
+            torch.cuda.synchronize()
+            st, word = A.device_error(clear=True)
+            assert st == _lib.WL_OK, f"call {call}: device error word 0x{word:08x}"
+    finally:
+        _lib.check(L.wl_diag_set_wait_limit(0))
+    # reference: the merge kernel over all nranks * S parts of each row
+    parts_o = torch.from_numpy(o.transpose(1, 0, 2, 3, 4).reshape(B, nranks * S, 64, 512)).cuda()
+    parts_l = torch.from_numpy(lse.transpose(1, 0, 2, 3).reshape(B, nranks * S, 64)).cuda()
+    ref_c, ref_l = A.lse_merge(parts_o, parts_l)
+    for r in range(nranks):
+        np.testing.assert_allclose(ctx[r].cpu().numpy(), ref_c.cpu().numpy(), rtol=1e-5, atol=1e-5)
+        got_l, want_l = lo[r].cpu().numpy(), ref_l.cpu().numpy()
+        assert np.array_equal(np.isinf(got_l), np.isinf(want_l))
+        fin = np.isfinite(want_l)
+        np.testing.assert_allclose(got_l[fin], want_l[fin], rtol=0, atol=1e-5)

@@ -134,10 +134,12 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_tc_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    pdl_wait();
-    pdl_trigger();
     if (tid == 0) {
-        // the CTA's whole weight slice, one TMA box per chunk
+        // The CTA's whole weight slice, one TMA box per chunk, fetched before the
+        // programmatic wait so that it streams while the previous kernel
+        // finishes. No kernel of this library writes the weights, and a
+        // caller's kernel that does precedes this one as an ordinary stream
+        // predecessor (it signals no early launch), so it has finished first.
         for (int i = 0; i < S::A_LOADS; ++i) {
             mbar_expect_tx(afull + i, S::A_CHUNK);
             if (MODE == GV_IDXQ)
@@ -148,6 +150,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_tc_kernel(const __grid_con
                 tma_load2d(sA + i * S::A_CHUNK, &p.tm_w, (int)blockIdx.x * GV_M + 64 * i, h * 448, afull + i);
         }
     }
+    pdl_wait();  // the activations below may come from the previous kernel
+    pdl_trigger();
     // activation row r, element k of this CTA's K range
     auto xrow = [&](int r) -> const float* {
         if (MODE == GV_IDXQ) return p.x + (long long)r * p.x_row + crank * S::K;

@@ -1725,6 +1725,54 @@ int32_t wl_diag_phase_count(void) {
     return g_ph_n;
 }
 
+size_t wl_diag_xmerge_bytes(int32_t nranks) {
+    if (nranks < 2 || nranks > wl::P2P_MAX_RANKS || (wl::AT_H % nranks)) return 0;
+    return (size_t)nranks * (p2p_region_bytes(nranks) + 256);
+}
+
+int wl_diag_xmerge(int32_t nranks, int32_t batch, int32_t nsplit, const float* o_part, const float* lse_part,
+                   void* regions, size_t regions_bytes, float* ctx, float* lse, void* stream) {
+    const size_t need = wl_diag_xmerge_bytes(nranks);
+    if (!need || batch <= 0 || batch > kP2PMaxRows || nsplit <= 0 || nsplit > 32 || !o_part || !lse_part ||
+        !regions || regions_bytes < need || !ctx || !aligned16(regions))
+        return WL_ERR_ARG;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t rb = p2p_region_bytes(nranks);
+    uint8_t* base = static_cast<uint8_t*>(regions);
+    auto region = [&](int q) { return base + (size_t)q * rb; };
+    auto ctr = [&](int q) { return reinterpret_cast<unsigned*>(base + (size_t)nranks * rb + (size_t)q * 64); };
+    const int64_t part = (int64_t)batch * nsplit;
+    auto params = [&](int r) {
+        wl::XMergeParams xp{};
+        for (int q = 0; q < nranks; ++q) xp.a.region[q] = region(q);
+        xp.a.nranks = nranks;
+        xp.a.rank = r;
+        xp.a.ctr = ctr(r);
+        xp.B = batch;
+        xp.hs = wl::AT_H / nranks;
+        xp.nsplit = nsplit;
+        xp.o_part = o_part + (int64_t)r * part * wl::AT_H * wl::AT_DV;
+        xp.lse_part = lse_part + (int64_t)r * part * wl::AT_H;
+        xp.part_off = p2p_off_part(nranks);
+        xp.part_slot = p2p_xslot(nranks);
+        xp.gath_off = p2p_off_gath(nranks);
+        xp.gath_slot = p2p_xslot(nranks);
+        xp.ctx = ctx + (int64_t)r * batch * wl::AT_H * wl::AT_DV;
+        xp.lse = lse ? lse + (int64_t)r * batch * wl::AT_H : nullptr;
+        return xp;
+    };
+    // Every stage of every emulated rank runs after the stage it reads from has
+    // completed on every rank, so no wait depends on a kernel still to come.
+    for (int r = 0; r < nranks; ++r)
+        wl::xscatter_kernel<<<dim3(wl::AT_H, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
+    for (int r = 0; r < nranks; ++r)
+        wl::xgather_kernel<<<dim3(wl::AT_H / nranks, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
+    for (int r = 0; r < nranks; ++r)
+        wl::xunpack_kernel<<<dim3(wl::AT_H, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+}
+
 int wl_diag_merge_exchange(const void* region, int64_t slot_words, const uint32_t* epoch_ctr, int32_t n_rows,
                            int32_t n_parts, float* ctx, float* lse, void* stream) {
     if (!region || !epoch_ctr || !ctx || slot_words <= 0 || !aligned16(region)) return WL_ERR_ARG;
