@@ -299,8 +299,13 @@ int splits_for(int32_t rows, long long n_max, int cap) {
     long long s = sm_count() / (rows > 0 ? rows : 1);
     s = s < 1 ? 1 : s;
     s = s > cap ? cap : s;
-    const long long tiles = ceil_div(n_max > 0 ? n_max : 1, wl::AT_TILE);
-    return (int)(s > tiles ? tiles : s);
+    const long long n = n_max > 0 ? n_max : 1;
+    const long long tiles = ceil_div(n, wl::AT_TILE);
+    if (s > tiles) s = tiles;
+    // no CTA left without work when the list is full: as many splits as whole
+    // shares of ceil(n / s) rounded up to tiles need
+    const long long per = ceil_div(ceil_div(n, s), wl::AT_TILE) * wl::AT_TILE;
+    return (int)ceil_div(n, per);
 }
 
 // ---- kernel launchers ----------------------------------------------------------
