@@ -243,7 +243,7 @@ def run_reference(args, rank):
 
 # ---- diagnostics run beside the timed region --------------------------------------------------
 PHASES_P2P = ["indexer", "local_topk", "cand_exchange", "global_topk", "attention", "reduce_scatter",
-              "all_gather", "unpack"]
+              "all_gather"]
 PHASES_NCCL = ["indexer", "local_topk", "cand_exchange", "global_topk", "attention", "local_merge",
                "all_gather", "merge"]
 PHASES_1GPU = ["indexer", "topk", "attention", "merge"]
@@ -399,10 +399,11 @@ def main():
 
         def step(i=0):
             call(io)
-        # histogram zeroing, indexer, top-k, global top-k, attention, local merge,
-        # final merge (+ two put kernels with the peer exchange; NCCL's own
-        # kernels otherwise)
-        launches_per_step = 9 if comm.p2p else 7
+        # peer exchange: histogram zeroing, indexer, local top-k, candidate put,
+        # global top-k, attention, reduce-scatter, all-gather; NCCL: histogram
+        # zeroing, indexer, local top-k, global top-k, attention, local merge,
+        # final merge (+ NCCL's own kernels)
+        launches_per_step = 8 if comm.p2p else 7
     else:
         nbytes = L.wl_attn_workspace_bytes(C.byref(cfg), T, B)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=device)

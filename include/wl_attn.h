@@ -423,7 +423,7 @@ int wl_diag_set_wait_limit(int64_t cycles);
  * wl_attn_decode: start | indexer | top-k | attention | merge (owner; a
  * consumer has no indexer or top-k stamps). Of wl_attn_decode_sharded over
  * peer memory: start | indexer | local top-k | candidate exchange | global
- * top-k | attention | (o, lse) reduce-scatter | all-gather | unpack; over
+ * top-k | attention | (o, lse) reduce-scatter | all-gather; over
  * NCCL: start | indexer | local top-k | candidate exchange | global top-k |
  * attention | local merge | all-gather | merge. Stamping adds one tiny launch per
  * boundary and breaks the overlap between phases: a diagnostic, not a

@@ -614,7 +614,12 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     // grid (splits, rows), each CTA one (o, lse) partial.
     wl::PfParams pp{};
     if (int e = encode_q_map(&pp.tm_q, q_abs, rows->n_rows)) return e;
-    pp.o_tma = aligned16(o_part) && encode_o_map(&pp.tm_o, o_part, (int64_t)rows->n_rows * max_splits) == WL_OK;
+    static const bool no_tma_store = [] {
+        const char* e = std::getenv("WL_ATTN_PLAIN_STORE");
+        return e && e[0] == '1';
+    }();
+    pp.o_tma = !no_tma_store && aligned16(o_part) &&
+               encode_o_map(&pp.tm_o, o_part, (int64_t)rows->n_rows * max_splits) == WL_OK;
     WL_CUDA_TRY(launch_pdl(wl::mla_attn64_kernel, dim3(max_splits, rows->n_rows), dim3(wl::PF_THREADS),
                            wl::PfLayout::BYTES, st, p, pp));
     WL_CUDA_TRY(cudaGetLastError());
@@ -1495,8 +1500,8 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
     const bool p2p = comm->p2p && B <= kP2PMaxRows && k <= kP2PMaxK && (k % 32) == 0 &&
                      (int64_t)N * k <= kTopkRegMax;
     // Phase stamps (diagnostics): start | indexer | local top-k | candidate
-    // exchange | global top-k | attention | (o, lse) reduce-scatter | all-gather
-    // | unpack (peer exchange); the NCCL exchange stamps start | indexer |
+    // exchange | global top-k | attention | (o, lse) reduce-scatter |
+    // all-gather (peer exchange); the NCCL exchange stamps start | indexer |
     // local top-k | candidate exchange | global top-k | attention | local merge
     // | all-gather | merge. A consumer layer has no indexer, top-k or
     // candidate stamps.
@@ -1625,9 +1630,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         xp.lse = io->lse;
         WL_CUDA_TRY(launch_pdl(wl::xscatter_kernel, dim3(wl::AT_H, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
         WL_PHASE(st);
-        WL_CUDA_TRY(launch_pdl(wl::xgather_kernel, dim3(xp.hs, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
-        WL_PHASE(st);
-        WL_CUDA_TRY(launch_pdl(wl::xunpack_kernel, dim3(wl::AT_H, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
+        WL_CUDA_TRY(launch_pdl(wl::xgather_kernel<true>, dim3(xp.hs, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
         WL_PHASE(st);
         return WL_OK;
     }
@@ -1771,7 +1774,7 @@ int wl_diag_xmerge(int32_t nranks, int32_t batch, int32_t nsplit, const float* o
     for (int r = 0; r < nranks; ++r)
         wl::xscatter_kernel<<<dim3(wl::AT_H, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
     for (int r = 0; r < nranks; ++r)
-        wl::xgather_kernel<<<dim3(wl::AT_H / nranks, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
+        wl::xgather_kernel<false><<<dim3(wl::AT_H / nranks, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
     for (int r = 0; r < nranks; ++r)
         wl::xunpack_kernel<<<dim3(wl::AT_H, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
     WL_CUDA_TRY(cudaGetLastError());

@@ -10,7 +10,8 @@
 //            owns the head;
 //   xgather  (rank q): merges the N partials of each of its (row, head) pairs
 //            and stores the final row into the GATH slot q of every rank;
-//   xunpack  (every rank): copies the N slices of its GATH slots into ctx/lse.
+//   xunpack  (every rank): copies the N slices of its GATH slots into ctx/lse
+//            (fused into xgather's CTAs in the decode path).
 // Per rank, NVLink carries about 2 x (N - 1) / N x B x 64 x 513 words (in the
 // wire format of p2p.cuh, 8 bytes per 4-byte word), instead of N x B x 64 x 513
 // words for an all-gather of every rank's partials.
@@ -93,15 +94,26 @@ __global__ void __launch_bounds__(32) xscatter_kernel(XMergeParams p) {
     for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
     const float inv = W > 0.f ? 1.f / W : 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < p.nsplit; ++s) {
-        const float w = __shfl_sync(0xffffffffu, wl, s & 31) * inv;
-        if (w == 0.f) continue;  // empty splits are never read
-        const float4 v =
-            *reinterpret_cast<const float4*>(p.o_part + (((long long)b * p.nsplit + s) * AT_H + h) * AT_DV + c);
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
+    // splits in groups of 16: all loads of a group in flight before any use
+    for (int s0 = 0; s0 < p.nsplit; s0 += 16) {
+        float4 v[16];
+        float w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int s = s0 + j;
+            w[j] = __shfl_sync(0xffffffffu, wl, s & 31) * inv;
+            if (s >= p.nsplit) w[j] = 0.f;
+            v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (w[j] != 0.f)  // empty splits are never read
+                v[j] = *reinterpret_cast<const float4*>(p.o_part + (((long long)b * p.nsplit + s) * AT_H + h) * AT_DV + c);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            acc.x = fmaf(w[j], v[j].x, acc.x);
+            acc.y = fmaf(w[j], v[j].y, acc.y);
+            acc.z = fmaf(w[j], v[j].z, acc.z);
+            acc.w = fmaf(w[j], v[j].w, acc.w);
+        }
     }
     const float L = (W > 0.f) ? M + logf(W) : -INFINITY;
     const int owner = h / p.hs, hl = h % p.hs;
@@ -112,7 +124,34 @@ __global__ void __launch_bounds__(32) xscatter_kernel(XMergeParams p) {
     xput_done(p.a, XCH_PART, epoch);
 }
 
-// grid (hs heads, 4 column quarters, B), 32 threads.
+// The final rows of heads {r hs + hl : r < N} (each owned by rank r) from this
+// rank's GATH slots into ctx / lse: what CTA (hl, q, b) of the gather unpacks.
+__device__ __forceinline__ void xunpack_head(const XMergeParams& p, int h, int q, int b, int lane, uint32_t eg) {
+    const int c = q * 128 + lane * 4;
+    const int owner = h / p.hs, hl = h % p.hs;
+    const uint64_t* slot =
+        reinterpret_cast<const uint64_t*>(p.a.region[p.a.rank] + p.gath_off + (long long)owner * p.gath_slot);
+    const long long row = (long long)b * p.hs + hl;
+    const uint64_t* w = slot + row * AT_DV + c;
+    uint64_t r0, r1, r2, r3;
+    ll_load2_raw(w, r0, r1);
+    ll_load2_raw(w + 2, r2, r3);
+    float4 v;
+    v.x = __uint_as_float(ll_wait1(w, eg, r0, 52));
+    v.y = __uint_as_float(ll_wait1(w + 1, eg, r1, 52));
+    v.z = __uint_as_float(ll_wait1(w + 2, eg, r2, 52));
+    v.w = __uint_as_float(ll_wait1(w + 3, eg, r3, 52));
+    *reinterpret_cast<float4*>(p.ctx + ((long long)b * AT_H + h) * AT_DV + c) = v;
+    if (q == 0 && lane == 0 && p.lse) {
+        const uint64_t* wl = slot + (long long)p.B * p.hs * AT_DV + row;
+        p.lse[(long long)b * AT_H + h] = __uint_as_float(ll_wait1(wl, eg, ll_load1_raw(wl), 53));
+    }
+}
+
+// grid (hs heads, 4 column quarters, B), 32 threads. UNPACK: the same CTA then
+// copies the N final slices of its (hl, q, b) position into ctx / lse (the
+// all-gather's receive side), so no third kernel is needed.
+template <bool UNPACK>
 __global__ void __launch_bounds__(32) xgather_kernel(XMergeParams p) {
     pdl_wait();
     pdl_trigger();
@@ -164,34 +203,24 @@ __global__ void __launch_bounds__(32) xgather_kernel(XMergeParams p) {
         xstore_row(slot + row * AT_DV + c, slot + (long long)p.B * p.hs * AT_DV + row, acc, L, eg,
                    q == 0 && lane == 0);
     }
+    if constexpr (UNPACK) {
+        // every rank's slice of this position; ours first (no wait), then the
+        // peers' in the order they were sent to us
+        for (int k = 0; k < N; ++k) {
+            const int r = (p.a.rank + k) % N;
+            xunpack_head(p, r * p.hs + hl, q, b, lane, eg);
+        }
+    }
     xput_done(p.a, XCH_GATH, eg);
 }
 
-// grid (64 heads, 4 column quarters, B), 32 threads.
+// grid (64 heads, 4 column quarters, B), 32 threads: the receive side on its
+// own (the emulated-rank test hook runs it as a separate stage).
 __global__ void __launch_bounds__(32) xunpack_kernel(XMergeParams p) {
     pdl_wait();
     pdl_trigger();
-    const int h = blockIdx.x, q = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
-    const int c = q * 128 + lane * 4;
-    const uint32_t eg = *reinterpret_cast<volatile unsigned*>(p.a.ctr + XCH_GATH);
-    const int owner = h / p.hs, hl = h % p.hs;
-    const uint64_t* slot =
-        reinterpret_cast<const uint64_t*>(p.a.region[p.a.rank] + p.gath_off + (long long)owner * p.gath_slot);
-    const long long row = (long long)b * p.hs + hl;
-    const uint64_t* w = slot + row * AT_DV + c;
-    uint64_t r0, r1, r2, r3;
-    ll_load2_raw(w, r0, r1);
-    ll_load2_raw(w + 2, r2, r3);
-    float4 v;
-    v.x = __uint_as_float(ll_wait1(w, eg, r0, 52));
-    v.y = __uint_as_float(ll_wait1(w + 1, eg, r1, 52));
-    v.z = __uint_as_float(ll_wait1(w + 2, eg, r2, 52));
-    v.w = __uint_as_float(ll_wait1(w + 3, eg, r3, 52));
-    *reinterpret_cast<float4*>(p.ctx + ((long long)b * AT_H + h) * AT_DV + c) = v;
-    if (q == 0 && lane == 0 && p.lse) {
-        const uint64_t* wl = slot + (long long)p.B * p.hs * AT_DV + row;
-        p.lse[(long long)b * AT_H + h] = __uint_as_float(ll_wait1(wl, eg, ll_load1_raw(wl), 53));
-    }
+    xunpack_head(p, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x,
+                 *reinterpret_cast<volatile unsigned*>(p.a.ctr + XCH_GATH));
 }
 
 }  // namespace wl
