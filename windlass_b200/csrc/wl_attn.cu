@@ -614,12 +614,9 @@ int launch_attn(const wl_attn_cfg* cfg, const wl_latent_cache* c, int32_t T, int
     // grid (splits, rows), each CTA one (o, lse) partial.
     wl::PfParams pp{};
     if (int e = encode_q_map(&pp.tm_q, q_abs, rows->n_rows)) return e;
-    static const bool no_tma_store = [] {
-        const char* e = std::getenv("WL_ATTN_PLAIN_STORE");
-        return e && e[0] == '1';
-    }();
-    pp.o_tma = !no_tma_store && aligned16(o_part) &&
-               encode_o_map(&pp.tm_o, o_part, (int64_t)rows->n_rows * max_splits) == WL_OK;
+    // O leaves through TMA stores (plain per-thread stores measured 2-3 us
+    // slower per layer-step); plain stores only when the map cannot be made
+    pp.o_tma = aligned16(o_part) && encode_o_map(&pp.tm_o, o_part, (int64_t)rows->n_rows * max_splits) == WL_OK;
     WL_CUDA_TRY(launch_pdl(wl::mla_attn64_kernel, dim3(max_splits, rows->n_rows), dim3(wl::PF_THREADS),
                            wl::PfLayout::BYTES, st, p, pp));
     WL_CUDA_TRY(cudaGetLastError());
