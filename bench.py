@@ -521,9 +521,13 @@ def main():
     # ---- outside the timed regions: phase breakdown, un-graphed latency, self-check ----
     names = (PHASES_P2P if comm.p2p else PHASES_NCCL) if comm is not None else PHASES_1GPU
     phases = phase_breakdown(torch, L, step, device, names)
+    phases_min = None
     if world > 1:
         pv = torch.tensor(list(phases.values()), device=device)
+        pm = pv.clone()
         dist.all_reduce(pv, op=dist.ReduceOp.MAX)
+        dist.all_reduce(pm, op=dist.ReduceOp.MIN)
+        phases_min = {k: round(float(v), 2) for k, v in zip(phases, pm.tolist())}
         phases = {k: round(float(v), 2) for k, v in zip(phases, pv.tolist())}
     single_us = single_layer_us(torch, step)
     if world > 1:
@@ -576,6 +580,7 @@ def main():
             "roofline": roof,
             "kernels_us": breakdown,
             "phases_us": phases,
+            "phases_us_min_over_ranks": phases_min,
             "single_layer_us": single_us,
             "parity": parity,
             "cpu_baseline": cpu,

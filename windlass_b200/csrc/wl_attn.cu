@@ -1627,7 +1627,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         xp.lse = io->lse;
         WL_CUDA_TRY(launch_pdl(wl::xscatter_kernel, dim3(wl::AT_H, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
         WL_PHASE(st);
-        WL_CUDA_TRY(launch_pdl(wl::xgather_kernel<true>, dim3(xp.hs, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
+        WL_CUDA_TRY(launch_pdl(wl::xgather_kernel<true>, dim3(xp.hs, wl::AT_DV / 128, B), dim3(32 * N), 0, st, xp));
         WL_PHASE(st);
         return WL_OK;
     }
@@ -1771,7 +1771,7 @@ int wl_diag_xmerge(int32_t nranks, int32_t batch, int32_t nsplit, const float* o
     for (int r = 0; r < nranks; ++r)
         wl::xscatter_kernel<<<dim3(wl::AT_H, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
     for (int r = 0; r < nranks; ++r)
-        wl::xgather_kernel<false><<<dim3(wl::AT_H / nranks, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
+        wl::xgather_kernel<false><<<dim3(wl::AT_H / nranks, wl::AT_DV / 128, batch), 32 * nranks, 0, st>>>(params(r));
     for (int r = 0; r < nranks; ++r)
         wl::xunpack_kernel<<<dim3(wl::AT_H, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
     WL_CUDA_TRY(cudaGetLastError());

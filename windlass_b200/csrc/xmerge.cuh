@@ -148,14 +148,17 @@ __device__ __forceinline__ void xunpack_head(const XMergeParams& p, int h, int q
     }
 }
 
-// grid (hs heads, 4 column quarters, B), 32 threads. UNPACK: the same CTA then
-// copies the N final slices of its (hl, q, b) position into ctx / lse (the
-// all-gather's receive side), so no third kernel is needed.
+// grid (hs heads, 4 column quarters, B), 32 N threads: every warp merges the
+// N partials of position (hl, q, b) (the same words, from this GPU's memory),
+// then warp w stores the result into rank (rank + w) % N and — UNPACK — copies
+// that rank's final slice of the position into ctx / lse (the all-gather's
+// receive side), so the N destinations and the N waits proceed in parallel
+// and no third kernel is needed.
 template <bool UNPACK>
-__global__ void __launch_bounds__(32) xgather_kernel(XMergeParams p) {
+__global__ void __launch_bounds__(32 * P2P_MAX_RANKS) xgather_kernel(XMergeParams p) {
     pdl_wait();
     pdl_trigger();
-    const int hl = blockIdx.x, q = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
+    const int hl = blockIdx.x, q = blockIdx.y, b = blockIdx.z, lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
     const int c = q * 128 + lane * 4;
     const int N = p.a.nranks;
     const uint32_t ep = *reinterpret_cast<volatile unsigned*>(p.a.ctr + XCH_PART);  // this step's PART epoch
@@ -197,19 +200,14 @@ __global__ void __launch_bounds__(32) xgather_kernel(XMergeParams p) {
         acc.w = fmaf(wv[s], __uint_as_float(ll_wait1(w + 3, ep, raw[s][3], 51)), acc.w);
     }
     const float L = (W > 0.f) ? M + logf(W) : -INFINITY;
-    for (int k = 0; k < N; ++k) {
-        const int d = (p.a.rank + k) % N;  // ranks start on different destinations
+    if (wi < N) {
+        // ranks start on different destinations; warp 0 stores to this rank's
+        // own region and then reads those words back (same threads)
+        const int d = (p.a.rank + wi) % N;
         uint64_t* slot = reinterpret_cast<uint64_t*>(p.a.region[d] + p.gath_off + (long long)p.a.rank * p.gath_slot);
         xstore_row(slot + row * AT_DV + c, slot + (long long)p.B * p.hs * AT_DV + row, acc, L, eg,
                    q == 0 && lane == 0);
-    }
-    if constexpr (UNPACK) {
-        // every rank's slice of this position; ours first (no wait), then the
-        // peers' in the order they were sent to us
-        for (int k = 0; k < N; ++k) {
-            const int r = (p.a.rank + k) % N;
-            xunpack_head(p, r * p.hs + hl, q, b, lane, eg);
-        }
+        if constexpr (UNPACK) xunpack_head(p, d * p.hs + hl, q, b, lane, eg);
     }
     xput_done(p.a, XCH_GATH, eg);
 }
