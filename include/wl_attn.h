@@ -450,17 +450,6 @@ int wl_diag_merge_exchange(const void* region, int64_t slot_words, const uint32_
  * wl_diag_xmerge_bytes(nranks) bytes (every rank's exchange region and
  * counters), 16-byte aligned. A test hook for the exchange's layout. */
 size_t wl_diag_xmerge_bytes(int32_t nranks);
-
-/* The sharded decode's global top-k (one cluster of nranks CTAs per row) over a
- * caller-made region in the candidate exchange's layout: slot s (rank s's
- * candidates) at word s*slot_words holds [batch][k] score words then
- * [batch][k] global-index words, each {payload, epoch}, the epoch read from
- * *epoch_ctr. Writes the top kg (ties to the lowest position, i.e. global
- * index) of each row's nranks*k candidates, ascending, to out [batch,
- * out_stride] and kg to n_out. k in {1024, 2048, 4096}, nranks in [2, 8].
- * A test hook for that kernel. */
-int wl_diag_seg_topk(const void* region, int64_t slot_words, const uint32_t* epoch_ctr, int32_t nranks, int32_t batch,
-                     int32_t k, int32_t kg, int32_t* out, int64_t out_stride, int32_t* n_out, void* stream);
 int wl_diag_xmerge(int32_t nranks, int32_t batch, int32_t nsplit, const float* o_part, const float* lse_part,
                    void* regions, size_t regions_bytes, float* ctx, float* lse, void* stream);
 

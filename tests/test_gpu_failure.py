@@ -137,47 +137,3 @@ def test_sharded_exchange_layout_on_one_gpu(nranks):
         assert np.array_equal(np.isinf(got_l), np.isinf(want_l))
         fin = np.isfinite(want_l)
         np.testing.assert_allclose(got_l[fin], want_l[fin], rtol=0, atol=1e-5)
-
-
-@pytest.mark.parametrize("nranks,k", [(2, 2048), (8, 2048), (4, 1024), (3, 4096)])
-def test_sharded_global_topk_cluster_kernel(nranks, k):
-    """The sharded decode's global top-k (one cluster of N CTAs per row, CTA s
-    over rank s's candidates, read in the exchange's wire format) equals the
-    exact top-k of the concatenated candidates with ties to the lowest
-    position — on candidates like the real ones (each segment a rank's top-k
-    of realistic index scores, ascending by index), with ties across segments,
-    and with padded segments (-inf, as a rank with fewer than k keys sends)."""
-    A.device_error(clear=True)
-    rng = np.random.default_rng(10 * nranks + k // 1024)
-    B = 3
-    kg = k
-    scores = np.empty((nranks, B, k), np.float32)
-    gidx = np.empty((nranks, B, k), np.int64)
-    for s in range(nranks):
-        for b in range(B):
-            x = rng.gamma(2.0, 1.0, 4 * k).astype(np.float32)
-            top = np.sort(np.argsort(-x, kind="stable")[:k])
-            scores[s, b], gidx[s, b] = x[top], s * 4 * k + top
-    thr_val = np.sort(scores[:, 1].reshape(-1))[-kg]
-    scores[:, 1, :40] = thr_val  # a tie that straddles the threshold, in every segment
-    scores[nranks - 1, 2, k // 2:] = -np.inf  # a short last shard: padding
-    gidx[nranks - 1, 2, k // 2:] = 0x7FFFFFFF
-    words = np.zeros((nranks, 2 * B * k), np.uint64)
-    for s in range(nranks):
-        words[s, :B * k] = _wire(scores[s].ravel(), 3)
-        words[s, B * k:] = (gidx[s].ravel().astype(np.uint64) & np.uint64(0xFFFFFFFF)) | (np.uint64(3) << np.uint64(32))
-    region = torch.from_numpy(words.view(np.int64).reshape(-1)).cuda()
-    epoch = torch.tensor([3], dtype=torch.int32, device="cuda")
-    out = torch.full((B, kg), -1, dtype=torch.int32, device="cuda")
-    n = torch.zeros(B, dtype=torch.int32, device="cuda")
-    _lib.check(_lib.lib().wl_diag_seg_topk(region.data_ptr(), 2 * B * k, epoch.data_ptr(), nranks, B, k, kg,
-                                           out.data_ptr(), kg, n.data_ptr(), torch.cuda.current_stream().cuda_stream))
-    torch.cuda.synchronize()
-    assert A.device_error(clear=True)[0] == _lib.WL_OK
-    got = out.cpu().numpy()
-    assert np.all(n.cpu().numpy() == kg)
-    for b in range(B):
-        row = scores[:, b].reshape(-1)  # position order = rank order = global order
-        pos = np.argsort(-row.astype(np.float64), kind="stable")[:kg]
-        want = np.sort(gidx[:, b].reshape(-1)[pos])
-        assert np.array_equal(got[b], want), f"row {b}"

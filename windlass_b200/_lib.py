@@ -121,7 +121,6 @@ SIGNATURES = {
     "wl_diag_phase_count": (i32, []),
     "wl_diag_merge_exchange": (C.c_int, [vp, i64, vp, i32, i32, vp, vp, vp]),
     "wl_diag_xmerge_bytes": (C.c_size_t, [i32]),
-    "wl_diag_seg_topk": (C.c_int, [vp, i64, vp, i32, i32, i32, i32, vp, i64, vp, vp]),
     "wl_diag_xmerge": (C.c_int, [i32, i32, i32, vp, vp, vp, C.c_size_t, vp, vp, vp]),
 }
 

@@ -1082,143 +1082,4 @@ __global__ void __launch_bounds__(TOPK_THREADS) sel_normalize_kernel(NormParams 
     if (tid == 0 && p.n_out) p.n_out[r] = (int)carry;
 }
 
-
-// ---- the sharded decode's global top-k: one cluster per row ---------------------------
-// Exact top-k over N segments of `seg_len` candidates, read in place from the
-// peer-exchange slots (segment s = rank s's local selection as (score, global
-// index) words, ascending global index, so position order is global key order
-// and ties resolve to the lowest global index). One cluster of N CTAs per row
-// (grid (N, rows), cluster (N)); CTA s holds segment s in registers, PER
-// consecutive candidates per thread. The same three radix levels as
-// topk_reg_kernel over key - lo (lo, hi: the row's extremes, exchanged over
-// distributed shared memory), each CTA counting its segment into its own
-// 2048-bin histogram and every CTA summing the N histograms over DSMEM; then
-// each CTA emits its selected candidates at their global positions (the
-// counts of the CTAs before it, exchanged the same way). Spreads what one
-// 1024-thread CTA did for N x k candidates over N SMs.
-constexpr int TOPKS_THREADS = 512;
-
-template <int PER>
-__global__ void __launch_bounds__(TOPKS_THREADS, 1) topk_seg_cluster_kernel(TopkParams p) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ uint32_t hist[2048];
-    __shared__ uint32_t scan_sh[36];
-    __shared__ uint32_t xch[4];  // this CTA's key min / max, then its counts > thr, == thr
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, r = blockIdx.y;
-    const uint32_t s = cluster_ctarank(), N = gridDim.x;
-    const int kk = p.k;  // <= N * seg_len (pads are -inf and never taken)
-    if (s == 0 && tid == 0 && p.n_out) p.n_out[r] = kk;
-    int* out = p.out + (long long)r * p.out_stride;
-    const uint32_t epoch = p2p_epoch(p.ll);
-    const uint64_t* seg = p2p_slot(p.ll, epoch, 0) + (long long)r * p.in_stride + (long long)s * p.seg_stride;
-    const int i0 = tid * PER;  // PER * TOPKS_THREADS == seg_len
-    uint32_t u[PER];
-    {
-        uint64_t w[PER];
-#pragma unroll
-        for (int j = 0; j < PER; j += 2) ll_load2_raw(seg + i0 + j, w[j], w[j + 1]);
-#pragma unroll
-        for (int j = 0; j < PER; ++j) u[j] = ordered_key(__uint_as_float(ll_wait1(seg + i0 + j, epoch, w[j], 24)));
-    }
-    // ---- the row's key range over the cluster ----
-    uint32_t lo = 0xffffffffu, hi = 0u;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-        lo = min(lo, u[j]);
-        hi = max(hi, u[j]);
-    }
-    lo = __reduce_min_sync(0xffffffffu, lo);
-    hi = __reduce_max_sync(0xffffffffu, hi);
-    if (lane == 0) {
-        scan_sh[warp] = lo;
-        hist[warp] = hi;
-    }
-    __syncthreads();
-    if (warp == 0) {
-        const int nw = TOPKS_THREADS / 32;
-        uint32_t l = lane < nw ? scan_sh[lane] : 0xffffffffu, h = lane < nw ? hist[lane] : 0u;
-        l = __reduce_min_sync(0xffffffffu, l);
-        h = __reduce_max_sync(0xffffffffu, h);
-        if (lane == 0) {
-            xch[0] = l;
-            xch[1] = h;
-        }
-    }
-    cluster_sync_all();
-    lo = 0xffffffffu;
-    hi = 0u;
-    for (uint32_t c = 0; c < N; ++c) {
-        lo = min(lo, dsmem_ld_u32(&xch[0], c));
-        hi = max(hi, dsmem_ld_u32(&xch[1], c));
-    }
-    const uint32_t span = hi - lo;
-    const int nbits = span ? 32 - __clz(span) : 0;
-    const int s1 = max(0, nbits - 11), s2 = max(0, s1 - 11);
-    // ---- three levels; each: own histogram, cluster barrier, sum over DSMEM ----
-    uint32_t prefix = 0, mask_hi = 0, remaining = (uint32_t)kk;
-    int shift_hi = 32;
-#pragma unroll 1
-    for (int level = 0; level < 3; ++level) {
-        const int shift = level == 0 ? s1 : level == 1 ? s2 : 0;
-        const int nb_bits = level == 0 ? min(11, nbits) : shift_hi - shift;
-        if (level > 0 && nb_bits <= 0) continue;  // uniform over the cluster
-        const uint32_t nb = 1u << nb_bits;
-        for (int i = tid; i < 2048; i += TOPKS_THREADS) hist[i] = 0;
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < PER; ++j) {
-            const uint32_t d = u[j] - lo;
-            if ((d & mask_hi) == prefix) atomicAdd(&hist[(d >> shift) & (nb - 1u)], 1u);
-        }
-        cluster_sync_all();  // every CTA's histogram is complete
-        uint32_t c4[4] = {0u, 0u, 0u, 0u};
-        for (uint32_t c = 0; c < N; ++c)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) c4[q] += dsmem_ld_u32(&hist[4 * tid + q], c);
-        uint32_t b, above;
-        block_find_from_top<4>(c4, remaining, scan_sh, &b, &above);
-        prefix |= b << shift;
-        mask_hi |= (nb - 1u) << shift;
-        remaining -= above;
-        shift_hi = shift;
-        cluster_sync_all();  // every CTA has read the histograms before they are reset
-    }
-    const uint32_t thr = prefix + lo, need = remaining;
-    // ---- ordered emission at global positions ----
-    uint32_t mgt = 0, meq = 0;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-        mgt |= (u[j] > thr ? 1u : 0u) << j;
-        meq |= (u[j] == thr ? 1u : 0u) << j;
-    }
-    uint32_t total;
-    const uint32_t ex = block_excl_scan(((uint32_t)__popc(meq) << 16) | (uint32_t)__popc(mgt), scan_sh, &total);
-    if (tid == 0) {
-        xch[2] = total & 0xffffu;
-        xch[3] = total >> 16;
-    }
-    cluster_sync_all();
-    uint32_t base_gt = 0, base_eq = 0;
-    for (uint32_t c = 0; c < s; ++c) {
-        base_gt += dsmem_ld_u32(&xch[2], c);
-        base_eq += dsmem_ld_u32(&xch[3], c);
-    }
-    uint32_t gt_b = base_gt + (ex & 0xffffu), eq_b = base_eq + (ex >> 16);
-    const uint64_t* idx = seg + p.ll_idx_off;
-    for (uint32_t m = mgt | meq; m; m &= m - 1) {
-        const int j = __ffs(m) - 1;
-        int pos = -1;
-        if ((mgt >> j) & 1u) {
-            pos = (int)(gt_b + min(eq_b, need));
-            ++gt_b;
-        } else {
-            if (eq_b < need) pos = (int)(gt_b + eq_b);
-            ++eq_b;
-        }
-        if (pos >= 0) out[pos] = (int)ll_wait1(idx + i0 + j, epoch, ll_load1_raw(idx + i0 + j), 25);
-    }
-    cluster_sync_all();  // no CTA leaves while another may read its shared memory
-}
-
 }  // namespace wl

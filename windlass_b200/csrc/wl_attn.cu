@@ -796,15 +796,6 @@ long long p2p_off_part(int nranks) { return wl::P2P_OFF_CAND + nranks * kP2PCand
 long long p2p_off_gath(int nranks) { return p2p_off_part(nranks) + nranks * p2p_xslot(nranks); }
 size_t p2p_region_bytes(int nranks) { return (size_t)(p2p_off_gath(nranks) + nranks * p2p_xslot(nranks)); }
 
-// WL_NO_SEG_TOPK=1: the sharded global top-k on one CTA per row (comparison knob).
-bool seg_topk_enabled() {
-    static const bool on = [] {
-        const char* e = std::getenv("WL_NO_SEG_TOPK");
-        return !(e && e[0] == '1');
-    }();
-    return on;
-}
-
 bool p2p_allowed() {
     static const bool on = [] {
         const char* e = std::getenv("WL_NO_P2P");
@@ -899,41 +890,6 @@ int launch_put(const wl_comm* c, int type, const void* src, size_t bytes, long l
     grid = grid < 1 ? 1 : (grid > sm_count() ? sm_count() : grid);
     WL_CUDA_TRY(launch_pdl(wl::p2p_put_kernel, dim3(grid), dim3(256), 0, st, p2p_args(c), type,
                            static_cast<const uint32_t*>(src), n32, dst_off, slot_bytes, parity_bytes));
-    return WL_OK;
-}
-
-// The sharded global top-k as one N-CTA cluster per row (topk_seg_cluster_kernel)
-// over the candidate words of the exchange `rc`: N segments of k per row.
-int launch_seg_topk(const wl::P2PRecv& rc, int N, int32_t B, int32_t k, int32_t kg, int32_t* out, int64_t out_stride,
-                    int32_t* n_out, cudaStream_t st) {
-    wl::TopkParams tp{};
-    tp.n_rows = B;
-    tp.k = kg;
-    tp.out = out;
-    tp.out_stride = out_stride;
-    tp.n_out = n_out;
-    tp.in_stride = k;
-    tp.seg_len = k;
-    tp.seg_stride = rc.slot_words;
-    tp.ll = rc;
-    tp.ll_idx_off = (int64_t)B * k;
-    cudaLaunchConfig_t lc{};
-    lc.gridDim = dim3(N, B);
-    lc.blockDim = dim3(wl::TOPKS_THREADS);
-    lc.stream = st;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = N;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    lc.attrs = at;
-    lc.numAttrs = pdl_enabled() ? 2 : 1;
-    const cudaError_t e = k == 1024   ? cudaLaunchKernelEx(&lc, wl::topk_seg_cluster_kernel<2>, tp)
-                          : k == 2048 ? cudaLaunchKernelEx(&lc, wl::topk_seg_cluster_kernel<4>, tp)
-                                      : cudaLaunchKernelEx(&lc, wl::topk_seg_cluster_kernel<8>, tp);
-    WL_CUDA_TRY(e);
     return WL_OK;
 }
 
@@ -1584,13 +1540,9 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
                 return e;
             WL_PHASE(st);
             const wl::P2PRecv rc = p2p_recv(comm, wl::XCH_CAND, wl::P2P_OFF_CAND, kP2PCandSlot, 0);
-            if (seg_topk_enabled() && N <= 8 && (k == 1024 || k == 2048 || k == 4096) && B <= 65535) {
-                if (int e = launch_seg_topk(rc, N, B, k, kg, io->sel_out, io->sel_stride, io->sel_n_out, st)) return e;
-            } else if (int e = launch_topk(nullptr, k, &crows, N * k, kg, nullptr, io->sel_out, io->sel_stride,
-                                           io->sel_n_out, st, nullptr, false, nullptr, k, rc.slot_words, &rc,
-                                           (int64_t)B * k)) {
+            if (int e = launch_topk(nullptr, k, &crows, N * k, kg, nullptr, io->sel_out, io->sel_stride, io->sel_n_out,
+                                    st, nullptr, false, nullptr, k, rc.slot_words, &rc, (int64_t)B * k))
                 return e;
-            }
         } else {
             if (ncclGroupStart() != ncclSuccess) return WL_ERR_NCCL;
             if (ncclAllGather(w.cand_score, w.cand_score_all, (size_t)B * k, ncclFloat32, comm->comm, st) !=
@@ -1776,16 +1728,6 @@ int wl_diag_phase_stamps(uint64_t* dev_buf, int32_t cap) {
 int32_t wl_diag_phase_count(void) {
     std::lock_guard<std::mutex> lk(g_ph_mu);
     return g_ph_n;
-}
-
-int wl_diag_seg_topk(const void* region, int64_t slot_words, const uint32_t* epoch_ctr, int32_t nranks, int32_t batch,
-                     int32_t k, int32_t kg, int32_t* out, int64_t out_stride, int32_t* n_out, void* stream) {
-    if (!region || !epoch_ctr || !out || !aligned16(region) || nranks < 2 || nranks > 8 || batch <= 0 ||
-        batch > 65535 || !(k == 1024 || k == 2048 || k == 4096) || kg <= 0 || kg > nranks * k ||
-        out_stride < kg || slot_words < 2LL * batch * k || (slot_words & 1))
-        return WL_ERR_ARG;
-    const wl::P2PRecv rc{static_cast<const uint64_t*>(region), slot_words, 0, epoch_ctr};
-    return launch_seg_topk(rc, nranks, batch, k, kg, out, out_stride, n_out, static_cast<cudaStream_t>(stream));
 }
 
 size_t wl_diag_xmerge_bytes(int32_t nranks) {
