@@ -67,29 +67,6 @@ __device__ __forceinline__ uint32_t ll_wait1(const uint64_t* src, uint32_t epoch
         __nanosleep(128);
     }
 }
-__device__ __forceinline__ void ll_store1(uint64_t* dst, uint32_t a, uint32_t epoch) {
-    const uint64_t x = ((uint64_t)epoch << 32) | a;
-    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(x) : "memory");
-}
-
-// Epoch of a put kernel of `type`: one more than the rank's counter; the last
-// CTA to finish advances the counter (every CTA has read it by then).
-__device__ __forceinline__ uint32_t xput_epoch(const P2PArgs& a, int type) {
-    return *reinterpret_cast<volatile unsigned*>(a.ctr + type) + 1u;
-}
-__device__ __forceinline__ void xput_done(const P2PArgs& a, int type, uint32_t epoch) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned nblk = gridDim.x * gridDim.y * gridDim.z;
-        const unsigned prev = atomicAdd(a.ctr + XCH_TYPES + type, 1u);
-        if (prev == nblk - 1) {
-            a.ctr[XCH_TYPES + type] = 0;
-            a.ctr[type] = epoch;
-        }
-    }
-}
-
 // Two consecutive words (16-byte aligned).
 __device__ __forceinline__ void ll_load2(const uint64_t* src, uint32_t epoch, unsigned site, uint32_t& a,
                                          uint32_t& b) {

@@ -198,46 +198,25 @@ struct TopkParams {
 // format): output position pos of row r also gets score[r * stride + pos] (the
 // selected score) and gidx[r * stride + pos] = base + key index; positions
 // [k', k) are padded with (-inf, INT_MAX).
-// With x_on the candidates go straight into slot x.rank of every rank's peer
-// exchange region instead (the sharded decode's candidate exchange, fused into
-// the selection): score words at x_off + (r * k + pos) * 8 bytes, index words
-// x_idx words further, tagged with the next candidate epoch; the kernel then
-// advances this rank's candidate epoch.
 struct CandOut {
     float* score;
     int* gidx;
     long long stride;
     int k;
     long long base;
-    int x_on;
-    P2PArgs x;
-    long long x_off;  // bytes
-    long long x_idx;  // words
 };
-
-__device__ __forceinline__ void cand_write(const CandOut& co, int r, int pos, float score, int gidx, uint32_t epoch) {
-    if (co.x_on) {
-        const long long w = (long long)r * co.k + pos;
-        for (int q = 0; q < co.x.nranks; ++q) {
-            const int d = (co.x.rank + q) % co.x.nranks;  // ranks start on different destinations
-            uint64_t* base = reinterpret_cast<uint64_t*>(co.x.region[d] + co.x_off);
-            ll_store1(base + w, __float_as_uint(score), epoch);
-            ll_store1(base + co.x_idx + w, (uint32_t)gidx, epoch);
-        }
-        return;
-    }
-    co.score[(long long)r * co.stride + pos] = score;
-    co.gidx[(long long)r * co.stride + pos] = gidx;
-}
 
 // Inverse of ordered_key (-0 comes back as +0).
 __device__ __forceinline__ float key_to_float(uint32_t key) {
     return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
 }
 
-__device__ __forceinline__ void cand_pad(const CandOut& co, int r, int from, int tid, int nt, uint32_t epoch = 0) {
-    if (!co.score && !co.x_on) return;
-    for (int pos = from + tid; pos < co.k; pos += nt) cand_write(co, r, pos, -INFINITY, 0x7fffffff, epoch);
+__device__ __forceinline__ void cand_pad(const CandOut& co, int r, int from, int tid, int nt) {
+    if (!co.score) return;
+    for (int pos = from + tid; pos < co.k; pos += nt) {
+        co.score[(long long)r * co.stride + pos] = -INFINITY;
+        co.gidx[(long long)r * co.stride + pos] = 0x7fffffff;
+    }
 }
 
 // One CTA per row. Rows of up to TOPK_SMEM_MAX elements are staged once in
@@ -626,22 +605,17 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
     const int kk = min(p.k, len);
     int* out = p.out + (long long)r * p.out_stride;
     const int lo = (int)rank * TOPKC_THREADS * PER, hi = min(len, lo + TOPKC_THREADS * PER);
-    const uint32_t xep = co.x_on ? *reinterpret_cast<volatile unsigned*>(co.x.ctr + XCH_CAND) + 1u : 0u;
-    auto finish = [&]() {  // every thread of every CTA, once
-        if (co.x_on) xput_done(co.x, XCH_CAND, xep);
-    };
     if (rank == 0 && tid == 0 && p.n_out) p.n_out[r] = kk > 0 ? kk : 0;
-    if (rank == 0) cand_pad(co, r, max(kk, 0), tid, TOPKC_THREADS, xep);
-    if (kk <= 0) {  // uniform over the cluster
-        finish();
-        return;
-    }
+    if (rank == 0) cand_pad(co, r, max(kk, 0), tid, TOPKC_THREADS);
+    if (kk <= 0) return;  // uniform over the cluster
     if (kk >= len) {
         for (int i = lo + tid; i < hi; i += TOPKC_THREADS) {
             out[i] = i;
-            if (co.score || co.x_on) cand_write(co, r, i, p.in[(long long)r * p.in_stride + i], (int)(co.base + i), xep);
+            if (co.score) {
+                co.score[(long long)r * co.stride + i] = p.in[(long long)r * p.in_stride + i];
+                co.gidx[(long long)r * co.stride + i] = (int)(co.base + i);
+            }
         }
-        finish();
         return;
     }
     // ---- loads: the first-level histogram (8 consecutive bins per thread) and
@@ -788,10 +762,12 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
             }
             if (pos >= 0) {
                 out[pos] = i0 + j;
-                if (co.score || co.x_on) cand_write(co, r, pos, key_to_float(u[j]), (int)(co.base + i0 + j), xep);
+                if (co.score) {
+                    co.score[(long long)r * co.stride + pos] = key_to_float(u[j]);
+                    co.gidx[(long long)r * co.stride + pos] = (int)(co.base + i0 + j);
+                }
             }
         }
-        finish();
         return;
     }
     // ---- levels 2, 3 over the cluster: bin `tid` of each pass summed over the CTAs ----
@@ -853,11 +829,13 @@ __global__ void __cluster_dims__(TOPKC_CL, 1, 1) __launch_bounds__(TOPKC_THREADS
         }
         if (pos >= 0) {
             out[pos] = i0 + j;
-            if (co.score || co.x_on) cand_write(co, r, pos, key_to_float(u[j]), (int)(co.base + i0 + j), xep);
+            if (co.score) {
+                co.score[(long long)r * co.stride + pos] = key_to_float(u[j]);
+                co.gidx[(long long)r * co.stride + pos] = (int)(co.base + i0 + j);
+            }
         }
     }
     cluster_wait();  // no CTA leaves while another may still read its totals
-    finish();
 }
 
 // ---- single-CTA top-k with the row in registers --------------------------------------

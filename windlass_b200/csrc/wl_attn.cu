@@ -1521,17 +1521,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         // Local top-k; its selection leaves as (score, global index) candidates,
         // k per row (padded), straight from the top-k's emission where it can.
         const bool cand_direct = T <= kTopkClusterMax;
-        // With the peer exchange and the cluster top-k (rows of 8 193 - 196 608
-        // keys), the selection writes its candidates straight into every rank's
-        // exchange region: no separate put.
-        const bool cand_fused = p2p && T > kTopkClusterMin && T <= kTopkClusterMax;
-        wl::CandOut co{w.cand_score, w.cand_idx, k, k, t0};
-        if (cand_fused) {
-            co.x_on = 1;
-            co.x = p2p_args(comm);
-            co.x_off = wl::P2P_OFF_CAND + (long long)comm->rank * kP2PCandSlot;
-            co.x_idx = (long long)B * k;
-        }
+        const wl::CandOut co{w.cand_score, w.cand_idx, k, k, t0};
         if (int e = launch_topk(index, T, &lrows, T, k, nullptr, w.sel, kl, w.cnt, st, &w.topk, fuse,
                                 cand_direct ? &co : nullptr))
             return e;
@@ -1545,11 +1535,9 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         if (p2p) {
             // Candidates to every rank's slot `rank`; the global top-k waits for all
             // N slots and reads them in place as rows of N segments of k.
-            if (!cand_fused) {
-                if (int e = launch_put(comm, wl::XCH_CAND, w.cand_score, (size_t)B * k * 8, wl::P2P_OFF_CAND,
-                                       kP2PCandSlot, 0, st))
-                    return e;
-            }
+            if (int e = launch_put(comm, wl::XCH_CAND, w.cand_score, (size_t)B * k * 8, wl::P2P_OFF_CAND, kP2PCandSlot, 0,
+                                   st))
+                return e;
             WL_PHASE(st);
             const wl::P2PRecv rc = p2p_recv(comm, wl::XCH_CAND, wl::P2P_OFF_CAND, kP2PCandSlot, 0);
             if (int e = launch_topk(nullptr, k, &crows, N * k, kg, nullptr, io->sel_out, io->sel_stride, io->sel_n_out,

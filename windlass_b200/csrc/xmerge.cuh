@@ -46,6 +46,29 @@ struct XMergeParams {
     float* lse;        // xunpack: [B][64] (may be null)
 };
 
+__device__ __forceinline__ void ll_store1(uint64_t* dst, uint32_t a, uint32_t epoch) {
+    const uint64_t x = ((uint64_t)epoch << 32) | a;
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(x) : "memory");
+}
+
+// Epoch of a put kernel of `type`: one more than the rank's counter; the last
+// CTA to finish advances the counter (every CTA has read it by then).
+__device__ __forceinline__ uint32_t xput_epoch(const P2PArgs& a, int type) {
+    return *reinterpret_cast<volatile unsigned*>(a.ctr + type) + 1u;
+}
+__device__ __forceinline__ void xput_done(const P2PArgs& a, int type, uint32_t epoch) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned nblk = gridDim.x * gridDim.y * gridDim.z;
+        const unsigned prev = atomicAdd(a.ctr + XCH_TYPES + type, 1u);
+        if (prev == nblk - 1) {
+            a.ctr[XCH_TYPES + type] = 0;
+            a.ctr[type] = epoch;
+        }
+    }
+}
+
 // The merged row of one (row, head) and 128 columns (4 per lane) into the
 // slot words at `dst` (o) and `dst_lse` (lse, lane 0 of column quarter 0).
 __device__ __forceinline__ void xstore_row(uint64_t* dst, uint64_t* dst_lse, const float4& v, float L,
