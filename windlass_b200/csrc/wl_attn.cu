@@ -1625,7 +1625,7 @@ int wl_attn_decode_sharded(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, 
         xp.gath_slot = p2p_xslot(N);
         xp.ctx = io->ctx;
         xp.lse = io->lse;
-        WL_CUDA_TRY(launch_pdl(wl::xscatter_kernel, dim3(wl::AT_H, wl::AT_DV / 128, B), dim3(32), 0, st, xp));
+        WL_CUDA_TRY(launch_pdl(wl::xscatter_kernel, dim3(wl::AT_H / wl::XS_HEADS, wl::AT_DV / 128, B), dim3(32 * wl::XS_HEADS), 0, st, xp));
         WL_PHASE(st);
         WL_CUDA_TRY(launch_pdl(wl::xgather_kernel<true>, dim3(xp.hs, wl::AT_DV / 128, B), dim3(32 * N), 0, st, xp));
         WL_PHASE(st);
@@ -1769,7 +1769,7 @@ int wl_diag_xmerge(int32_t nranks, int32_t batch, int32_t nsplit, const float* o
     // Every stage of every emulated rank runs after the stage it reads from has
     // completed on every rank, so no wait depends on a kernel still to come.
     for (int r = 0; r < nranks; ++r)
-        wl::xscatter_kernel<<<dim3(wl::AT_H, wl::AT_DV / 128, batch), 32, 0, st>>>(params(r));
+        wl::xscatter_kernel<<<dim3(wl::AT_H / wl::XS_HEADS, wl::AT_DV / 128, batch), 32 * wl::XS_HEADS, 0, st>>>(params(r));
     for (int r = 0; r < nranks; ++r)
         wl::xgather_kernel<false><<<dim3(wl::AT_H / nranks, wl::AT_DV / 128, batch), 32 * nranks, 0, st>>>(params(r));
     for (int r = 0; r < nranks; ++r)

@@ -78,11 +78,15 @@ __device__ __forceinline__ void xstore_row(uint64_t* dst, uint64_t* dst_lse, con
     if (with_lse) ll_store1(dst_lse, __float_as_uint(L), epoch);
 }
 
-// grid (64 heads, 4 column quarters, B), 32 threads: lane l owns 4 columns.
-__global__ void __launch_bounds__(32) xscatter_kernel(XMergeParams p) {
+// grid (64 / XS_HEADS, 4 column quarters, B), 32 XS_HEADS threads: warp w
+// takes head XS_HEADS x + w, lane l 4 columns. (Fewer, larger CTAs: every CTA
+// ends with one atomic on the epoch counter, and 2048 single-warp CTAs spent
+// microseconds queueing on it.)
+constexpr int XS_HEADS = 8;
+__global__ void __launch_bounds__(32 * XS_HEADS) xscatter_kernel(XMergeParams p) {
     pdl_wait();
     pdl_trigger();
-    const int h = blockIdx.x, q = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
+    const int h = blockIdx.x * XS_HEADS + (threadIdx.x >> 5), q = blockIdx.y, b = blockIdx.z, lane = threadIdx.x & 31;
     const int c = q * 128 + lane * 4;
     const uint32_t epoch = xput_epoch(p.a, XCH_PART);
     float ls = -INFINITY;
