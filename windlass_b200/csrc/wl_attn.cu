@@ -742,6 +742,17 @@ __global__ void gather_candidates_kernel(const float* index, long long index_str
     ci[(long long)r * k + j] = g;
 }
 
+// The identity selection 0..T-1 of every row (an owner layer with
+// index_topk >= T: the reference's top-k returns every key).
+__global__ void identity_sel_kernel(int T, int* out, long long stride, int* n_out) {
+    wl::pdl_wait();
+    wl::pdl_trigger();
+    const int r = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x)
+        out[(long long)r * stride + i] = i;
+    if (blockIdx.x == 0 && threadIdx.x == 0 && n_out) n_out[r] = T;
+}
+
 __global__ void row_counts_kernel(int n_rows, int len0, int len_step, int T, int k, int* out) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n_rows) return;
@@ -1211,6 +1222,22 @@ static int decode_select(const wl_attn_cfg* cfg, const wl_attn_decode_io* io, co
                          const int32_t** sel, const int32_t** cnt, int64_t* stride, cudaStream_t st) {
     const int32_t B = io->batch, T = io->T;
     const wl_rows rows{B, 1, T, 0};
+    if (io->mode == WL_MODE_OWNER && cfg->index_topk >= T && !io->index_out) {
+        // Every key is selected whatever the scores: publish the identity list
+        // and attend densely (the same list, so the same result bit for bit);
+        // no indexer or top-k runs. (A caller that wants the scores sets
+        // index_out and gets the full path.)
+        int32_t* out = io->sel_out ? io->sel_out : w.sel;
+        const int64_t ostride = io->sel_out ? io->sel_stride : T;
+        if (io->sel_out && io->sel_stride < T) return WL_ERR_ARG;
+        if (io->sel_out || io->sel_n_out)
+            WL_CUDA_TRY(launch_pdl(identity_sel_kernel, dim3((unsigned)ceil_div(T, 1024), B), dim3(256), 0, st, (int)T,
+                                   out, (long long)ostride, io->sel_n_out));
+        *sel = nullptr;
+        *cnt = nullptr;
+        *stride = 0;
+        return WL_OK;
+    }
     if (io->mode == WL_MODE_OWNER) {
         float* index = io->index_out ? io->index_out : w.index;
         const int64_t istride = io->index_out ? io->index_stride : T;
