@@ -270,7 +270,8 @@ def phase_breakdown(torch, L, step, device, names, reps=20):
         t = buf[:n].cpu().numpy().astype(np.float64)
         rows.append(np.diff(t) * 1e-3)
     d = np.median(np.array(rows[2:]), axis=0)
-    names = names if len(names) == len(d) else [f"phase{i}" for i in range(len(d))]
+    if len(names) != len(d):  # e.g. an owner layer with index_topk >= T: no indexer or top-k phases
+        names = names[-len(d):] if len(d) <= len(names) else [f"phase{i}" for i in range(len(d))]
     return {k: round(float(v), 2) for k, v in zip(names, d)}
 
 
