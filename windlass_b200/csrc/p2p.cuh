@@ -87,15 +87,13 @@ __global__ void __launch_bounds__(256) p2p_put_kernel(P2PArgs a, int type, const
     pdl_trigger();
     const uint32_t epoch = *reinterpret_cast<volatile unsigned*>(a.ctr + type) + 1u;
     const long long off = dst_off + (long long)a.rank * slot_bytes + ((epoch & 1u) ? 0 : parity_bytes);
-    // (destination, word pair) flattened destination-major: a warp's 32 stores
-    // go to one rank, consecutive; the threads of a CTA cover all ranks at once
     const long long n2 = n32 / 2, stride = (long long)gridDim.x * blockDim.x;
-    for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < n2 * a.nranks; t += stride) {
-        const int q = (int)(t / n2);
-        const long long i = t - (long long)q * n2;
-        const int pr = (a.rank + q) % a.nranks;  // ranks start on different destinations
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n2; i += stride) {
         const uint2 v = reinterpret_cast<const uint2*>(src)[i];
-        ll_store2(reinterpret_cast<uint64_t*>(a.region[pr] + off) + 2 * i, v.x, v.y, epoch);
+        for (int q = 0; q < a.nranks; ++q) {
+            const int pr = (a.rank + q) % a.nranks;  // ranks start on different destinations
+            ll_store2(reinterpret_cast<uint64_t*>(a.region[pr] + off) + 2 * i, v.x, v.y, epoch);
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) {

@@ -897,7 +897,7 @@ int launch_put(const wl_comm* c, int type, const void* src, size_t bytes, long l
                long long parity_bytes, cudaStream_t st) {
     if (bytes % 8) return WL_ERR_ARG;
     const long long n32 = (long long)(bytes / 4);
-    int grid = (int)ceil_div(n32 / 2 * c->nranks, 256);
+    int grid = (int)ceil_div(n32 / 2, 256 * 2);
     grid = grid < 1 ? 1 : (grid > sm_count() ? sm_count() : grid);
     WL_CUDA_TRY(launch_pdl(wl::p2p_put_kernel, dim3(grid), dim3(256), 0, st, p2p_args(c), type,
                            static_cast<const uint32_t*>(src), n32, dst_off, slot_bytes, parity_bytes));
