@@ -141,4 +141,60 @@ __global__ void __launch_bounds__(32) lse_merge_kernel(MergeParams p) {
         p.lse[(long long)r * p.lse_out_row_stride + h] = (W > 0.f) ? M + logf(W) : -INFINITY;
 }
 
+// The same merge for parts in plain memory with four warps per (row, head,
+// 128 columns): warp w loads and weighs parts w, w + 4, ... (at most 8, all in
+// flight at once), then warp 0 adds the four partial sums in warp order. A
+// row's partials cost one round of load latency on four times the threads.
+constexpr int MG_WARPS = 4;
+__global__ void __launch_bounds__(32 * MG_WARPS) lse_merge4_kernel(MergeParams p) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float4 part[MG_WARPS - 1][32];
+    const int h = blockIdx.x, q = blockIdx.y, r = blockIdx.z, lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+    const int c = q * 128 + lane * 4;
+    float ls = -INFINITY;
+    if (lane < p.n_parts) ls = p.lse_part[(long long)r * p.lse_row_stride + h + (long long)lane * p.lse_part_stride];
+    float M = ls;
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float wl = (M == -INFINITY || ls == -INFINITY) ? 0.f : exp2f((ls - M) * 1.4426950408889634f);
+    float W = wl;
+    for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+    const long long oi = (long long)r * p.row_stride + (long long)h * p.dv + c;
+    constexpr int G = 32 / MG_WARPS;
+    float4 v[G];
+    float wv[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+        const int s = wi + MG_WARPS * j;
+        wv[j] = __shfl_sync(0xffffffffu, wl, s) * inv;
+        if (s >= p.n_parts) wv[j] = 0.f;
+        v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (wv[j] != 0.f) v[j] = *reinterpret_cast<const float4*>(p.o_part + oi + (long long)s * p.part_stride);
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+        acc.x = fmaf(wv[j], v[j].x, acc.x);
+        acc.y = fmaf(wv[j], v[j].y, acc.y);
+        acc.z = fmaf(wv[j], v[j].z, acc.z);
+        acc.w = fmaf(wv[j], v[j].w, acc.w);
+    }
+    if (wi > 0) part[wi - 1][lane] = acc;
+    __syncthreads();
+    if (wi == 0) {
+#pragma unroll
+        for (int w = 0; w < MG_WARPS - 1; ++w) {
+            const float4 o = part[w][lane];
+            acc.x += o.x;
+            acc.y += o.y;
+            acc.z += o.z;
+            acc.w += o.w;
+        }
+        *reinterpret_cast<float4*>(p.ctx + (long long)r * p.ctx_row_stride + (long long)h * p.dv + c) = acc;
+        if (q == 0 && lane == 0 && p.lse)
+            p.lse[(long long)r * p.lse_out_row_stride + h] = (W > 0.f) ? M + logf(W) : -INFINITY;
+    }
+}
+
 }  // namespace wl

@@ -640,7 +640,10 @@ int launch_merge(const float* o_part, const float* lse_part, int32_t n_rows, int
     }
     if (ll)
         WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel<true>, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
-    else
+    else if (n_rows < 4)  // few rows: four warps per CTA hide the partials' load latency
+        WL_CUDA_TRY(launch_pdl(wl::lse_merge4_kernel, dim3(n_heads, dv / 128, n_rows), dim3(32 * wl::MG_WARPS), 0, st,
+                               p));
+    else  // enough CTAs to fill the SMs with one warp each
         WL_CUDA_TRY(launch_pdl(wl::lse_merge_kernel<false>, dim3(n_heads, dv / 128, n_rows), dim3(32), 0, st, p));
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
